@@ -1,0 +1,309 @@
+/*
+ * p3d.h — C ABI of the B200-native (sm_100a) sparse-voxel SLat kernel library
+ * (libp3dcuda.so).
+ *
+ * This is the drop-in boundary for the hot path of Pixal3D.cpp: the
+ * SparseTensor ops of src/sparse.cpp, the sparse transformer block of
+ * src/sparse_transformer.cpp, their use by src/slat_flow.cpp and
+ * src/slat_decoder.cpp, and the Euler/CFG loop of src/flow_sampler.cpp.
+ * Each entry point below names the reference interface it replaces
+ * (path:line inside the Pixal3D.cpp project).  The C++17 host layer
+ * (pixal3d/cpp_b200/host/) implements the reference's own
+ * include/pixal3d/{sparse,sparse_transformer,flow_sampler,slat_flow,
+ * slat_decoder}.h signatures on top of these calls.
+ *
+ * Conventions
+ *  - All tensor arguments are DEVICE pointers on the context's device; the
+ *    caller owns them.  Calls are stream-ordered on the context's stream and
+ *    return a p3d_status (0 = OK).  p3d_last_error() gives the message.
+ *  - coords: int32 [n][4] rows (batch, x, y, z), rows contiguous by batch.
+ *  - feats: row-major [n][channels]; 16-bit operands are raw uint16 bit
+ *    patterns of IEEE bfloat16 or binary16 as the call's dtype argument says.
+ *  - Linear weights [out][in]; conv weights [27][out][in] with
+ *    kernel = kd*9 + kh*3 + kw and offset (kd-1, kh-1, kw-1) on (x, y, z).
+ *  - Neighbour maps: int32 [27][n], missing neighbour = n.
+ *  - Device-side faults that a kernel can detect (hash probe bound,
+ *    duplicate coordinate, bounded-wait timeout) are latched in a per-context
+ *    device flag; p3d_ctx_check() synchronizes and reports it.
+ */
+#ifndef P3D_H
+#define P3D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum p3d_status {
+    P3D_OK = 0,
+    P3D_ERR_INVALID = 1,      /* bad argument: null pointer, shape, alignment */
+    P3D_ERR_CUDA = 2,         /* CUDA runtime error */
+    P3D_ERR_HASH_FULL = 3,    /* coordinate hash probe bound exceeded */
+    P3D_ERR_TIMEOUT = 4,      /* a device-side bounded wait expired */
+    P3D_ERR_UNSUPPORTED = 5,  /* shape outside what the kernels implement */
+    P3D_ERR_NO_DEVICE = 6,    /* no sm_100 device */
+    P3D_ERR_DUPLICATE = 7,    /* duplicate coordinate in a sparse tensor */
+    P3D_ERR_NONFINITE = 8     /* non-finite value found by a validity probe */
+};
+
+/* Element types.  GEMM/conv/attention operands are 16-bit (bf16 or f16, both
+ * on the tensor cores with f32 accumulation); f32 is used for residual
+ * streams, statistics and model outputs. */
+enum p3d_dtype { P3D_F32 = 0, P3D_BF16 = 1, P3D_F16 = 2 };
+
+/* GEMM / conv epilogues (bit flags; at most one activation). */
+enum p3d_epilogue {
+    P3D_EPI_NONE = 0,
+    P3D_EPI_GELU_TANH = 1,   /* out = gelu_tanh(acc + bias) */
+    P3D_EPI_SILU = 2,        /* out = silu(acc + bias) */
+    P3D_EPI_RESIDUAL = 4     /* out(f32) += gate[batch(row)] * (acc + bias) */
+};
+
+typedef struct p3d_ctx p3d_ctx;
+
+/* ---------------------------------------------------------------- context */
+
+/* Create a context on `device` using `stream` (cudaStream_t, may be NULL for
+ * the legacy default stream).  No reference counterpart: replaces the
+ * ggml backend/scheduler plumbing of src/backend.cpp for this path. */
+int p3d_ctx_create(int device, void *stream, p3d_ctx **out);
+int p3d_ctx_destroy(p3d_ctx *ctx);
+int p3d_ctx_set_stream(p3d_ctx *ctx, void *stream);
+void *p3d_ctx_stream(const p3d_ctx *ctx);
+/* Message of the last failed call on this context ("" if none). */
+const char *p3d_last_error(const p3d_ctx *ctx);
+/* Synchronize the stream and report (then clear) the device fault flag. */
+int p3d_ctx_check(p3d_ctx *ctx);
+/* Number of kernels this library launched on ctx since creation. */
+int64_t p3d_ctx_launch_count(const p3d_ctx *ctx);
+int p3d_version(void);
+
+/* ------------------------------------------------------ coordinates/hash */
+
+/* Table slots for n keys (power of two >= 2n).  Keys are uint64, values
+ * int32; the caller allocates both arrays of this length. */
+int64_t p3d_coord_hash_capacity(int64_t n);
+
+/* Insert every row of coords into an open-addressing table (warp-cooperative
+ * linear probing in HBM, bounded probes).  Replaces the
+ * std::unordered_map<Coord,size_t,CoordHash> builds in
+ * src/sparse.cpp:1017-1022 and src/slat_decoder.cpp:630-635.  A duplicate
+ * coordinate latches P3D_ERR_DUPLICATE (SparseTensorF32::valid,
+ * src/sparse.cpp:318-321). */
+int p3d_coord_hash_build(p3d_ctx *ctx, const int32_t *coords, int64_t n, uint64_t *table_keys,
+                         int32_t *table_vals, int64_t capacity);
+
+/* 27-offset gather map [27][n], sentinel n.  Replaces
+ * build_neighbor_gather_map / build_reference_neighbor_gather_map
+ * (src/slat_decoder.cpp:609-714); bit-exact with the reference. */
+int p3d_neighbor_map27(p3d_ctx *ctx, const int32_t *coords, int64_t n, const uint64_t *table_keys,
+                       const int32_t *table_vals, int64_t capacity, int32_t *nbr_out);
+
+/* Bytes of scratch p3d_neighbor_map27_ws needs for n points. */
+size_t p3d_neighbor_map27_workspace(int64_t n);
+/* Hash build + neighbour map in one call, using caller scratch `ws` of
+ * p3d_neighbor_map27_workspace(n) bytes (256-byte aligned). */
+int p3d_neighbor_map27_ws(p3d_ctx *ctx, const int32_t *coords, int64_t n, void *ws, size_t ws_bytes,
+                          int32_t *nbr_out);
+
+/* Downsample topology (sparse_downsample_mean, src/sparse.cpp:536-602):
+ * parents = coords / factor (per batch), output rows sorted
+ * lexicographically by (b,x,y,z) like the reference.  Uses a dense
+ * occupancy grid of batch*ceil(sx/f)*ceil(sy/f)*ceil(sz/f) int32 cells in
+ * `grid` (caller scratch).  Writes out_coords [m][4], parent[n] (output row
+ * of each input row), child[m][f^3] (input row of each child octant or -1,
+ * octant = (x%f)*f*f + (y%f)*f + z%f) and *out_m (device int64).  `grid` holds
+ * p3d_downsample_grid_ints(...) int32.
+ * out_coords/child must hold n rows (m <= n). */
+int p3d_downsample_topology(p3d_ctx *ctx, const int32_t *coords, int64_t n, int batch, int sx, int sy,
+                            int sz, int factor, int32_t *grid, int32_t *out_coords, int32_t *parent,
+                            int32_t *child, int64_t *out_m);
+/* int32 cells of `grid` scratch p3d_downsample_topology needs. */
+int64_t p3d_downsample_grid_ints(int batch, int sx, int sy, int sz, int factor);
+/* Mean of children features (f32 or bf16 in, same dtype out), summed in
+ * octant order == the reference's input-row order for sorted input. */
+int p3d_downsample_mean(p3d_ctx *ctx, const void *x, int64_t m, int channels, int factor,
+                        const int32_t *child, int dtype, void *out);
+/* Nearest 2x upsample (no reference; benchmark config 2): out[i] = x[parent[i]]. */
+int p3d_upsample_nearest(p3d_ctx *ctx, const void *x, int64_t n, int channels, const int32_t *parent,
+                         int dtype, void *out);
+
+/* Channel-to-spatial topology (sparse_channel_to_spatial,
+ * src/sparse.cpp:604-702): child c of parent p is kept when mask is NULL or
+ * mask[p*f^3 + c] > 0; output rows in parent order then child order.
+ * Writes out_coords (n*f^3 rows max), src_row/src_child per output row and
+ * *out_m (device int64).  scratch: n+1 int64. */
+int p3d_c2s_topology(p3d_ctx *ctx, const int32_t *coords, int64_t n, int factor, const float *mask,
+                     int64_t *scratch, int32_t *out_coords, int32_t *src_row, int8_t *src_child,
+                     int64_t *out_m);
+/* Feature half of channel-to-spatial: out[j] = x[src_row[j], src_child[j]*cout : +cout],
+ * optionally repeating each channel `repeat` times (repeat_channels,
+ * src/slat_decoder.cpp:80-109). */
+int p3d_c2s_gather(p3d_ctx *ctx, const void *x, int64_t in_channels, const int32_t *src_row,
+                   const int8_t *src_child, int64_t m, int cout, int repeat, int dtype, void *out);
+
+/* ------------------------------------------------------------ contractions */
+
+/* y = epilogue(x W^T + bias) on tcgen05/TMEM tensor cores, TMA-fed, 16-bit
+ * operands (ab_dtype P3D_BF16 or P3D_F16), f32 accumulation.  Replaces
+ * sparse_linear / varlen_linear / row_linear (src/sparse.cpp:337-488,
+ * src/slat_flow.cpp:85-111).
+ * x: [m][ldx] (k used), w: [n][k], bias f32 [n] or NULL.
+ * out: [m][ldo] of out_dtype.  For P3D_EPI_RESIDUAL out must be f32 and is
+ * updated in place: out += g * (acc + bias), g = gate[b*gate_ld + col] with
+ * b the batch of the row from batch_offsets[nbatch+1] (or 1 if gate NULL).
+ * Requires k % 8 == 0, ldx % 8 == 0, 16-byte aligned x/w. */
+int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, const float *bias, int64_t m,
+               int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue,
+               const float *gate, int64_t gate_ld, const int32_t *batch_offsets, int nbatch);
+
+/* Submanifold 3x3x3 sparse conv as one gather-GEMM on tcgen05 tiles:
+ * out[p] = epilogue(bias + sum_k W[k] x[nbr[k][p]]).  Replaces
+ * sparse_submanifold_conv3d (src/sparse.cpp:999-1055) and the ggml
+ * get_rows/mul_mat chain gpu_sparse_conv_node (src/slat_decoder.cpp:855-906).
+ * x [n][cin] (cin % 64 == 0), w [27][cout][cin], both of ab_dtype.
+ * Epilogues as p3d_linear (RESIDUAL adds into f32 out). */
+int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const int32_t *nbr,
+                    const void *w, int ab_dtype, const float *bias, int64_t cout, void *out, int64_t ldo,
+                    int out_dtype, int epilogue, const float *gate, int64_t gate_ld,
+                    const int32_t *batch_offsets, int nbatch);
+
+/* Varlen flash attention, head_dim 64, 16-bit in/out (dtype), f32 softmax/accum.
+ * Sequence s covers q rows [cu_q[s], cu_q[s+1]) and k/v rows
+ * [cu_k[s], cu_k[s+1]).  Replaces sparse_scaled_dot_product_attention
+ * (src/sparse.cpp:704-783), sparse_cross_attention (:785-859) and the
+ * chunked ggml sdpa of src/slat_flow.cpp:947-1001. */
+int p3d_varlen_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k, int64_t ldk,
+                         const void *v, int64_t ldv, void *out, int64_t ldo, const int32_t *cu_q,
+                         const int32_t *cu_k, int nseq, int64_t max_q, int heads, int head_dim,
+                         float scale, int dtype);
+
+/* ------------------------------------------------------ fused elementwise */
+
+/* LayerNorm over channels of f32 rows (two-pass, like sparse_layer_norm,
+ * src/sparse.cpp:490-534), then optional affine (gamma/beta) and optional
+ * AdaLN modulation y*(1+scale[b])+shift[b] with shift = mod[b*mod_ld + c],
+ * scale = mod[b*mod_ld + C + c] (affine_modulate,
+ * src/sparse_transformer.cpp:71-99).  out bf16 or f32. */
+int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, int channels, float eps,
+                           const float *gamma, const float *beta, const float *mod, int64_t mod_ld,
+                           const int32_t *batch_offsets, int nbatch, void *out, int out_dtype);
+
+/* Per-head RMS norm (sparse_multihead_rms_norm, src/sparse.cpp:919-997) and
+ * optional interleaved 3D RoPE (sparse_rotary_position_embedding,
+ * src/sparse.cpp:861-917) in place on 16-bit rows x[n][ld] (heads*head_dim
+ * used).  gamma may be NULL (no norm); coords NULL means no RoPE. */
+int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads, int head_dim,
+                        const float *gamma, const int32_t *coords, float freq_min, float freq_base,
+                        int dtype);
+
+/* out = act(x) elementwise (gelu_tanh_in_place src/sparse_transformer.cpp:123-134;
+ * silu src/slat_decoder.cpp:68-78).  dtype applies to x and out. */
+int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out);
+
+/* GroupNorm over the points of each batch item (no reference; benchmark
+ * config 2 SparseResBlock3d), then optional SiLU; f32 in, bf16 out.
+ * stats: caller scratch of nbatch*groups*2 doubles. */
+int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int channels, int groups, float eps,
+                        const float *gamma, const float *beta, const int32_t *batch_offsets, int nbatch,
+                        int silu, double *stats, void *out, int out_dtype);
+
+/* Euler/CFG update of flow_euler_sample_f32 (src/flow_sampler.cpp:245-343):
+ * pred = g*v_pos + (1-g)*v_neg (or v_pos when v_neg NULL), optional guidance
+ * rescale (src/flow_sampler.cpp:200-241) with per-batch population std,
+ * then x -= (t - t_next) * pred.  x, v_*: f32 [n][c]; stats scratch of
+ * nbatch*4 doubles. */
+int p3d_euler_cfg_step(p3d_ctx *ctx, float *x, const float *v_pos, const float *v_neg, int64_t n,
+                       int channels, const int32_t *batch_offsets, int nbatch, float t, float t_next,
+                       float guidance, float guidance_rescale, float sigma_min, double *stats);
+
+/* Precision conversion between any two p3d_dtype element types. */
+int p3d_convert(p3d_ctx *ctx, const void *x, int x_dtype, int64_t count, void *out, int out_dtype);
+
+/* ------------------------------------------------------- SLat flow model */
+
+/* Hyper-parameters (SLatFlowHParams, include/pixal3d/slat_flow.h:12-37) plus
+ * the benchmark-config extensions with no reference: pe_mode 1 = sinusoidal
+ * absolute 3D PE, io_resblocks > 0 = SparseResBlock3d input/output stages
+ * around a 2x downsample/upsample of the trunk. */
+typedef struct p3d_flow_hparams {
+    int in_channels, out_channels, model_channels, cond_channels;
+    int num_blocks, num_heads, mlp_hidden, proj_in_channels;
+    int proj_mode;     /* image_attn_mode: 0 cross, 1 proj */
+    int qk_rms_norm, qk_rms_norm_cross;
+    int pe_mode;       /* 0 rope, 1 ape */
+    int io_resblocks;  /* 0 = reference model */
+    int groups;        /* GroupNorm groups for io resblocks */
+    int operand_dtype; /* 16-bit GEMM/attention operand type: P3D_F16 or P3D_BF16 */
+    float norm_eps, rope_freq_min, rope_freq_base;
+} p3d_flow_hparams;
+
+/* Per-block weight pointers, f32, DEVICE memory, in
+ * SparseTransformerBlockWeightsF32 order (include/pixal3d/sparse_transformer.h:30-54). */
+typedef struct p3d_block_weights {
+    const float *modulation, *qkv_w, *qkv_b, *q_gamma, *k_gamma, *out_w, *out_b;
+    const float *norm2_w, *norm2_b, *cq_w, *cq_b, *ckv_w, *ckv_b, *cq_gamma, *ck_gamma;
+    const float *co_w, *co_b, *proj_w, *proj_b, *mlp0_w, *mlp0_b, *mlp2_w, *mlp2_b;
+} p3d_block_weights;
+
+/* io resblock weights (no reference): GN1 affine, conv1, GN2 affine, conv2. */
+typedef struct p3d_resblock_weights {
+    const float *gn1_w, *gn1_b, *conv1_w, *conv1_b, *gn2_w, *gn2_b, *conv2_w, *conv2_b;
+} p3d_resblock_weights;
+
+/* Model weights (SLatFlowWeightsF32, include/pixal3d/slat_flow.h:39-51),
+ * f32 DEVICE pointers.  blocks: num_blocks entries; io_in/io_out:
+ * io_resblocks entries each (may be NULL when io_resblocks == 0). */
+typedef struct p3d_flow_weights {
+    const float *input_w, *input_b, *t_w0, *t_b0, *t_w2, *t_b2, *mod_w, *mod_b, *output_w, *output_b;
+    const p3d_block_weights *blocks;
+    const p3d_resblock_weights *io_in, *io_out;
+} p3d_flow_weights;
+
+typedef struct p3d_flow p3d_flow;
+
+/* Upload/convert weights into the device layout (16-bit GEMM operands).
+ * Replaces SLatFlowModel::load's tensor upload (src/slat_flow.cpp:578-663). */
+int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out);
+int p3d_flow_destroy(p3d_flow *flow);
+
+/* Bind a coordinate set (device coords [n][4], batch-contiguous, `batch`
+ * items) and a condition layout (ctx_offsets[batch+1] host array) and size
+ * workspaces.  Builds neighbour maps / downsample maps once. */
+int p3d_flow_prepare(p3d_flow *flow, const int32_t *coords, int64_t n, int batch, int sx, int sy, int sz,
+                     const int64_t *ctx_offsets_host);
+
+/* One forward (slat_flow_forward_f32, src/slat_flow.cpp:161-249):
+ * x f32 [n][in], timesteps f32 [batch] (device), ctx bf16 or f32
+ * [T][cond] (ctx_dtype: P3D_F32, or the model's operand dtype), proj f32
+ * [n][proj_in] or NULL, out f32 [n][out]. */
+int p3d_flow_forward(p3d_flow *flow, const float *x, const float *timesteps, const void *ctx_feats,
+                     int ctx_dtype, const float *proj, float *out);
+
+/* Sampler config (FlowEulerSamplerConfig, include/pixal3d/flow_sampler.h:14-23). */
+typedef struct p3d_sampler_config {
+    int steps;
+    float sigma_min, rescale_t, guidance_strength, guidance_rescale;
+    float guidance_interval_min, guidance_interval_max;
+    int use_graph; /* capture one step as a CUDA graph and replay it */
+} p3d_sampler_config;
+
+/* SLatFlowModel::sample (src/slat_flow.cpp:1401-1447) with flow_euler_sample_f32
+ * (src/flow_sampler.cpp:245-343) entirely on device.  The flow must have been
+ * prepared with batch = 2*images: rows of image i appear as batch 2i
+ * (conditional) and 2i+1 (unconditional, zeros condition), contiguous per
+ * batch item, same coordinates.  ctx layout: conditional tokens of image i
+ * in batch 2i, zeros (or anything; they are cleared) in 2i+1.
+ * x: f32 [n/2 rows: image-major, the conditional copy's rows] in/out. */
+int p3d_flow_sample(p3d_flow *flow, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
+                    const p3d_sampler_config *cfg);
+/* Kernel launches one sampler step issued (forward + update), for reporting. */
+int64_t p3d_flow_launches_per_step(const p3d_flow *flow);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* P3D_H */

@@ -1,0 +1,147 @@
+"""ctypes binding of the C ABI in include/p3d.h (libp3dcuda.so).
+
+The library is the product; there is no fallback.  Importing this module on
+a machine without the built library raises immediately, and every call
+checks its p3d_status and raises P3DError with the library's message.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libp3dcuda.so"
+
+P3D_OK = 0
+P3D_ERR_INVALID = 1
+P3D_ERR_CUDA = 2
+P3D_ERR_HASH_FULL = 3
+P3D_ERR_TIMEOUT = 4
+P3D_ERR_UNSUPPORTED = 5
+P3D_ERR_NO_DEVICE = 6
+P3D_ERR_DUPLICATE = 7
+P3D_ERR_NONFINITE = 8
+
+P3D_F32 = 0
+P3D_BF16 = 1
+P3D_F16 = 2
+
+EPI_NONE = 0
+EPI_GELU_TANH = 1
+EPI_SILU = 2
+EPI_RESIDUAL = 4
+
+
+class P3DError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"p3d status {status}: {message}")
+        self.status = status
+
+
+if not LIB_PATH.exists():
+    raise ImportError(f"{LIB_PATH} is not built; run `python -m pixal3d.cpp_b200.build` (no CPU fallback exists)")
+
+lib = C.CDLL(str(LIB_PATH))
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_int64
+f32 = C.c_float
+sz = C.c_size_t
+
+
+class FlowHParams(C.Structure):
+    """p3d_flow_hparams (include/p3d.h)."""
+    _fields_ = [(n, i32) for n in (
+        "in_channels", "out_channels", "model_channels", "cond_channels", "num_blocks", "num_heads",
+        "mlp_hidden", "proj_in_channels", "proj_mode", "qk_rms_norm", "qk_rms_norm_cross", "pe_mode",
+        "io_resblocks", "groups", "operand_dtype")] + [("norm_eps", f32), ("rope_freq_min", f32),
+                                                        ("rope_freq_base", f32)]
+
+
+BLOCK_WEIGHT_FIELDS = ["modulation", "qkv_w", "qkv_b", "q_gamma", "k_gamma", "out_w", "out_b", "norm2_w", "norm2_b",
+                       "cq_w", "cq_b", "ckv_w", "ckv_b", "cq_gamma", "ck_gamma", "co_w", "co_b", "proj_w", "proj_b",
+                       "mlp0_w", "mlp0_b", "mlp2_w", "mlp2_b"]
+RESBLOCK_WEIGHT_FIELDS = ["gn1_w", "gn1_b", "conv1_w", "conv1_b", "gn2_w", "gn2_b", "conv2_w", "conv2_b"]
+FLOW_TOP_FIELDS = ["input_w", "input_b", "t_w0", "t_b0", "t_w2", "t_b2", "mod_w", "mod_b", "output_w", "output_b"]
+
+
+class BlockWeights(C.Structure):
+    _fields_ = [(n, vp) for n in BLOCK_WEIGHT_FIELDS]
+
+
+class ResBlockWeights(C.Structure):
+    _fields_ = [(n, vp) for n in RESBLOCK_WEIGHT_FIELDS]
+
+
+class FlowWeights(C.Structure):
+    _fields_ = [(n, vp) for n in FLOW_TOP_FIELDS] + [
+        ("blocks", C.POINTER(BlockWeights)), ("io_in", C.POINTER(ResBlockWeights)),
+        ("io_out", C.POINTER(ResBlockWeights))]
+
+
+class SamplerConfig(C.Structure):
+    _fields_ = [("steps", i32), ("sigma_min", f32), ("rescale_t", f32), ("guidance_strength", f32),
+                ("guidance_rescale", f32), ("guidance_interval_min", f32), ("guidance_interval_max", f32),
+                ("use_graph", i32)]
+
+
+def _sig(name, res, *args):
+    fn = getattr(lib, name)
+    fn.restype = res
+    fn.argtypes = list(args)
+    return fn
+
+
+_sig("p3d_version", i32)
+_sig("p3d_ctx_create", i32, i32, vp, C.POINTER(vp))
+_sig("p3d_ctx_destroy", i32, vp)
+_sig("p3d_ctx_set_stream", i32, vp, vp)
+_sig("p3d_ctx_stream", vp, vp)
+_sig("p3d_last_error", C.c_char_p, vp)
+_sig("p3d_ctx_check", i32, vp)
+_sig("p3d_ctx_launch_count", i64, vp)
+_sig("p3d_coord_hash_capacity", i64, i64)
+_sig("p3d_coord_hash_build", i32, vp, vp, i64, vp, vp, i64)
+_sig("p3d_neighbor_map27", i32, vp, vp, i64, vp, vp, i64, vp)
+_sig("p3d_neighbor_map27_workspace", sz, i64)
+_sig("p3d_neighbor_map27_ws", i32, vp, vp, i64, vp, sz, vp)
+_sig("p3d_downsample_grid_ints", i64, i32, i32, i32, i32, i32)
+_sig("p3d_downsample_topology", i32, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp)
+_sig("p3d_downsample_mean", i32, vp, vp, i64, i32, i32, vp, i32, vp)
+_sig("p3d_upsample_nearest", i32, vp, vp, i64, i32, vp, i32, vp)
+_sig("p3d_c2s_topology", i32, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp)
+_sig("p3d_c2s_gather", i32, vp, vp, i64, vp, vp, i64, i32, i32, i32, vp)
+_sig("p3d_linear", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i32, vp, i64, vp, i32)
+_sig("p3d_subm_conv3d", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i32, i32, vp, i64, vp, i32)
+_sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, i64, i32, i32, f32, i32)
+_sig("p3d_layernorm_modulate", i32, vp, vp, i64, i32, f32, vp, vp, vp, i64, vp, i32, vp, i32)
+_sig("p3d_qk_rmsnorm_rope", i32, vp, vp, i64, i64, i32, i32, vp, vp, f32, f32, i32)
+_sig("p3d_activation", i32, vp, vp, i64, i32, i32, vp)
+_sig("p3d_group_norm_silu", i32, vp, vp, i64, i32, i32, f32, vp, vp, vp, i32, i32, vp, vp, i32)
+_sig("p3d_euler_cfg_step", i32, vp, vp, vp, vp, i64, i32, vp, i32, f32, f32, f32, f32, f32, vp)
+_sig("p3d_convert", i32, vp, vp, i32, i64, vp, i32)
+
+OPTIONAL = {}
+
+
+def _optional(name, res, *args):
+    try:
+        OPTIONAL[name] = _sig(name, res, *args)
+    except AttributeError:
+        pass
+
+
+_optional("p3d_flow_create", i32, vp, C.POINTER(FlowHParams), C.POINTER(FlowWeights), C.POINTER(vp))
+_optional("p3d_flow_destroy", i32, vp)
+_optional("p3d_flow_prepare", i32, vp, vp, i64, i32, i32, i32, i32, C.POINTER(i64))
+_optional("p3d_flow_forward", i32, vp, vp, vp, vp, i32, vp, vp)
+_optional("p3d_flow_sample", i32, vp, vp, vp, i32, vp, C.POINTER(SamplerConfig))
+_optional("p3d_flow_last_error", C.c_char_p, vp)
+_optional("p3d_flow_launches_per_step", i64, vp)
+
+
+def exported_symbols() -> list[str]:
+    """Names the header declares; used by the CPU test that checks exports."""
+    import re
+    hdr = (Path(__file__).resolve().parent.parent.parent / "include" / "p3d.h").read_text()
+    return sorted(set(re.findall(r"\b(p3d_[a-z0-9_]+)\s*\(", hdr)))

@@ -1,0 +1,102 @@
+// Context, error reporting and precision conversions.
+#include <cstdio>
+
+#include "p3d_common.cuh"
+
+namespace p3d {
+
+int set_error(p3d_ctx *ctx, int status, const std::string &msg) {
+    if (ctx) ctx->error = msg;
+    return status;
+}
+
+int check_launch(p3d_ctx *ctx, const char *what) {
+    ++ctx->launches;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return P3D_OK;
+}
+
+namespace {
+
+template <typename TI, typename TO>
+__global__ void convert_kernel(const TI *__restrict__ x, int64_t n, TO *__restrict__ y) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = from_f32<TO>(to_f32(x[i]));
+}
+
+}  // namespace
+}  // namespace p3d
+
+using namespace p3d;
+
+extern "C" int p3d_version(void) { return 1; }
+
+extern "C" int p3d_ctx_create(int device, void *stream, p3d_ctx **out) {
+    if (!out) return P3D_ERR_INVALID;
+    *out = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= device || device < 0) return P3D_ERR_NO_DEVICE;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return P3D_ERR_NO_DEVICE;
+    if (prop.major != 10) return P3D_ERR_NO_DEVICE;  // built for sm_100a only
+    if (cudaSetDevice(device) != cudaSuccess) return P3D_ERR_CUDA;
+    p3d_ctx *ctx = new p3d_ctx();
+    ctx->device = device;
+    ctx->stream = static_cast<cudaStream_t>(stream);
+    ctx->num_sms = prop.multiProcessorCount;
+    if (cudaMalloc(&ctx->fault, sizeof(int)) != cudaSuccess || cudaMemset(ctx->fault, 0, sizeof(int)) != cudaSuccess) {
+        delete ctx;
+        return P3D_ERR_CUDA;
+    }
+    *out = ctx;
+    return P3D_OK;
+}
+
+extern "C" int p3d_ctx_destroy(p3d_ctx *ctx) {
+    if (!ctx) return P3D_OK;
+    if (ctx->fault) cudaFree(ctx->fault);
+    delete ctx;
+    return P3D_OK;
+}
+
+extern "C" int p3d_ctx_set_stream(p3d_ctx *ctx, void *stream) {
+    if (!ctx) return P3D_ERR_INVALID;
+    ctx->stream = static_cast<cudaStream_t>(stream);
+    return P3D_OK;
+}
+
+extern "C" void *p3d_ctx_stream(const p3d_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
+
+extern "C" const char *p3d_last_error(const p3d_ctx *ctx) { return ctx ? ctx->error.c_str() : "null context"; }
+
+extern "C" int64_t p3d_ctx_launch_count(const p3d_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+extern "C" int p3d_ctx_check(p3d_ctx *ctx) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    int fault = 0;
+    P3D_CUDA(ctx, cudaMemcpy(&fault, ctx->fault, sizeof(int), cudaMemcpyDeviceToHost));
+    if (fault) {
+        P3D_CUDA(ctx, cudaMemset(ctx->fault, 0, sizeof(int)));
+        const char *what = fault == P3D_ERR_TIMEOUT     ? "device wait timed out"
+                           : fault == P3D_ERR_HASH_FULL ? "coordinate hash table full"
+                           : fault == P3D_ERR_DUPLICATE ? "sparse coordinates contain a duplicate point"
+                           : fault == P3D_ERR_NONFINITE ? "non-finite value"
+                                                        : "device fault";
+        return set_error(ctx, fault, what);
+    }
+    return P3D_OK;
+}
+
+extern "C" int p3d_convert(p3d_ctx *ctx, const void *x, int x_dtype, int64_t count, void *out, int out_dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out, "p3d_convert: null pointer");
+    P3D_REQUIRE(ctx, x_dtype >= P3D_F32 && x_dtype <= P3D_F16 && out_dtype >= P3D_F32 && out_dtype <= P3D_F16,
+                "p3d_convert: bad dtype");
+    if (count == 0) return P3D_OK;
+    const unsigned grid = static_cast<unsigned>(ceil_div(count, 256));
+    P3D_DISPATCH(x_dtype, TI, P3D_DISPATCH(out_dtype, TO, convert_kernel<TI, TO><<<grid, 256, 0, ctx->stream>>>(
+                                                              static_cast<const TI *>(x), count, static_cast<TO *>(out))));
+    return check_launch(ctx, "convert");
+}

@@ -1,0 +1,360 @@
+// Fused, vectorised elementwise / normalisation kernels of the SLat block:
+// LayerNorm (+affine) (+AdaLN modulate), per-head RMS norm + 3D RoPE,
+// activations, GroupNorm (+SiLU), and the Euler/CFG flow update.
+// All are HBM-bound: one read and one write of each row, f32 math.
+#include "p3d_common.cuh"
+
+namespace p3d {
+namespace {
+
+unsigned blocks_for(int64_t n, int per_block) { return static_cast<unsigned>(ceil_div(n, per_block)); }
+
+template <typename T>
+__device__ __forceinline__ void store_val(T *p, float v) {
+    *p = from_f32<T>(v);
+}
+
+// ------------------------------------------------------------- LayerNorm
+// One warp per row.  Two-pass statistics like sparse_layer_norm
+// (src/sparse.cpp:514-531): mean, then mean of squared deviations.
+template <typename TO, bool VEC>
+__global__ void layernorm_mod_kernel(const float *__restrict__ x, int64_t n, int C, float eps,
+                                     const float *__restrict__ gamma, const float *__restrict__ beta,
+                                     const float *__restrict__ mod, int64_t mod_ld,
+                                     const int32_t *__restrict__ offsets, int nbatch, TO *__restrict__ out) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float *xr = x + row * C;
+    float s = 0.0f;
+    if (VEC) {
+        for (int c = lane * 4; c < C; c += 128) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+            s += (v.x + v.y) + (v.z + v.w);
+        }
+    } else {
+        for (int c = lane; c < C; c += 32) s += xr[c];
+    }
+    const float mean = warp_sum(s) / static_cast<float>(C);
+    float ss = 0.0f;
+    if (VEC) {
+        for (int c = lane * 4; c < C; c += 128) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+            const float a = v.x - mean, b = v.y - mean, cc = v.z - mean, d = v.w - mean;
+            ss += (a * a + b * b) + (cc * cc + d * d);
+        }
+    } else {
+        for (int c = lane; c < C; c += 32) {
+            const float d = xr[c] - mean;
+            ss += d * d;
+        }
+    }
+    const float var = warp_sum(ss) / static_cast<float>(C);
+    const float inv = 1.0f / sqrtf(var + eps);
+    const float *shift = nullptr, *scale = nullptr;
+    if (mod) {
+        const int b = batch_of_row(offsets, nbatch, row);
+        shift = mod + static_cast<int64_t>(b) * mod_ld;
+        scale = shift + C;
+    }
+    TO *o = out + row * C;
+    for (int c = lane; c < C; c += 32) {
+        float v = (xr[c] - mean) * inv;
+        if (gamma) v = v * gamma[c] + beta[c];
+        if (mod) v = v * (1.0f + scale[c]) + shift[c];
+        store_val(o + c, v);
+    }
+}
+
+// ------------------------------------------------ per-head RMS + 3D RoPE
+// One warp per row; lane p owns rotation pair p (elements 2p, 2p+1) of
+// every head.  head_dim <= 64.
+template <typename T>
+__global__ void qk_rms_rope_kernel(T *__restrict__ x, int64_t n, int64_t ld, int heads, int hd,
+                                   const float *__restrict__ gamma, const int4 *__restrict__ coords, float fmin,
+                                   float fbase) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const int pairs = hd / 2;
+    const bool active = lane < pairs;
+    float cs = 1.0f, sn = 0.0f;
+    if (coords && active) {
+        const int fd = pairs / 3;
+        if (lane < 3 * fd) {
+            const int4 c = coords[row];
+            const int axis = lane / fd;
+            const int coord = axis == 0 ? c.y : (axis == 1 ? c.z : c.w);
+            const float freq = fmin / powf(fbase, static_cast<float>(lane % fd) / static_cast<float>(fd));
+            const float phase = static_cast<float>(coord) * freq;
+            sincosf(phase, &sn, &cs);
+        }
+    }
+    const float mult = sqrtf(static_cast<float>(hd));
+    T *xr = x + row * ld;
+    for (int h = 0; h < heads; ++h) {
+        float e = 0.0f, o = 0.0f;
+        uint32_t *pp = reinterpret_cast<uint32_t *>(xr + h * hd + 2 * lane);
+        if (active) {
+            const float2 v = unpack2<T>(*pp);
+            e = v.x;
+            o = v.y;
+        }
+        if (gamma) {
+            const float sq = warp_sum(e * e + o * o);
+            const float inv = 1.0f / fmaxf(sqrtf(sq), 1e-12f);
+            if (active) {
+                e = e * inv * mult * gamma[h * hd + 2 * lane];
+                o = o * inv * mult * gamma[h * hd + 2 * lane + 1];
+            }
+        }
+        if (active) {
+            const float re = e * cs - o * sn;
+            const float ro = e * sn + o * cs;
+            *pp = pack2<T>(re, ro);
+        }
+    }
+}
+
+// ------------------------------------------------------------ activations
+template <typename T>
+__global__ void activation_kernel(const T *__restrict__ x, int64_t n, int act, T *__restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = to_f32(x[i]);
+    store_val(out + i, act == P3D_EPI_GELU_TANH ? gelu_tanh_f(v) : silu_f(v));
+}
+
+// ------------------------------------------------------------- GroupNorm
+// Stats: block (b, g, slice) accumulates sum / sum of squares of its rows
+// of batch b over the channels of group g, in double, then one atomicAdd.
+__global__ void groupnorm_stats_kernel(const float *__restrict__ x, int C, int groups, const int32_t *__restrict__ offsets,
+                                       int slices, double *__restrict__ stats) {
+    const int bg = blockIdx.x;
+    const int b = bg / groups, g = bg % groups;
+    const int gs = C / groups;
+    const int64_t r0 = offsets[b], r1 = offsets[b + 1];
+    const int64_t rows = r1 - r0;
+    const int64_t per = (rows + slices - 1) / slices;
+    const int64_t s0 = r0 + per * blockIdx.y;
+    const int64_t s1 = min(r1, s0 + per);
+    double sum = 0.0, sq = 0.0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int64_t r = s0 + warp; r < s1; r += nw) {
+        const float *xr = x + r * C + g * gs;
+        for (int c = lane; c < gs; c += 32) {
+            const double v = xr[c];
+            sum += v;
+            sq += v * v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    __shared__ double red[2][32];
+    if (lane == 0) {
+        red[0][warp] = sum;
+        red[1][warp] = sq;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = 0.0, q = 0.0;
+        for (int w = 0; w < nw; ++w) {
+            a += red[0][w];
+            q += red[1][w];
+        }
+        atomicAdd(stats + 2 * bg, a);
+        atomicAdd(stats + 2 * bg + 1, q);
+    }
+}
+
+template <typename TO>
+__global__ void groupnorm_apply_kernel(const float *__restrict__ x, int64_t n, int C, int groups, float eps,
+                                       const float *__restrict__ gamma, const float *__restrict__ beta,
+                                       const int32_t *__restrict__ offsets, int nbatch, const double *__restrict__ stats,
+                                       int silu, TO *__restrict__ out) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const int b = batch_of_row(offsets, nbatch, row);
+    const double cnt = static_cast<double>(offsets[b + 1] - offsets[b]) * (C / groups);
+    const int gs = C / groups;
+    for (int c = lane; c < C; c += 32) {
+        const int g = c / gs;
+        const double mean = stats[2 * (b * groups + g)] / cnt;
+        const double var = fmax(stats[2 * (b * groups + g) + 1] / cnt - mean * mean, 0.0);
+        const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+        float v = (x[row * C + c] - static_cast<float>(mean)) * rstd;
+        if (gamma) v = v * gamma[c] + beta[c];
+        if (silu) v = silu_f(v);
+        store_val(out + row * C + c, v);
+    }
+}
+
+// ------------------------------------------------------------ Euler / CFG
+// x0 = a*x - b*v with a = 1 - sigma_min, b = sigma_min + a*t (pred_to_xstart,
+// src/flow_sampler.cpp:139-147).  Stats per batch: sum/sumsq of x0(pos) and
+// x0(cfg) for the guidance-rescale std (sparse_batch_std, :164-198).
+__global__ void cfg_rescale_stats_kernel(const float *__restrict__ x, const float *__restrict__ vp,
+                                         const float *__restrict__ vn, int64_t n, int C,
+                                         const int32_t *__restrict__ offsets, int nbatch, float t, float g,
+                                         float sigma_min, double *__restrict__ stats) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+    double s0 = 0, q0 = 0, s1 = 0, q1 = 0;
+    for (int c = lane; c < C; c += 32) {
+        const int64_t i = row * C + c;
+        const float p = vp[i];
+        const float pred = vn ? g * p + (1.0f - g) * vn[i] : p;
+        const float xp = a * x[i] - bb * p;
+        const float xc = a * x[i] - bb * pred;
+        s0 += xp;
+        q0 += static_cast<double>(xp) * xp;
+        s1 += xc;
+        q1 += static_cast<double>(xc) * xc;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+    }
+    if (lane == 0) {
+        const int b = batch_of_row(offsets, nbatch, row);
+        atomicAdd(stats + 4 * b + 0, s0);
+        atomicAdd(stats + 4 * b + 1, q0);
+        atomicAdd(stats + 4 * b + 2, s1);
+        atomicAdd(stats + 4 * b + 3, q1);
+    }
+}
+
+__global__ void euler_cfg_kernel(float *__restrict__ x, const float *__restrict__ vp, const float *__restrict__ vn,
+                                 int64_t n, int C, const int32_t *__restrict__ offsets, int nbatch, float t, float dt,
+                                 float g, float gr, float sigma_min, const double *__restrict__ stats) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * C) return;
+    const float p = vp[i];
+    float pred = vn ? g * p + (1.0f - g) * vn[i] : p;
+    if (stats) {
+        // apply_guidance_rescale (src/flow_sampler.cpp:210-241)
+        const int64_t row = i / C;
+        const int b = batch_of_row(offsets, nbatch, row);
+        const double cnt = static_cast<double>(offsets[b + 1] - offsets[b]) * C;
+        const double m0 = stats[4 * b] / cnt, m1 = stats[4 * b + 2] / cnt;
+        const float sp = static_cast<float>(sqrt(fmax(stats[4 * b + 1] / cnt - m0 * m0, 0.0)));
+        const float sc = static_cast<float>(sqrt(fmax(stats[4 * b + 3] / cnt - m1 * m1, 0.0)));
+        const float ratio = sc != 0.0f ? sp / sc : 1.0f;
+        const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+        float x0 = a * x[i] - bb * pred;
+        x0 = gr * (x0 * ratio) + (1.0f - gr) * x0;
+        pred = (a * x[i] - x0) / bb;
+    }
+    x[i] -= dt * pred;
+}
+
+}  // namespace
+}  // namespace p3d
+
+using namespace p3d;
+
+extern "C" int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, int channels, float eps,
+                                      const float *gamma, const float *beta, const float *mod, int64_t mod_ld,
+                                      const int32_t *batch_offsets, int nbatch, void *out, int out_dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && channels > 0, "p3d_layernorm_modulate: bad argument");
+    P3D_REQUIRE(ctx, (gamma == nullptr) == (beta == nullptr),
+                "sparse layer norm affine parameters must be both null or non-null");
+    P3D_REQUIRE(ctx, eps > 0.0f, "sparse layer norm epsilon must be finite and positive");
+    P3D_REQUIRE(ctx, !mod || (batch_offsets && nbatch > 0), "p3d_layernorm_modulate: modulation needs batch offsets");
+    if (n == 0) return P3D_OK;
+    const bool vec = channels % 128 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const unsigned grid = blocks_for(n, 8);
+    P3D_DISPATCH(out_dtype, TO, {
+        if (vec)
+            layernorm_mod_kernel<TO, true><<<grid, 256, 0, ctx->stream>>>(
+                x, n, channels, eps, gamma, beta, mod, mod_ld, batch_offsets, nbatch, static_cast<TO *>(out));
+        else
+            layernorm_mod_kernel<TO, false><<<grid, 256, 0, ctx->stream>>>(
+                x, n, channels, eps, gamma, beta, mod, mod_ld, batch_offsets, nbatch, static_cast<TO *>(out));
+    });
+    return check_launch(ctx, "layernorm_mod");
+}
+
+extern "C" int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads, int head_dim,
+                                   const float *gamma, const int32_t *coords, float freq_min, float freq_base,
+                                   int dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && heads > 0 && head_dim > 0 && head_dim % 2 == 0 && head_dim <= 64,
+                "sparse RoPE head dimensions are invalid");
+    P3D_REQUIRE(ctx, ld >= static_cast<int64_t>(heads) * head_dim, "p3d_qk_rmsnorm_rope: ld too small");
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(x) & 3) == 0 && ld % 2 == 0, "p3d_qk_rmsnorm_rope: misaligned");
+    P3D_REQUIRE(ctx, freq_min > 0.0f && freq_base > 0.0f, "sparse RoPE frequencies must be finite and positive");
+    P3D_REQUIRE(ctx, is_16bit(dtype), "p3d_qk_rmsnorm_rope: dtype must be bf16 or f16");
+    if (n == 0) return P3D_OK;
+    if (dtype == P3D_BF16)
+        qk_rms_rope_kernel<__nv_bfloat16><<<blocks_for(n, 8), 256, 0, ctx->stream>>>(
+            static_cast<__nv_bfloat16 *>(x), n, ld, heads, head_dim, gamma, reinterpret_cast<const int4 *>(coords),
+            freq_min, freq_base);
+    else
+        qk_rms_rope_kernel<__half><<<blocks_for(n, 8), 256, 0, ctx->stream>>>(
+            static_cast<__half *>(x), n, ld, heads, head_dim, gamma, reinterpret_cast<const int4 *>(coords), freq_min,
+            freq_base);
+    return check_launch(ctx, "qk_rms_rope");
+}
+
+extern "C" int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && (act == P3D_EPI_GELU_TANH || act == P3D_EPI_SILU), "p3d_activation: bad argument");
+    if (count == 0) return P3D_OK;
+    P3D_DISPATCH(dtype, T,
+                 activation_kernel<T><<<blocks_for(count, 256), 256, 0, ctx->stream>>>(
+                     static_cast<const T *>(x), count, act, static_cast<T *>(out)));
+    return check_launch(ctx, "activation");
+}
+
+extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int channels, int groups, float eps,
+                                   const float *gamma, const float *beta, const int32_t *batch_offsets, int nbatch,
+                                   int silu, double *stats, void *out, int out_dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && stats && batch_offsets && nbatch > 0, "p3d_group_norm_silu: null pointer");
+    P3D_REQUIRE(ctx, groups > 0 && channels % groups == 0, "p3d_group_norm_silu: channels % groups != 0");
+    P3D_CUDA(ctx, cudaMemsetAsync(stats, 0, sizeof(double) * 2 * nbatch * groups, ctx->stream));
+    if (n == 0) return P3D_OK;
+    dim3 sgrid(nbatch * groups, 16);
+    groupnorm_stats_kernel<<<sgrid, 256, 0, ctx->stream>>>(x, channels, groups, batch_offsets, 16, stats);
+    int rc = check_launch(ctx, "groupnorm_stats");
+    if (rc) return rc;
+    P3D_DISPATCH(out_dtype, TO,
+                 groupnorm_apply_kernel<TO><<<blocks_for(n, 8), 256, 0, ctx->stream>>>(
+                     x, n, channels, groups, eps, gamma, beta, batch_offsets, nbatch, stats, silu,
+                     static_cast<TO *>(out)));
+    return check_launch(ctx, "groupnorm_apply");
+}
+
+extern "C" int p3d_euler_cfg_step(p3d_ctx *ctx, float *x, const float *v_pos, const float *v_neg, int64_t n,
+                                  int channels, const int32_t *batch_offsets, int nbatch, float t, float t_next,
+                                  float guidance, float guidance_rescale, float sigma_min, double *stats) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && v_pos && channels > 0, "p3d_euler_cfg_step: bad argument");
+    const bool rescale = v_neg && guidance_rescale > 0.0f;
+    P3D_REQUIRE(ctx, !rescale || (stats && batch_offsets && nbatch > 0),
+                "p3d_euler_cfg_step: guidance rescale needs stats scratch and batch offsets");
+    if (n == 0) return P3D_OK;
+    if (rescale) {
+        P3D_CUDA(ctx, cudaMemsetAsync(stats, 0, sizeof(double) * 4 * nbatch, ctx->stream));
+        cfg_rescale_stats_kernel<<<blocks_for(n, 8), 256, 0, ctx->stream>>>(x, v_pos, v_neg, n, channels,
+                                                                          batch_offsets, nbatch, t, guidance,
+                                                                          sigma_min, stats);
+        int rc = check_launch(ctx, "cfg_rescale_stats");
+        if (rc) return rc;
+    }
+    euler_cfg_kernel<<<blocks_for(n * channels, 256), 256, 0, ctx->stream>>>(
+        x, v_pos, v_neg, n, channels, batch_offsets, nbatch, t, t - t_next, guidance, guidance_rescale, sigma_min,
+        rescale ? stats : nullptr);
+    return check_launch(ctx, "euler_cfg");
+}

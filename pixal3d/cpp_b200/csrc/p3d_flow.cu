@@ -1,0 +1,804 @@
+// Device-resident SLat flow model and flow-Euler/CFG sampler.
+//
+// Mirrors slat_flow_forward_f32 (src/slat_flow.cpp:161-249) and
+// SLatFlowModel::sample (src/slat_flow.cpp:1401-1447) with
+// flow_euler_sample_f32 (src/flow_sampler.cpp:245-343), but keeps every
+// tensor in HBM for the whole sampling run:
+//   - weights are converted once to bf16 GEMM operands (biases, norms and
+//     the modulation MLP stay f32);
+//   - the coordinate topology (batch offsets, neighbour maps, downsample
+//     maps) is built once per coordinate set in p3d_flow_prepare;
+//   - CFG runs as ONE batched forward: batch items [0, I) are the
+//     conditional images, [I, 2I) the unconditional copies (zeros
+//     condition), so velocity halves are contiguous and the Euler/CFG update
+//     is a single fused kernel;
+//   - the sampler keeps its t schedule and a step counter on the device, so
+//     one step (forward + update) is captured once as a CUDA graph and
+//     replayed for every remaining step.
+// Residual stream h is f32; GEMM inputs bf16; accumulation f32.
+#include <cmath>
+#include <vector>
+
+#include "p3d_common.cuh"
+
+extern "C" int p3d_layernorm_modulate(p3d_ctx *, const float *, int64_t, int, float, const float *, const float *,
+                                      const float *, int64_t, const int32_t *, int, void *, int);
+extern "C" int p3d_qk_rmsnorm_rope(p3d_ctx *, void *, int64_t, int64_t, int, int, const float *, const int32_t *,
+                                   float, float, int);
+extern "C" int p3d_group_norm_silu(p3d_ctx *, const float *, int64_t, int, int, float, const float *, const float *,
+                                   const int32_t *, int, int, double *, void *, int);
+extern "C" int64_t p3d_downsample_grid_ints(int, int, int, int, int);
+
+namespace p3d {
+namespace {
+
+unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>(ceil_div(n, per)); }
+
+// ------------------------------------------------------ small kernels
+
+// Sinusoidal timestep embedding cos||sin, dim 256, period 1e4
+// (timestep_embedding, src/flow.cpp:92-123).  t_b = mult * ts[base + b*stride]
+// where base = 4 * (*counter) when counter is given (sampler schedule).
+__global__ void temb_freq_kernel(const float *ts, int stride, const int *counter, float mult, int batch, int dim,
+                                 float *out) {
+    const int b = blockIdx.x, i = threadIdx.x;
+    const int half = dim / 2;
+    if (i >= half) return;
+    const int base = counter ? 4 * (*counter) : 0;
+    const float t = mult * ts[base + b * stride];
+    const float log_period = 9.210340371976184f;  // (float)log(10000.0)
+    const float frac = static_cast<float>(i) / static_cast<float>(half);
+    const float arg = t * expf(-log_period * frac);
+    out[b * dim + i] = cosf(arg);
+    out[b * dim + half + i] = sinf(arg);
+}
+
+// y[b, n] = act_out(bias[n] + sum_k W[n, k] * act_in(x[b, k])) for B <= 16
+// rows; one warp per output feature.  act: 0 none, 1 silu (x/(1+e^-x)),
+// 2 silu in the sign-split form of src/slat_flow.cpp:79-83.
+__device__ __forceinline__ float act_f(float v, int act) {
+    if (act == 1) return v * (1.0f / (1.0f + expf(-v)));
+    if (act == 2) {
+        if (v >= 0.0f) return v / (1.0f + expf(-v));
+        const float e = expf(v);
+        return v * e / (1.0f + e);
+    }
+    return v;
+}
+
+template <int B>
+__global__ void small_linear_kernel(const float *__restrict__ x, int K, const float *__restrict__ W,
+                                    const float *__restrict__ bias, int N, float *__restrict__ y, int act_in,
+                                    int act_out, int rows) {
+    const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const int lane = threadIdx.x & 31;
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.0f;
+    const float *w = W + static_cast<int64_t>(n) * K;
+    for (int k = lane; k < K; k += 32) {
+        const float wv = w[k];
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (b < rows) acc[b] += wv * act_f(x[b * K + k], act_in);
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        const float s = warp_sum(acc[b]);
+        if (lane == 0 && b < rows) y[b * N + n] = act_f(s + (bias ? bias[n] : 0.0f), act_out);
+    }
+}
+
+int small_linear(p3d_ctx *ctx, const float *x, int rows, int K, const float *W, const float *b, int N, float *y,
+                 int act_in, int act_out) {
+    for (int r0 = 0; r0 < rows; r0 += 16) {
+        const int r = rows - r0 < 16 ? rows - r0 : 16;
+        small_linear_kernel<16><<<blocks_for(N, 8), 256, 0, ctx->stream>>>(x + r0 * K, K, W, b, N, y + r0 * N, act_in,
+                                                                          act_out, r);
+        int rc = check_launch(ctx, "small_linear");
+        if (rc) return rc;
+    }
+    return P3D_OK;
+}
+
+// mods[b, j] = block_mod[j] + tmod[b, j]
+__global__ void add_mod_kernel(const float *bm, const float *tmod, int batch, int six_c, float *mods) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(batch) * six_c) return;
+    mods[i] = bm[i % six_c] + tmod[i];
+}
+
+// f32 [n, in] -> 16-bit [n, in_pad] (zero padded).
+template <typename T>
+__global__ void pad16_kernel(const float *x, int64_t n, int in, int in_pad, T *out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * in_pad) return;
+    const int64_t r = i / in_pad;
+    const int c = static_cast<int>(i - r * in_pad);
+    out[i] = from_f32<T>(c < in ? x[r * in + c] : 0.0f);
+}
+
+int pad16(p3d_ctx *ctx, const float *x, int64_t n, int in, int in_pad, void *out, int dtype) {
+    if (n * in_pad == 0) return P3D_OK;
+    const unsigned grid = blocks_for(n * in_pad, 256);
+    if (dtype == P3D_BF16)
+        pad16_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__nv_bfloat16 *>(out));
+    else
+        pad16_kernel<__half><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__half *>(out));
+    return check_launch(ctx, "pad16");
+}
+
+// Sinusoidal absolute 3D PE added to h (no reference; benchmark config 1/2):
+// per axis a, fd = C/6 frequencies f_i = 10000^(-i/fd): [sin(c_a f_i), cos(c_a f_i)].
+__global__ void ape_add_kernel(float *h, const int4 *coords, int64_t n, int C) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * C) return;
+    const int64_t r = i / C;
+    const int c = static_cast<int>(i - r * C);
+    const int fd = C / 6;
+    if (c >= 6 * fd) return;
+    const int a = c / (2 * fd), j = c % (2 * fd);
+    const int f = j % fd;
+    const int4 cc = coords[r];
+    const int coord = a == 0 ? cc.y : (a == 1 ? cc.z : cc.w);
+    const float freq = 1.0f / powf(10000.0f, static_cast<float>(f) / static_cast<float>(fd));
+    const float arg = static_cast<float>(coord) * freq;
+    h[i] += j < fd ? sinf(arg) : cosf(arg);
+}
+
+// Sampler: schedule rows are {t, t_next, guidance, unused}.
+__global__ void euler_sched_stats_kernel(const float *__restrict__ x, const float *__restrict__ vp,
+                                         const float *__restrict__ vn, int64_t n, int C,
+                                         const int32_t *__restrict__ offsets, int nbatch, const float *sched,
+                                         const int *counter, float sigma_min, double *__restrict__ stats) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float *s = sched + 4 * (*counter);
+    const float t = s[0], g = s[2];
+    const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+    double s0 = 0, q0 = 0, s1 = 0, q1 = 0;
+    for (int c = lane; c < C; c += 32) {
+        const int64_t i = row * C + c;
+        const float p = vp[i];
+        const float pred = g * p + (1.0f - g) * vn[i];
+        const float xp = a * x[i] - bb * p;
+        const float xc = a * x[i] - bb * pred;
+        s0 += xp;
+        q0 += static_cast<double>(xp) * xp;
+        s1 += xc;
+        q1 += static_cast<double>(xc) * xc;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+    }
+    if (lane == 0) {
+        const int b = batch_of_row(offsets, nbatch, row);
+        atomicAdd(stats + 4 * b + 0, s0);
+        atomicAdd(stats + 4 * b + 1, q0);
+        atomicAdd(stats + 4 * b + 2, s1);
+        atomicAdd(stats + 4 * b + 3, q1);
+    }
+}
+
+__global__ void euler_sched_kernel(float *__restrict__ x, const float *__restrict__ vp, const float *__restrict__ vn,
+                                   int64_t n, int C, const int32_t *__restrict__ offsets, int nbatch,
+                                   const float *sched, const int *counter, float gr, float sigma_min,
+                                   const double *__restrict__ stats, float *__restrict__ x_model) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * C) return;
+    const float *s = sched + 4 * (*counter);
+    const float t = s[0], dt = s[0] - s[1], g = s[2];
+    const float p = vp[i];
+    float pred = g * p + (1.0f - g) * vn[i];
+    if (stats) {
+        const int64_t row = i / C;
+        const int b = batch_of_row(offsets, nbatch, row);
+        const double cnt = static_cast<double>(offsets[b + 1] - offsets[b]) * C;
+        const double m0 = stats[4 * b] / cnt, m1 = stats[4 * b + 2] / cnt;
+        const float sp = static_cast<float>(sqrt(fmax(stats[4 * b + 1] / cnt - m0 * m0, 0.0)));
+        const float sc = static_cast<float>(sqrt(fmax(stats[4 * b + 3] / cnt - m1 * m1, 0.0)));
+        const float ratio = sc != 0.0f ? sp / sc : 1.0f;
+        const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+        float x0 = a * x[i] - bb * pred;
+        x0 = gr * (x0 * ratio) + (1.0f - gr) * x0;
+        pred = (a * x[i] - x0) / bb;
+    }
+    const float nx = x[i] - dt * pred;
+    x[i] = nx;
+    // next forward's input: conditional and unconditional copies
+    x_model[i] = nx;
+    x_model[n * C + i] = nx;
+}
+
+__global__ void advance_kernel(int *counter) { *counter += 1; }
+
+__global__ void zero_f32_rows_kernel(float *p, int64_t count) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < count) p[i] = 0.0f;
+}
+
+}  // namespace
+}  // namespace p3d
+
+using namespace p3d;
+
+namespace {
+
+struct DevBlock {
+    float *modulation = nullptr, *qkv_b = nullptr, *q_gamma = nullptr, *k_gamma = nullptr, *out_b = nullptr;
+    float *norm2_w = nullptr, *norm2_b = nullptr, *cq_b = nullptr, *ckv_b = nullptr, *cq_gamma = nullptr;
+    float *ck_gamma = nullptr, *co_b = nullptr, *proj_b = nullptr, *mlp0_b = nullptr, *mlp2_b = nullptr;
+    uint16_t *qkv_w = nullptr, *out_w = nullptr, *cq_w = nullptr, *ckv_w = nullptr, *co_w = nullptr;
+    uint16_t *proj_w = nullptr, *mlp0_w = nullptr, *mlp2_w = nullptr;
+};
+
+struct DevRes {
+    float *gn1_w = nullptr, *gn1_b = nullptr, *conv1_b = nullptr, *gn2_w = nullptr, *gn2_b = nullptr,
+          *conv2_b = nullptr;
+    uint16_t *conv1_w = nullptr, *conv2_w = nullptr;
+};
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+struct p3d_flow {
+    p3d_ctx *ctx = nullptr;
+    p3d_flow_hparams hp{};
+    int C = 0, in_pad = 0, cond_pad = 0, proj_pad = 0;
+    std::vector<void *> allocs;
+    // weights
+    uint16_t *input_w = nullptr, *output_w = nullptr;
+    float *input_b = nullptr, *output_b = nullptr, *t_w0 = nullptr, *t_b0 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr,
+          *mod_w = nullptr, *mod_b = nullptr;
+    std::vector<DevBlock> blocks;
+    std::vector<DevRes> io_in, io_out;
+    // topology
+    bool prepared = false;
+    int batch = 0;
+    int64_t n = 0, nt = 0, T = 0, max_fine = 0, max_trunk = 0, max_ctx = 0;
+    int32_t *coords = nullptr, *trunk_coords = nullptr, *fine_off = nullptr, *trunk_off = nullptr, *ctx_off = nullptr;
+    int32_t *nbr = nullptr, *parent = nullptr, *child = nullptr;
+    // workspaces
+    float *h = nullptr, *hf = nullptr, *ftmp = nullptr, *tfreq = nullptr, *temb = nullptr, *temb2 = nullptr,
+          *tmod = nullptr, *mods = nullptr, *x_model = nullptr, *vel = nullptr, *sched = nullptr, *ts = nullptr;
+    // 16-bit operand buffers (dt = P3D_F16 or P3D_BF16)
+    uint16_t *xn = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr, *kv = nullptr, *cq = nullptr,
+             *ctx_bf = nullptr, *proj_bf = nullptr, *x_in = nullptr, *fbf = nullptr;
+    int dt = P3D_F16;
+    double *stats = nullptr;
+    int *counter = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string error;
+    int64_t launches_per_step = 0;
+
+    template <typename T>
+    int alloc(T **p, int64_t count) {
+        *p = nullptr;
+        if (count <= 0) count = 1;
+        cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * count);
+        if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        allocs.push_back(*p);
+        return P3D_OK;
+    }
+    void free_prepared();
+    ~p3d_flow() {
+        for (void *p : allocs) cudaFree(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+std::vector<void *> *g_prep_allocs = nullptr;
+
+int upload16(p3d_flow *f, const float *src, int64_t rows, int64_t cols, int64_t cols_pad, uint16_t **dst) {
+    if (!src) return set_error(f->ctx, P3D_ERR_INVALID, "missing SLat flow weight");
+    int rc = f->alloc(dst, rows * cols_pad);
+    if (rc) return rc;
+    return pad16(f->ctx, src, rows, static_cast<int>(cols), static_cast<int>(cols_pad), *dst, f->dt);
+}
+
+int copy_f32(p3d_flow *f, const float *src, int64_t count, float **dst, bool required = true) {
+    if (!src) {
+        *dst = nullptr;
+        return required ? set_error(f->ctx, P3D_ERR_INVALID, "missing SLat flow tensor") : P3D_OK;
+    }
+    int rc = f->alloc(dst, count);
+    if (rc) return rc;
+    P3D_CUDA(f->ctx, cudaMemcpyAsync(*dst, src, sizeof(float) * count, cudaMemcpyDeviceToDevice, f->ctx->stream));
+    return P3D_OK;
+}
+
+#define P3D_TRY(expr)          \
+    do {                       \
+        int rc_ = (expr);      \
+        if (rc_) return rc_;   \
+    } while (0)
+
+// ----------------------------------------------------------- the forward
+// Runs on ctx->stream (the flow's stream while sampling).  x: f32 [n, in].
+// ts / ts_stride / counter / mult feed the timestep embedding.
+int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, const int *counter, float mult,
+                 const float *proj, float *out) {
+    p3d_ctx *ctx = f->ctx;
+    const p3d_flow_hparams &hp = f->hp;
+    const int C = f->C, H = hp.num_heads, B = f->batch;
+    const int64_t n = f->n, nt = f->nt;
+    const bool io = hp.io_resblocks > 0;
+    const int dt = f->dt;
+    // timestep MLP -> SiLU -> 6C modulation (src/slat_flow.cpp:208-222)
+    temb_freq_kernel<<<B, 128, 0, ctx->stream>>>(ts, ts_stride, counter, mult, B, 256, f->tfreq);
+    P3D_TRY(check_launch(ctx, "temb_freq"));
+    P3D_TRY(small_linear(ctx, f->tfreq, B, 256, f->t_w0, f->t_b0, C, f->temb, 0, 1));
+    P3D_TRY(small_linear(ctx, f->temb, B, C, f->t_w2, f->t_b2, C, f->temb2, 0, 0));
+    P3D_TRY(small_linear(ctx, f->temb2, B, C, f->mod_w, f->mod_b, 6 * C, f->tmod, 2, 0));
+    // input linear
+    P3D_TRY(pad16(ctx, x, n, hp.in_channels, f->in_pad, f->x_in, dt));
+    float *hin = io ? f->hf : f->h;
+    P3D_TRY(p3d_linear(ctx, f->x_in, f->in_pad, f->input_w, dt, f->input_b, n, C, f->in_pad, hin, C, P3D_F32, P3D_EPI_NONE,
+                       nullptr, 0, nullptr, 0));
+    if (io) {
+        for (const DevRes &r : f->io_in) {
+            P3D_TRY(p3d_group_norm_silu(ctx, f->hf, n, C, hp.groups, 1e-5f, r.gn1_w, r.gn1_b, f->fine_off, B, 1,
+                                        f->stats, f->fbf, dt));
+            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
+                                    P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_group_norm_silu(ctx, f->ftmp, n, C, hp.groups, 1e-5f, r.gn2_w, r.gn2_b, f->fine_off, B, 1,
+                                        f->stats, f->fbf, dt));
+            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
+                                    P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0));
+        }
+        P3D_TRY(p3d_downsample_mean(ctx, f->hf, nt, C, 2, f->child, P3D_F32, f->h));
+    }
+    if (hp.pe_mode == 1) {
+        ape_add_kernel<<<blocks_for(nt * C, 256), 256, 0, ctx->stream>>>(f->h, reinterpret_cast<const int4 *>(f->trunk_coords),
+                                                                        nt, C);
+        P3D_TRY(check_launch(ctx, "ape_add"));
+    }
+    const float attn_scale = 1.0f / sqrtf(static_cast<float>(C / H));
+    const int mlp = hp.mlp_hidden;
+    if (hp.proj_mode && proj) {
+        P3D_TRY(pad16(ctx, proj, nt, hp.proj_in_channels, f->proj_pad, f->proj_bf, dt));
+    }
+    for (const DevBlock &bw : f->blocks) {
+        add_mod_kernel<<<blocks_for(static_cast<int64_t>(B) * 6 * C, 256), 256, 0, ctx->stream>>>(
+            bw.modulation, f->tmod, B, 6 * C, f->mods);
+        P3D_TRY(check_launch(ctx, "add_mod"));
+        // self-attention branch (src/sparse_transformer.cpp:194-235)
+        P3D_TRY(p3d_layernorm_modulate(ctx, f->h, nt, C, hp.norm_eps, nullptr, nullptr, f->mods, 6 * C, f->trunk_off,
+                                       B, f->xn, dt));
+        P3D_TRY(p3d_linear(ctx, f->xn, C, bw.qkv_w, dt, bw.qkv_b, nt, 3 * C, C, f->qkv, 3 * C, dt, P3D_EPI_NONE,
+                           nullptr, 0, nullptr, 0));
+        const int32_t *rope_coords = hp.pe_mode == 0 ? f->trunk_coords : nullptr;
+        if (hp.qk_rms_norm || rope_coords) {
+            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->qkv, nt, 3 * C, H, C / H, hp.qk_rms_norm ? bw.q_gamma : nullptr,
+                                        rope_coords, hp.rope_freq_min, hp.rope_freq_base, dt));
+            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->qkv + C, nt, 3 * C, H, C / H, hp.qk_rms_norm ? bw.k_gamma : nullptr,
+                                        rope_coords, hp.rope_freq_min, hp.rope_freq_base, dt));
+        }
+        P3D_TRY(p3d_varlen_attention(ctx, f->qkv, 3 * C, f->qkv + C, 3 * C, f->qkv + 2 * C, 3 * C, f->attn, C,
+                                     f->trunk_off, f->trunk_off, B, f->max_trunk, H, C / H, attn_scale, dt));
+        P3D_TRY(p3d_linear(ctx, f->attn, C, bw.out_w, dt, bw.out_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL,
+                           f->mods + 2 * C, 6 * C, f->trunk_off, B));
+        // cross-attention branch (:237-275)
+        P3D_TRY(p3d_layernorm_modulate(ctx, f->h, nt, C, hp.norm_eps, bw.norm2_w, bw.norm2_b, nullptr, 0, nullptr, 0,
+                                       f->xn, dt));
+        P3D_TRY(p3d_linear(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, P3D_EPI_NONE, nullptr, 0,
+                           nullptr, 0));
+        if (hp.qk_rms_norm_cross)
+            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->cq, nt, C, H, C / H, bw.cq_gamma, nullptr, 1.0f, 10000.0f, dt));
+        P3D_TRY(p3d_linear(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad, f->kv, 2 * C,
+                           dt, P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+        if (hp.qk_rms_norm_cross)
+            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->kv, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f, dt));
+        P3D_TRY(p3d_varlen_attention(ctx, f->cq, C, f->kv, 2 * C, f->kv + C, 2 * C, f->attn, C, f->trunk_off,
+                                     f->ctx_off, B, f->max_trunk, H, C / H, attn_scale, dt));
+        P3D_TRY(p3d_linear(ctx, f->attn, C, bw.co_w, dt, bw.co_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL, nullptr, 0,
+                           nullptr, 0));
+        if (hp.proj_mode && proj)
+            P3D_TRY(p3d_linear(ctx, f->proj_bf, f->proj_pad, bw.proj_w, dt, bw.proj_b, nt, C, f->proj_pad, f->h, C,
+                               P3D_F32, P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0));
+        // MLP branch (:277-290)
+        P3D_TRY(p3d_layernorm_modulate(ctx, f->h, nt, C, hp.norm_eps, nullptr, nullptr, f->mods + 3 * C, 6 * C,
+                                       f->trunk_off, B, f->xn, dt));
+        P3D_TRY(p3d_linear(ctx, f->xn, C, bw.mlp0_w, dt, bw.mlp0_b, nt, mlp, C, f->mlp, mlp, dt, P3D_EPI_GELU_TANH,
+                           nullptr, 0, nullptr, 0));
+        P3D_TRY(p3d_linear(ctx, f->mlp, mlp, bw.mlp2_w, dt, bw.mlp2_b, nt, C, mlp, f->h, C, P3D_F32, P3D_EPI_RESIDUAL,
+                           f->mods + 5 * C, 6 * C, f->trunk_off, B));
+    }
+    float *hout = f->h;
+    if (io) {
+        P3D_TRY(p3d_upsample_nearest(ctx, f->h, n, C, f->parent, P3D_F32, f->hf));
+        for (const DevRes &r : f->io_out) {
+            P3D_TRY(p3d_group_norm_silu(ctx, f->hf, n, C, hp.groups, 1e-5f, r.gn1_w, r.gn1_b, f->fine_off, B, 1,
+                                        f->stats, f->fbf, dt));
+            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
+                                    P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_group_norm_silu(ctx, f->ftmp, n, C, hp.groups, 1e-5f, r.gn2_w, r.gn2_b, f->fine_off, B, 1,
+                                        f->stats, f->fbf, dt));
+            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
+                                    P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0));
+        }
+        hout = f->hf;
+    }
+    // final LayerNorm (eps 1e-5, src/slat_flow.cpp:244-248) + output linear
+    uint16_t *xfin = io ? f->fbf : f->xn;
+    P3D_TRY(p3d_layernorm_modulate(ctx, hout, n, C, 1e-5f, nullptr, nullptr, nullptr, 0, nullptr, 0, xfin, dt));
+    P3D_TRY(p3d_linear(ctx, xfin, C, f->output_w, dt, f->output_b, n, hp.out_channels, C, out, hp.out_channels, P3D_F32,
+                       P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+    return P3D_OK;
+}
+
+struct StreamSwap {
+    p3d_ctx *ctx;
+    cudaStream_t saved;
+    StreamSwap(p3d_ctx *c, cudaStream_t s) : ctx(c), saved(c->stream) { ctx->stream = s; }
+    ~StreamSwap() { ctx->stream = saved; }
+};
+
+}  // namespace
+
+void p3d_flow::free_prepared() {}
+
+extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out) {
+    if (!ctx || !hp || !w || !out) return P3D_ERR_INVALID;
+    *out = nullptr;
+    const int C = hp->model_channels;
+    P3D_REQUIRE(ctx, C > 0 && hp->num_heads > 0 && C % hp->num_heads == 0 && C / hp->num_heads == 64,
+                "p3d_flow_create: head_dim must be 64");
+    P3D_REQUIRE(ctx, C % 64 == 0, "p3d_flow_create: model_channels must be a multiple of 64");
+    P3D_REQUIRE(ctx, hp->in_channels > 0 && hp->out_channels > 0 && hp->cond_channels > 0 && hp->num_blocks > 0,
+                "invalid SLat flow hyperparameters");
+    P3D_REQUIRE(ctx, hp->mlp_hidden > 0 && hp->mlp_hidden % 8 == 0, "p3d_flow_create: mlp_hidden must be a multiple of 8");
+    P3D_REQUIRE(ctx, !hp->proj_mode || hp->proj_in_channels > 0, "SLat flow projection channels must be positive");
+    P3D_REQUIRE(ctx, !(hp->proj_mode && hp->io_resblocks > 0), "p3d_flow_create: proj mode with io stages is undefined");
+    P3D_REQUIRE(ctx, hp->io_resblocks == 0 || (hp->groups > 0 && C % hp->groups == 0),
+                "p3d_flow_create: groups must divide model_channels");
+    P3D_REQUIRE(ctx, w->blocks, "missing SLat flow block weights");
+    p3d_flow *f = new p3d_flow();
+    f->ctx = ctx;
+    f->hp = *hp;
+    f->C = C;
+    f->in_pad = static_cast<int>(round_up(hp->in_channels, 8));
+    f->cond_pad = static_cast<int>(round_up(hp->cond_channels, 8));
+    f->proj_pad = static_cast<int>(round_up(hp->proj_in_channels > 0 ? hp->proj_in_channels : 8, 8));
+    f->dt = hp->operand_dtype == P3D_BF16 ? P3D_BF16 : P3D_F16;
+    auto fail = [&](int rc) {
+        delete f;
+        return rc;
+    };
+    int rc;
+    if ((rc = upload16(f, w->input_w, C, hp->in_channels, f->in_pad, &f->input_w))) return fail(rc);
+    if ((rc = copy_f32(f, w->input_b, C, &f->input_b))) return fail(rc);
+    if ((rc = copy_f32(f, w->t_w0, static_cast<int64_t>(C) * 256, &f->t_w0))) return fail(rc);
+    if ((rc = copy_f32(f, w->t_b0, C, &f->t_b0))) return fail(rc);
+    if ((rc = copy_f32(f, w->t_w2, static_cast<int64_t>(C) * C, &f->t_w2))) return fail(rc);
+    if ((rc = copy_f32(f, w->t_b2, C, &f->t_b2))) return fail(rc);
+    if ((rc = copy_f32(f, w->mod_w, static_cast<int64_t>(6) * C * C, &f->mod_w))) return fail(rc);
+    if ((rc = copy_f32(f, w->mod_b, 6 * C, &f->mod_b))) return fail(rc);
+    if ((rc = upload16(f, w->output_w, hp->out_channels, C, C, &f->output_w))) return fail(rc);
+    if ((rc = copy_f32(f, w->output_b, hp->out_channels, &f->output_b))) return fail(rc);
+    const int mlp = hp->mlp_hidden;
+    for (int i = 0; i < hp->num_blocks; ++i) {
+        const p3d_block_weights &s = w->blocks[i];
+        DevBlock d;
+        if ((rc = copy_f32(f, s.modulation, 6 * C, &d.modulation))) return fail(rc);
+        if ((rc = upload16(f, s.qkv_w, 3 * C, C, C, &d.qkv_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.qkv_b, 3 * C, &d.qkv_b))) return fail(rc);
+        if ((rc = copy_f32(f, s.q_gamma, C, &d.q_gamma, hp->qk_rms_norm != 0))) return fail(rc);
+        if ((rc = copy_f32(f, s.k_gamma, C, &d.k_gamma, hp->qk_rms_norm != 0))) return fail(rc);
+        if ((rc = upload16(f, s.out_w, C, C, C, &d.out_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.out_b, C, &d.out_b))) return fail(rc);
+        if ((rc = copy_f32(f, s.norm2_w, C, &d.norm2_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.norm2_b, C, &d.norm2_b))) return fail(rc);
+        if ((rc = upload16(f, s.cq_w, C, C, C, &d.cq_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.cq_b, C, &d.cq_b))) return fail(rc);
+        if ((rc = upload16(f, s.ckv_w, 2 * C, hp->cond_channels, f->cond_pad, &d.ckv_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.ckv_b, 2 * C, &d.ckv_b))) return fail(rc);
+        if ((rc = copy_f32(f, s.cq_gamma, C, &d.cq_gamma, hp->qk_rms_norm_cross != 0))) return fail(rc);
+        if ((rc = copy_f32(f, s.ck_gamma, C, &d.ck_gamma, hp->qk_rms_norm_cross != 0))) return fail(rc);
+        if ((rc = upload16(f, s.co_w, C, C, C, &d.co_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.co_b, C, &d.co_b))) return fail(rc);
+        if (hp->proj_mode) {
+            if ((rc = upload16(f, s.proj_w, C, hp->proj_in_channels, f->proj_pad, &d.proj_w))) return fail(rc);
+            if ((rc = copy_f32(f, s.proj_b, C, &d.proj_b))) return fail(rc);
+        }
+        if ((rc = upload16(f, s.mlp0_w, mlp, C, C, &d.mlp0_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.mlp0_b, mlp, &d.mlp0_b))) return fail(rc);
+        if ((rc = upload16(f, s.mlp2_w, C, mlp, mlp, &d.mlp2_w))) return fail(rc);
+        if ((rc = copy_f32(f, s.mlp2_b, C, &d.mlp2_b))) return fail(rc);
+        f->blocks.push_back(d);
+    }
+    for (int side = 0; side < 2; ++side) {
+        const p3d_resblock_weights *src = side == 0 ? w->io_in : w->io_out;
+        std::vector<DevRes> &dst = side == 0 ? f->io_in : f->io_out;
+        for (int i = 0; i < hp->io_resblocks; ++i) {
+            if (!src) return fail(set_error(ctx, P3D_ERR_INVALID, "missing io resblock weights"));
+            const p3d_resblock_weights &s = src[i];
+            DevRes d;
+            const int64_t cw = static_cast<int64_t>(27) * C;
+            if ((rc = copy_f32(f, s.gn1_w, C, &d.gn1_w))) return fail(rc);
+            if ((rc = copy_f32(f, s.gn1_b, C, &d.gn1_b))) return fail(rc);
+            if ((rc = upload16(f, s.conv1_w, cw, C, C, &d.conv1_w))) return fail(rc);
+            if ((rc = copy_f32(f, s.conv1_b, C, &d.conv1_b))) return fail(rc);
+            if ((rc = copy_f32(f, s.gn2_w, C, &d.gn2_w))) return fail(rc);
+            if ((rc = copy_f32(f, s.gn2_b, C, &d.gn2_b))) return fail(rc);
+            if ((rc = upload16(f, s.conv2_w, cw, C, C, &d.conv2_w))) return fail(rc);
+            if ((rc = copy_f32(f, s.conv2_b, C, &d.conv2_b))) return fail(rc);
+            dst.push_back(d);
+        }
+    }
+    if (cudaStreamCreateWithFlags(&f->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_error(ctx, P3D_ERR_CUDA, "cudaStreamCreate failed"));
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        return fail(set_error(ctx, P3D_ERR_CUDA, "weight upload failed"));
+    *out = f;
+    return P3D_OK;
+}
+
+extern "C" int p3d_flow_destroy(p3d_flow *flow) {
+    if (flow) {
+        cudaStreamSynchronize(flow->stream);
+        delete flow;
+    }
+    return P3D_OK;
+}
+
+extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, int batch, int sx, int sy, int sz,
+                                const int64_t *ctx_offsets_host) {
+    if (!f) return P3D_ERR_INVALID;
+    p3d_ctx *ctx = f->ctx;
+    P3D_REQUIRE(ctx, !f->prepared, "p3d_flow_prepare: already prepared (create a new flow per coordinate set)");
+    P3D_REQUIRE(ctx, coords && ctx_offsets_host && n > 0 && batch > 0, "p3d_flow_prepare: bad argument");
+    const p3d_flow_hparams &hp = f->hp;
+    const int C = f->C;
+    f->batch = batch;
+    f->n = n;
+    // host copies of coords -> batch offsets (rows contiguous by batch)
+    std::vector<int32_t> hc(static_cast<size_t>(n) * 4);
+    P3D_CUDA(ctx, cudaMemcpy(hc.data(), coords, sizeof(int32_t) * hc.size(), cudaMemcpyDeviceToHost));
+    std::vector<int32_t> off(batch + 1, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const int b = hc[i * 4];
+        if (b < 0 || b >= batch || (i > 0 && hc[(i - 1) * 4] > b))
+            return set_error(ctx, P3D_ERR_INVALID, "sparse coordinates must be contiguous by batch");
+        off[b + 1]++;
+    }
+    for (int b = 0; b < batch; ++b) {
+        off[b + 1] += off[b];
+        f->max_fine = std::max<int64_t>(f->max_fine, off[b + 1] - off[b]);
+    }
+    std::vector<int32_t> coff(batch + 1);
+    for (int b = 0; b <= batch; ++b) coff[b] = static_cast<int32_t>(ctx_offsets_host[b]);
+    for (int b = 0; b < batch; ++b) {
+        if (coff[b + 1] <= coff[b]) return set_error(ctx, P3D_ERR_INVALID, "sparse cross-attention has an empty key sequence");
+        f->max_ctx = std::max<int64_t>(f->max_ctx, coff[b + 1] - coff[b]);
+    }
+    f->T = coff[batch];
+    P3D_TRY(f->alloc(&f->coords, n * 4));
+    P3D_CUDA(ctx, cudaMemcpy(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice));
+    P3D_TRY(f->alloc(&f->fine_off, batch + 1));
+    P3D_CUDA(ctx, cudaMemcpy(f->fine_off, off.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+    P3D_TRY(f->alloc(&f->ctx_off, batch + 1));
+    P3D_CUDA(ctx, cudaMemcpy(f->ctx_off, coff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+    const bool io = hp.io_resblocks > 0;
+    if (io) {
+        // fine-level neighbour map and 2x downsample topology
+        P3D_TRY(f->alloc(&f->nbr, 27 * n));
+        size_t wsb = p3d_neighbor_map27_workspace(n);
+        void *ws = nullptr;
+        P3D_CUDA(ctx, cudaMalloc(&ws, wsb));
+        int rc = p3d_neighbor_map27_ws(ctx, f->coords, n, ws, wsb, f->nbr);
+        const int64_t gints = p3d_downsample_grid_ints(batch, sx, sy, sz, 2);
+        int32_t *grid = nullptr;
+        int64_t *dm = nullptr;
+        if (!rc) rc = f->alloc(&f->trunk_coords, n * 4);
+        if (!rc) rc = f->alloc(&f->parent, n);
+        if (!rc) rc = f->alloc(&f->child, n * 8);
+        if (!rc && cudaMalloc(&grid, sizeof(int32_t) * gints) != cudaSuccess) rc = P3D_ERR_CUDA;
+        if (!rc && cudaMalloc(&dm, sizeof(int64_t)) != cudaSuccess) rc = P3D_ERR_CUDA;
+        if (!rc)
+            rc = p3d_downsample_topology(ctx, f->coords, n, batch, sx, sy, sz, 2, grid, f->trunk_coords, f->parent,
+                                         f->child, dm);
+        int64_t m = 0;
+        if (!rc && cudaMemcpy(&m, dm, sizeof(int64_t), cudaMemcpyDeviceToHost) != cudaSuccess) rc = P3D_ERR_CUDA;
+        cudaFree(ws);
+        cudaFree(grid);
+        cudaFree(dm);
+        if (rc) return rc;
+        P3D_TRY(p3d_ctx_check(ctx));
+        f->nt = m;
+        std::vector<int32_t> tc(static_cast<size_t>(m) * 4);
+        P3D_CUDA(ctx, cudaMemcpy(tc.data(), f->trunk_coords, sizeof(int32_t) * tc.size(), cudaMemcpyDeviceToHost));
+        std::vector<int32_t> toff(batch + 1, 0);
+        for (int64_t i = 0; i < m; ++i) toff[tc[i * 4] + 1]++;
+        for (int b = 0; b < batch; ++b) {
+            toff[b + 1] += toff[b];
+            f->max_trunk = std::max<int64_t>(f->max_trunk, toff[b + 1] - toff[b]);
+        }
+        P3D_TRY(f->alloc(&f->trunk_off, batch + 1));
+        P3D_CUDA(ctx, cudaMemcpy(f->trunk_off, toff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+        P3D_TRY(f->alloc(&f->hf, n * C));
+        P3D_TRY(f->alloc(&f->ftmp, n * C));
+        P3D_TRY(f->alloc(&f->fbf, n * C));
+        P3D_TRY(f->alloc(&f->stats, 2 * batch * hp.groups + 4 * batch));
+    } else {
+        f->nt = n;
+        f->trunk_coords = f->coords;
+        f->trunk_off = f->fine_off;
+        f->max_trunk = f->max_fine;
+        P3D_TRY(f->alloc(&f->stats, 4 * batch));
+    }
+    const int64_t nt = f->nt;
+    P3D_TRY(f->alloc(&f->h, nt * C));
+    P3D_TRY(f->alloc(&f->xn, std::max(nt, n) * C));
+    P3D_TRY(f->alloc(&f->qkv, nt * 3 * C));
+    P3D_TRY(f->alloc(&f->attn, nt * C));
+    P3D_TRY(f->alloc(&f->cq, nt * C));
+    P3D_TRY(f->alloc(&f->mlp, nt * hp.mlp_hidden));
+    P3D_TRY(f->alloc(&f->kv, f->T * 2 * C));
+    P3D_TRY(f->alloc(&f->ctx_bf, f->T * f->cond_pad));
+    P3D_TRY(f->alloc(&f->proj_bf, nt * f->proj_pad));
+    P3D_TRY(f->alloc(&f->x_in, n * f->in_pad));
+    P3D_TRY(f->alloc(&f->tfreq, batch * 256));
+    P3D_TRY(f->alloc(&f->temb, batch * C));
+    P3D_TRY(f->alloc(&f->temb2, batch * C));
+    P3D_TRY(f->alloc(&f->tmod, batch * 6 * C));
+    P3D_TRY(f->alloc(&f->mods, batch * 6 * C));
+    P3D_TRY(f->alloc(&f->x_model, n * hp.in_channels));
+    P3D_TRY(f->alloc(&f->vel, n * hp.out_channels));
+    P3D_TRY(f->alloc(&f->ts, batch));
+    P3D_TRY(f->alloc(&f->counter, 1));
+    f->prepared = true;
+    return P3D_OK;
+}
+
+namespace {
+int load_ctx(p3d_flow *f, const void *ctx_feats, int ctx_dtype) {
+    p3d_ctx *ctx = f->ctx;
+    const int cc = f->hp.cond_channels;
+    if (ctx_dtype == P3D_F32) return pad16(ctx, static_cast<const float *>(ctx_feats), f->T, cc, f->cond_pad, f->ctx_bf, f->dt);
+    P3D_REQUIRE(ctx, ctx_dtype == f->dt, "p3d_flow: 16-bit condition must use the model's operand dtype");
+    P3D_REQUIRE(ctx, cc == f->cond_pad, "p3d_flow: 16-bit condition needs cond_channels % 8 == 0");
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->ctx_bf, ctx_feats, sizeof(uint16_t) * f->T * cc, cudaMemcpyDeviceToDevice,
+                                  ctx->stream));
+    return P3D_OK;
+}
+}  // namespace
+
+extern "C" int p3d_flow_forward(p3d_flow *f, const float *x, const float *timesteps, const void *ctx_feats,
+                                int ctx_dtype, const float *proj, float *out) {
+    if (!f) return P3D_ERR_INVALID;
+    p3d_ctx *ctx = f->ctx;
+    P3D_REQUIRE(ctx, f->prepared, "p3d_flow_forward: call p3d_flow_prepare first");
+    P3D_REQUIRE(ctx, x && timesteps && ctx_feats && out, "SLat flow input, timestep, or context shape mismatch");
+    P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
+    P3D_TRY(load_ctx(f, ctx_feats, ctx_dtype));
+    return forward_impl(f, x, timesteps, 1, nullptr, 1.0f, proj, out);
+}
+
+extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
+                               const p3d_sampler_config *cfg) {
+    if (!f || !cfg) return P3D_ERR_INVALID;
+    p3d_ctx *ctx = f->ctx;
+    P3D_REQUIRE(ctx, f->prepared, "p3d_flow_sample: call p3d_flow_prepare first");
+    P3D_REQUIRE(ctx, f->batch % 2 == 0, "p3d_flow_sample: batch must be 2 x images (conditional, unconditional)");
+    P3D_REQUIRE(ctx, f->hp.in_channels == f->hp.out_channels, "p3d_flow_sample: in/out channels differ");
+    P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
+    P3D_REQUIRE(ctx, cfg->steps > 0 && cfg->sigma_min >= 0.0f && cfg->sigma_min < 1.0f && cfg->rescale_t > 0.0f &&
+                         cfg->guidance_rescale >= 0.0f && cfg->guidance_interval_min <= cfg->guidance_interval_max,
+                "invalid flow Euler sampler configuration");
+    const int I = f->batch / 2;
+    // Both halves must hold the same rows in the same order.
+    std::vector<int32_t> off(f->batch + 1);
+    P3D_CUDA(ctx, cudaMemcpy(off.data(), f->fine_off, sizeof(int32_t) * (f->batch + 1), cudaMemcpyDeviceToHost));
+    const int64_t half = off[I];
+    P3D_REQUIRE(ctx, 2 * half == f->n, "p3d_flow_sample: unconditional half must mirror the conditional half");
+    const int ch = f->hp.in_channels;
+    // t schedule (src/flow_sampler.cpp:268-286), computed in f32 like the reference
+    std::vector<float> sched(4 * (cfg->steps + 1), 0.0f);
+    const float steps = static_cast<float>(cfg->steps);
+    for (int s = 0; s < cfg->steps; ++s) {
+        const float lin = 1.0f - static_cast<float>(s) / steps;
+        const float den = 1.0f + (cfg->rescale_t - 1.0f) * lin;
+        const float t = cfg->rescale_t * lin / den;
+        const float nl = 1.0f - static_cast<float>(s + 1) / steps;
+        const float nden = 1.0f + (cfg->rescale_t - 1.0f) * nl;
+        const float tn = cfg->rescale_t * nl / nden;
+        if (!(den > 0.0f) || !(nden > 0.0f)) return set_error(ctx, P3D_ERR_INVALID, "flow Euler timestep schedule is not finite");
+        const bool in_interval = t >= cfg->guidance_interval_min && t <= cfg->guidance_interval_max;
+        sched[4 * s] = t;
+        sched[4 * s + 1] = tn;
+        sched[4 * s + 2] = in_interval ? cfg->guidance_strength : 1.0f;
+    }
+    if (!f->sched) P3D_TRY(f->alloc(&f->sched, 4 * 4096));
+    P3D_REQUIRE(ctx, cfg->steps < 4096, "p3d_flow_sample: too many steps");
+    StreamSwap swap(ctx, f->stream);
+    // order after the caller's stream
+    cudaEvent_t ev;
+    P3D_CUDA(ctx, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaEventRecord(ev, swap.saved);
+    cudaStreamWaitEvent(f->stream, ev, 0);
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->sched, sched.data(), sizeof(float) * sched.size(), cudaMemcpyHostToDevice, f->stream));
+    P3D_CUDA(ctx, cudaMemsetAsync(f->counter, 0, sizeof(int), f->stream));
+    // condition: conditional tokens for items [0, I), zeros for [I, 2I)
+    P3D_TRY(load_ctx(f, ctx_feats, ctx_dtype));
+    {
+        std::vector<int32_t> coff(f->batch + 1);
+        P3D_CUDA(ctx, cudaMemcpy(coff.data(), f->ctx_off, sizeof(int32_t) * (f->batch + 1), cudaMemcpyDeviceToHost));
+        const int64_t z0 = coff[I], z1 = coff[f->batch];
+        P3D_CUDA(ctx, cudaMemsetAsync(f->ctx_bf + z0 * f->cond_pad, 0, sizeof(uint16_t) * (z1 - z0) * f->cond_pad,
+                                      f->stream));
+    }
+    const float *proj_model = nullptr;
+    float *proj_buf = nullptr;
+    if (f->hp.proj_mode) {
+        P3D_TRY(f->alloc(&proj_buf, f->n * f->hp.proj_in_channels));
+        const int64_t hp_rows = half * f->hp.proj_in_channels;
+        P3D_CUDA(ctx, cudaMemcpyAsync(proj_buf, proj, sizeof(float) * hp_rows, cudaMemcpyDeviceToDevice, f->stream));
+        zero_f32_rows_kernel<<<blocks_for(hp_rows, 256), 256, 0, f->stream>>>(proj_buf + hp_rows, hp_rows);
+        P3D_TRY(check_launch(ctx, "zero_rows"));
+        proj_model = proj_buf;
+    }
+    // model input = [x; x]
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model + half * ch, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice,
+                                  f->stream));
+    const bool rescale = cfg->guidance_rescale > 0.0f;
+    auto one_step = [&]() -> int {
+        P3D_TRY(forward_impl(f, f->x_model, f->sched, 0, f->counter, 1000.0f, proj_model, f->vel));
+        const float *vp = f->vel, *vn = f->vel + half * ch;
+        if (rescale) {
+            P3D_CUDA(ctx, cudaMemsetAsync(f->stats, 0, sizeof(double) * 4 * I, f->stream));
+            euler_sched_stats_kernel<<<blocks_for(half, 8), 256, 0, f->stream>>>(
+                x, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, cfg->sigma_min, f->stats);
+            P3D_TRY(check_launch(ctx, "euler_stats"));
+        }
+        euler_sched_kernel<<<blocks_for(half * ch, 256), 256, 0, f->stream>>>(
+            x, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, cfg->guidance_rescale, cfg->sigma_min,
+            rescale ? f->stats : nullptr, f->x_model);
+        P3D_TRY(check_launch(ctx, "euler_sched"));
+        advance_kernel<<<1, 1, 0, f->stream>>>(f->counter);
+        return check_launch(ctx, "advance");
+    };
+    const int64_t l0 = ctx->launches;
+    int rc = one_step();
+    f->launches_per_step = ctx->launches - l0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (!rc && cfg->steps > 1 && cfg->use_graph) {
+        if (cudaStreamBeginCapture(f->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            rc = set_error(ctx, P3D_ERR_CUDA, "cudaStreamBeginCapture failed");
+        if (!rc) {
+            const int rc_cap = one_step();
+            const cudaError_t e = cudaStreamEndCapture(f->stream, &graph);
+            if (rc_cap) rc = rc_cap;
+            else if (e != cudaSuccess) rc = set_error(ctx, P3D_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+        }
+        if (!rc && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+            rc = set_error(ctx, P3D_ERR_CUDA, "cudaGraphInstantiate failed");
+    }
+    for (int s = 1; s < cfg->steps && !rc; ++s) {
+        if (exec) {
+            if (cudaGraphLaunch(exec, f->stream) != cudaSuccess) rc = set_error(ctx, P3D_ERR_CUDA, "cudaGraphLaunch failed");
+            ++ctx->launches;
+        } else {
+            rc = one_step();
+        }
+    }
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    cudaEventRecord(ev, f->stream);
+    cudaStreamWaitEvent(swap.saved, ev, 0);
+    cudaEventDestroy(ev);
+    return rc;
+}
+
+extern "C" int64_t p3d_flow_launches_per_step(const p3d_flow *f) { return f ? f->launches_per_step : 0; }

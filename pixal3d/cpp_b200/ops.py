@@ -1,0 +1,282 @@
+"""Torch-tensor front end of the C ABI (include/p3d.h).
+
+PyTorch is plumbing here: it owns device memory and streams.  Every compute
+call goes to libp3dcuda.so; each wrapper validates shapes/dtypes, passes raw
+device pointers and the current torch stream, and raises P3DError on a
+non-zero status.  Names follow the reference's operators
+(src/sparse.cpp, src/sparse_transformer.cpp, src/flow_sampler.cpp).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+from ._lib import P3DError
+
+_CTX: dict[int, "Context"] = {}
+
+
+class Context:
+    """One p3d_ctx per device; its stream follows torch's current stream."""
+
+    def __init__(self, device: int):
+        h = C.c_void_p()
+        rc = L.lib.p3d_ctx_create(device, None, C.byref(h))
+        if rc != 0:
+            raise P3DError(rc, f"p3d_ctx_create(device={device}) failed")
+        self.h = h
+        self.device = device
+
+    def bind(self) -> "Context":
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        L.lib.p3d_ctx_set_stream(self.h, C.c_void_p(s))
+        return self
+
+    def check(self, rc: int) -> None:
+        if rc != 0:
+            raise P3DError(rc, L.lib.p3d_last_error(self.h).decode())
+
+    def sync_check(self) -> None:
+        self.check(L.lib.p3d_ctx_check(self.h))
+
+    @property
+    def launches(self) -> int:
+        return int(L.lib.p3d_ctx_launch_count(self.h))
+
+
+def ctx(device: torch.device | int | None = None) -> Context:
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, torch.device):
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    else:
+        idx = int(device)
+    if idx not in _CTX:
+        _CTX[idx] = Context(idx)
+    return _CTX[idx].bind()
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return L.P3D_F32
+    if t.dtype == torch.bfloat16:
+        return L.P3D_BF16
+    if t.dtype == torch.float16:
+        return L.P3D_F16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+HALF = (torch.bfloat16, torch.float16)
+
+
+def _rows(t: torch.Tensor) -> int:
+    """Row pitch (elements) of a 2-D row-major view with unit column stride."""
+    assert t.dim() == 2 and t.stride(1) == 1, "expected a 2-D row-major view"
+    return t.stride(0)
+
+
+# ---------------------------------------------------------------- topology
+
+def neighbor_map27(coords: torch.Tensor) -> torch.Tensor:
+    """[27, n] int32 neighbour map, sentinel n (build_neighbor_gather_map,
+    src/slat_decoder.cpp:609-714)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    ws_bytes = int(L.lib.p3d_neighbor_map27_workspace(n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=coords.device)
+    out = torch.empty((27, n), dtype=torch.int32, device=coords.device)
+    c.check(L.lib.p3d_neighbor_map27_ws(c.h, _p(coords), n, _p(ws), ws_bytes, _p(out)))
+    return out
+
+
+def downsample_topology(coords: torch.Tensor, batch: int, shape, factor: int = 2):
+    """Parents of sparse_downsample_mean (src/sparse.cpp:536-602).
+    Returns (out_coords [m,4], parent [n], child [m, f^3], m)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    gints = int(L.lib.p3d_downsample_grid_ints(batch, *shape, factor))
+    grid = torch.empty(gints, dtype=torch.int32, device=coords.device)
+    oc = torch.empty((max(n, 1), 4), dtype=torch.int32, device=coords.device)
+    parent = torch.empty(max(n, 1), dtype=torch.int32, device=coords.device)
+    child = torch.empty((max(n, 1), factor ** 3), dtype=torch.int32, device=coords.device)
+    m = torch.zeros(1, dtype=torch.int64, device=coords.device)
+    c.check(L.lib.p3d_downsample_topology(c.h, _p(coords), n, batch, *shape, factor, _p(grid), _p(oc), _p(parent),
+                                          _p(child), _p(m)))
+    mm = int(m.item())
+    return oc[:mm], parent[:n], child[:mm], mm
+
+
+def downsample_mean(x: torch.Tensor, child: torch.Tensor, factor: int = 2) -> torch.Tensor:
+    c = ctx(x.device)
+    m = child.shape[0]
+    out = torch.empty((m, x.shape[1]), dtype=x.dtype, device=x.device)
+    c.check(L.lib.p3d_downsample_mean(c.h, _p(x), m, x.shape[1], factor, _p(child), _dt(x), _p(out)))
+    return out
+
+
+def upsample_nearest(x: torch.Tensor, parent: torch.Tensor) -> torch.Tensor:
+    c = ctx(x.device)
+    n = parent.shape[0]
+    out = torch.empty((n, x.shape[1]), dtype=x.dtype, device=x.device)
+    c.check(L.lib.p3d_upsample_nearest(c.h, _p(x), n, x.shape[1], _p(parent), _dt(x), _p(out)))
+    return out
+
+
+def c2s_topology(coords: torch.Tensor, factor: int = 2, mask: torch.Tensor | None = None):
+    """Subdivision topology (sparse_channel_to_spatial, src/sparse.cpp:604-702).
+    Returns (out_coords [m,4], src_row [m], src_child [m], m)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    nc = factor ** 3
+    scratch = torch.empty(n + 1, dtype=torch.int64, device=coords.device)
+    oc = torch.empty((max(n * nc, 1), 4), dtype=torch.int32, device=coords.device)
+    sr = torch.empty(max(n * nc, 1), dtype=torch.int32, device=coords.device)
+    sc = torch.empty(max(n * nc, 1), dtype=torch.int8, device=coords.device)
+    m = torch.zeros(1, dtype=torch.int64, device=coords.device)
+    if mask is not None:
+        assert mask.dtype == torch.float32 and mask.shape == (n, nc)
+    c.check(L.lib.p3d_c2s_topology(c.h, _p(coords), n, factor, _p(mask), _p(scratch), _p(oc), _p(sr), _p(sc), _p(m)))
+    mm = int(m.item())
+    return oc[:mm], sr[:mm], sc[:mm], mm
+
+
+def c2s_gather(x: torch.Tensor, src_row: torch.Tensor, src_child: torch.Tensor, cout: int,
+               repeat: int = 1) -> torch.Tensor:
+    c = ctx(x.device)
+    m = src_row.shape[0]
+    out = torch.empty((m, cout * repeat), dtype=x.dtype, device=x.device)
+    c.check(L.lib.p3d_c2s_gather(c.h, _p(x), x.shape[1], _p(src_row), _p(src_child), m, cout, repeat, _dt(x),
+                                 _p(out)))
+    return out
+
+
+# ------------------------------------------------------------ contractions
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+           out_dtype: torch.dtype = torch.bfloat16, epilogue: int = L.EPI_NONE, gate: torch.Tensor | None = None,
+           batch_offsets: torch.Tensor | None = None) -> torch.Tensor:
+    """epilogue(x W^T + b) on tcgen05 (sparse_linear, src/sparse.cpp:337-451).
+    x and w: the same 16-bit type (bf16 or f16)."""
+    assert x.dtype in HALF and w.dtype == x.dtype
+    c = ctx(x.device)
+    m, k = x.shape
+    n = w.shape[0]
+    assert w.shape[1] == k and w.is_contiguous()
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    gate_ld = gate.stride(0) if gate is not None else 0
+    nb = batch_offsets.shape[0] - 1 if batch_offsets is not None else 0
+    c.check(L.lib.p3d_linear(c.h, _p(x), _rows(x), _p(w), _dt(x), _p(bias), m, n, k, _p(out), _rows(out), _dt(out), epilogue,
+                             _p(gate), gate_ld, _p(batch_offsets), nb))
+    return out
+
+
+def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32,
+                epilogue: int = L.EPI_NONE, gate: torch.Tensor | None = None,
+                batch_offsets: torch.Tensor | None = None) -> torch.Tensor:
+    """Gather-GEMM submanifold conv (sparse_submanifold_conv3d, src/sparse.cpp:999-1055).
+    x [n, cin], w [27, cout, cin], both bf16 or both f16."""
+    assert x.dtype in HALF and w.dtype == x.dtype and x.is_contiguous() and w.is_contiguous()
+    c = ctx(x.device)
+    n, cin = x.shape
+    cout = w.shape[1]
+    if out is None:
+        out = torch.empty((n, cout), dtype=out_dtype, device=x.device)
+    gate_ld = gate.stride(0) if gate is not None else 0
+    nb = batch_offsets.shape[0] - 1 if batch_offsets is not None else 0
+    c.check(L.lib.p3d_subm_conv3d(c.h, _p(x), n, cin, _p(nbr), _p(w), _dt(x), _p(bias), cout, _p(out), _rows(out), _dt(out),
+                                  epilogue, _p(gate), gate_ld, _p(batch_offsets), nb))
+    return out
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: torch.Tensor, cu_k: torch.Tensor,
+                     max_q: int, heads: int, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Flash attention over packed ragged sequences, head_dim 64
+    (sparse_scaled_dot_product_attention / sparse_cross_attention)."""
+    c = ctx(q.device)
+    assert q.dtype in HALF and k.dtype == q.dtype and v.dtype == q.dtype
+    if out is None:
+        out = torch.empty((q.shape[0], heads * 64), dtype=q.dtype, device=q.device)
+    c.check(L.lib.p3d_varlen_attention(c.h, _p(q), _rows(q), _p(k), _rows(k), _p(v), _rows(v), _p(out), _rows(out),
+                                       _p(cu_q), _p(cu_k), cu_q.shape[0] - 1, max_q, heads, 64, scale, _dt(q)))
+    return out
+
+
+# ------------------------------------------------------------ elementwise
+
+def layernorm_modulate(x: torch.Tensor, eps: float, gamma=None, beta=None, mod: torch.Tensor | None = None,
+                       batch_offsets: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm (+affine) (+AdaLN: mod rows are [shift(C) | scale(C) | ...])."""
+    assert x.dtype == torch.float32 and x.is_contiguous()
+    c = ctx(x.device)
+    n, ch = x.shape
+    if out is None:
+        out = torch.empty((n, ch), dtype=out_dtype, device=x.device)
+    nb = batch_offsets.shape[0] - 1 if batch_offsets is not None else 0
+    c.check(L.lib.p3d_layernorm_modulate(c.h, _p(x), n, ch, eps, _p(gamma), _p(beta), _p(mod),
+                                         mod.stride(0) if mod is not None else 0, _p(batch_offsets), nb, _p(out),
+                                         _dt(out)))
+    return out
+
+
+def qk_rmsnorm_rope(x: torch.Tensor, heads: int, head_dim: int, gamma: torch.Tensor | None = None,
+                    coords: torch.Tensor | None = None, freq_min: float = 1.0, freq_base: float = 10000.0) -> None:
+    """In place on 16-bit rows (view with row pitch)."""
+    assert x.dtype in HALF
+    c = ctx(x.device)
+    c.check(L.lib.p3d_qk_rmsnorm_rope(c.h, _p(x), x.shape[0], _rows(x), heads, head_dim, _p(gamma), _p(coords),
+                                      freq_min, freq_base, _dt(x)))
+
+
+def activation(x: torch.Tensor, act: int) -> torch.Tensor:
+    c = ctx(x.device)
+    out = torch.empty_like(x)
+    c.check(L.lib.p3d_activation(c.h, _p(x), x.numel(), act, _dt(x), _p(out)))
+    return out
+
+
+def group_norm_silu(x: torch.Tensor, groups: int, eps: float, gamma, beta, batch_offsets: torch.Tensor,
+                    silu: bool = True, out_dtype=torch.bfloat16) -> torch.Tensor:
+    c = ctx(x.device)
+    n, ch = x.shape
+    nb = batch_offsets.shape[0] - 1
+    stats = torch.empty(2 * nb * groups, dtype=torch.float64, device=x.device)
+    out = torch.empty((n, ch), dtype=out_dtype, device=x.device)
+    c.check(L.lib.p3d_group_norm_silu(c.h, _p(x), n, ch, groups, eps, _p(gamma), _p(beta), _p(batch_offsets), nb,
+                                      int(silu), _p(stats), _p(out), _dt(out)))
+    return out
+
+
+def euler_cfg_step(x: torch.Tensor, v_pos: torch.Tensor, v_neg: torch.Tensor | None, batch_offsets: torch.Tensor,
+                   t: float, t_next: float, guidance: float, guidance_rescale: float, sigma_min: float) -> None:
+    c = ctx(x.device)
+    n, ch = x.shape
+    nb = batch_offsets.shape[0] - 1
+    stats = torch.empty(4 * nb, dtype=torch.float64, device=x.device)
+    c.check(L.lib.p3d_euler_cfg_step(c.h, _p(x), _p(v_pos), _p(v_neg), n, ch, _p(batch_offsets), nb, t, t_next,
+                                     guidance, guidance_rescale, sigma_min, _p(stats)))
+
+
+def convert(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    c = ctx(x.device)
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    c.check(L.lib.p3d_convert(c.h, _p(x), _dt(x), x.numel(), _p(out), _dt(out)))
+    return out
+
+
+def batch_offsets_of(coords: torch.Tensor, batch: int) -> torch.Tensor:
+    """int32 [batch+1] row offsets of a batch-contiguous coordinate list."""
+    b = coords[:, 0].to(torch.int64)
+    counts = torch.bincount(b, minlength=batch)
+    off = torch.zeros(batch + 1, dtype=torch.int32, device=coords.device)
+    off[1:] = torch.cumsum(counts, 0).to(torch.int32)
+    return off

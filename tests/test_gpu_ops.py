@@ -1,0 +1,428 @@
+"""GPU parity of each kernel behind the C ABI against the pinned oracle.
+
+Tolerances: integer/topology outputs bit-exact; feature outputs within the
+north-star bound max-abs 2e-2 and relative-L2 5e-3 against the f32 oracle.
+GEMM-class kernels are additionally checked tightly (relative-L2 2e-3... see
+TIGHT) against a torch fp32 computation on the SAME bf16-rounded operands, so
+an indexing or layout bug cannot hide inside the bf16 tolerance.
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import oracle as O
+from pixal3d.cpp_b200.workloads import shell_coords, batched
+from tests import _fixtures as FX
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+REL_L2 = 5e-3
+TIGHT = 2e-3
+
+
+def ops():
+    from pixal3d.cpp_b200 import ops as _ops
+    return _ops
+
+
+def L():
+    from pixal3d.cpp_b200 import _lib
+    return _lib
+
+
+def check(actual, expected, max_abs=MAX_ABS, rel_l2=REL_L2, what=""):
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert a.shape == e.shape, (what, a.shape, e.shape)
+    err = np.abs(a - e)
+    mx = float(err.max()) if err.size else 0.0
+    rl = float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30)) if err.size else 0.0
+    assert mx <= max_abs and rl <= rel_l2, f"{what}: max_abs {mx:.3e} (<= {max_abs}) rel_l2 {rl:.3e} (<= {rel_l2})"
+    return mx, rl
+
+
+def bf16_out_tol(expected):
+    """Max-abs bound for a bf16-STORED output: the north-star 2e-2 scaled by
+    the output magnitude, since storing |y| ~ 4 in bf16 alone moves it by up
+    to |y| * 2^-9."""
+    return MAX_ABS * max(1.0, float(np.abs(expected).max()))
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def bf(a):
+    return dev(a.astype(np.float32), torch.bfloat16)
+
+
+def hf(a):
+    return dev(a.astype(np.float32), torch.float16)
+
+
+def rounded16(a):
+    """float32 values of a after f16 rounding."""
+    return np.ascontiguousarray(a.astype(np.float32)).astype(np.float16).astype(np.float32)
+
+
+def rounded(a):
+    """float32 values of a after bf16 rounding (what the kernel consumes)."""
+    return torch.from_numpy(np.ascontiguousarray(a.astype(np.float32))).to(torch.bfloat16).float().numpy()
+
+
+# ----------------------------------------------------------- topology
+
+def test_neighbor_map_config0_bitexact():
+    c = shell_coords()
+    got = ops().neighbor_map27(dev(c)).cpu().numpy()
+    np.testing.assert_array_equal(got, O.neighbor_map27(c))
+    assert int((got < c.shape[0]).sum()) == 453614
+
+
+def test_neighbor_map_golden_bitexact():
+    v = np.load(FX.GOLDEN / "ref_vectors.npz")
+    got = ops().neighbor_map27(dev(v["coords"])).cpu().numpy()
+    np.testing.assert_array_equal(got, v["nbr"])
+
+
+def test_neighbor_map_edge_cases():
+    o = ops()
+    one = np.array([[0, 5, 5, 5]], np.int32)
+    got = o.neighbor_map27(dev(one)).cpu().numpy()
+    exp = np.full((27, 1), 1, np.int32)
+    exp[13, 0] = 0
+    np.testing.assert_array_equal(got, exp)
+    # a duplicated coordinate latches P3D_ERR_DUPLICATE
+    dup = np.array([[0, 1, 1, 1], [0, 1, 1, 1]], np.int32)
+    o.neighbor_map27(dev(dup))
+    with pytest.raises(L().P3DError) as e:
+        o.ctx().sync_check()
+    assert e.value.status == L().P3D_ERR_DUPLICATE
+
+
+def test_downsample_bitexact():
+    o = ops()
+    v = np.load(FX.GOLDEN / "ref_vectors.npz")
+    c = v["coords"]
+    oc, parent, child, m = o.downsample_topology(dev(c), 2, (16, 16, 16), 2)
+    np.testing.assert_array_equal(oc.cpu().numpy(), v["down_coords"])
+    feats = o.downsample_mean(dev(v["conv_x"]), child, 2).cpu().numpy()
+    # f32 in octant order == reference summation order: bit-identical
+    np.testing.assert_array_equal(feats, v["down_feats"])
+    # config-0 shell, batch 2 (CFG pair)
+    c2 = batched(shell_coords(), 2)
+    oc2, parent2, _, m2 = o.downsample_topology(dev(c2), 2, (64, 64, 64), 2)
+    rc, _, rp = O.downsample_mean(c2, np.zeros((c2.shape[0], 1), np.float32), 2)
+    np.testing.assert_array_equal(oc2.cpu().numpy(), rc)
+    np.testing.assert_array_equal(parent2.cpu().numpy(), rp)
+    assert m2 == 2 * 4092
+
+
+def test_c2s_bitexact():
+    o = ops()
+    v = np.load(FX.GOLDEN / "ref_vectors.npz")
+    c = v["coords"]
+    oc, sr, sc, m = o.c2s_topology(dev(c), 2, dev(v["c2s_mask"]))
+    np.testing.assert_array_equal(oc.cpu().numpy(), v["c2s_coords"])
+    feats = o.c2s_gather(dev(v["c2s_x"]), sr, sc, 3).cpu().numpy()
+    np.testing.assert_array_equal(feats, v["c2s_feats"])
+    # unmasked + the fixture's packed example
+    d = FX.sparse_fixture()
+    g = FX.parse_golden("sparse_numeric_fixture")
+    oc, sr, sc, m = o.c2s_topology(dev(d["packed_coords"]), 2, dev(d["subdiv"]))
+    np.testing.assert_array_equal(oc.cpu().numpy().ravel(), g["sparse_channel_to_spatial_coords"].astype(np.int32))
+    np.testing.assert_allclose(o.c2s_gather(dev(d["packed"]), sr, sc, 2).cpu().numpy().ravel(),
+                               g["sparse_channel_to_spatial_output"], atol=1e-7)
+    oc, sr, sc, m = o.c2s_topology(dev(c), 2, None)
+    assert m == 8 * c.shape[0]
+
+
+# -------------------------------------------------------- contractions
+
+@pytest.mark.parametrize("m,n,k", [(1, 64, 64), (130, 8, 8), (300, 96, 72), (4133, 256, 64), (1000, 384, 1024),
+                                   (777, 200, 136), (8192, 1024, 1024)])
+def test_linear_shapes(m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32) * 0.1
+    o = ops()
+    y32 = o.linear(bf(x), bf(w), dev(b), out_dtype=torch.float32).cpu().numpy()
+    tight = rounded(x) @ rounded(w).T + b
+    check(y32, tight, max_abs=1e-3 * max(1, np.abs(tight).max()), rel_l2=1e-5, what="linear vs bf16-rounded fp32")
+    check(y32, O.linear(x, w, b), what="linear vs oracle")
+    y16 = o.linear(bf(x), bf(w), dev(b), out_dtype=torch.bfloat16).float().cpu().numpy()
+    ref = O.linear(x, w, b)
+    check(y16, ref, max_abs=bf16_out_tol(ref), what="linear bf16 out")
+
+
+def test_linear_epilogues():
+    rng = np.random.default_rng(3)
+    m, n, k = 1000, 512, 256
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32) * 0.1
+    o = ops()
+    ref = O.linear(x, w, b)
+    g = o.linear(bf(x), bf(w), dev(b), out_dtype=torch.float32, epilogue=L().EPI_GELU_TANH).cpu().numpy()
+    check(g, O.gelu_tanh(ref), what="gelu epilogue")
+    s = o.linear(bf(x), bf(w), dev(b), out_dtype=torch.bfloat16, epilogue=L().EPI_SILU).float().cpu().numpy()
+    check(s, O.silu(ref), max_abs=bf16_out_tol(O.silu(ref)), what="silu epilogue")
+    # gated residual with two batch items split at row 600
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    gate = rng.standard_normal((2, n)).astype(np.float32)
+    offs = np.array([0, 600, m], np.int32)
+    out = dev(res.copy())
+    o.linear(bf(x), bf(w), dev(b), out=out, epilogue=L().EPI_RESIDUAL, gate=dev(gate), batch_offsets=dev(offs))
+    bidx = np.where(np.arange(m) < 600, 0, 1)
+    exp = res + gate[bidx] * ref
+    check(out.cpu().numpy(), exp, max_abs=bf16_out_tol(exp) / 4, what="residual epilogue")
+
+
+def test_linear_strided_input():
+    """A column slice of a wider row (the attention output / qkv views)."""
+    rng = np.random.default_rng(5)
+    m, k, n = 513, 128, 192
+    big = rng.standard_normal((m, 3 * k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    t = bf(big)
+    y = ops().linear(t[:, k:2 * k], bf(w), None, out_dtype=torch.float32).cpu().numpy()
+    check(y, rounded(big[:, k:2 * k]) @ rounded(w).T, max_abs=1e-3, rel_l2=1e-5, what="strided A")
+
+
+def _conv_case(coords, cin, cout, seed):
+    rng = np.random.default_rng(seed)
+    n = coords.shape[0]
+    x = rng.standard_normal((n, cin)).astype(np.float32)
+    w = (rng.standard_normal((27, cout, cin)) / math.sqrt(27 * cin)).astype(np.float32)
+    b = (rng.standard_normal(cout) * 0.1).astype(np.float32)
+    return x, w, b
+
+
+@pytest.mark.parametrize("cin,cout", [(64, 64), (128, 384), (64, 8)])
+def test_subm_conv3d(cin, cout):
+    c = shell_coords() if cin == 64 and cout == 64 else shell_coords(40, 14.0, 1.3)
+    x, w, b = _conv_case(c, cin, cout, cin + cout)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    got = o.subm_conv3d(bf(x), nbr, bf(w), dev(b), out_dtype=torch.float32).cpu().numpy()
+    nb = O.neighbor_map27(c)
+    tight = O.subm_conv3d(c, rounded(x), rounded(w), b, nb)
+    check(got, tight, max_abs=2e-3, rel_l2=TIGHT * 0.05, what="conv vs bf16-rounded fp32")
+    check(got, O.subm_conv3d(c, x, w, b, nb), what="conv vs oracle")
+
+
+def test_subm_conv3d_residual_bf16():
+    c = shell_coords(32, 10.0, 1.2)
+    x, w, b = _conv_case(c, 64, 128, 9)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    ref = O.subm_conv3d(c, x, w, b)
+    y16 = o.subm_conv3d(bf(x), nbr, bf(w), dev(b), out_dtype=torch.bfloat16).float().cpu().numpy()
+    check(y16, ref, max_abs=bf16_out_tol(ref), what="conv bf16 out")
+    res = np.random.default_rng(1).standard_normal(ref.shape).astype(np.float32)
+    out = dev(res.copy())
+    o.subm_conv3d(bf(x), nbr, bf(w), dev(b), out=out, epilogue=L().EPI_RESIDUAL)
+    check(out.cpu().numpy(), res + ref, what="conv residual")
+
+
+def test_sparse_fixture_ops_on_gpu():
+    """The reference's sparse_numeric_fixture inputs through the GPU kernels
+    (channels zero-padded to the kernels' granularity, as the host layer
+    does) against the reference's own outputs."""
+    d = FX.sparse_fixture()
+    g = FX.parse_golden("sparse_numeric_fixture")
+    o = ops()
+    c = d["coords"]
+    xp = np.zeros((10, 64), np.float32)
+    xp[:, :3] = d["x"]
+    wl = np.zeros((4, 8), np.float32)
+    wl[:, :3] = d["lin_w"]
+    y = o.linear(bf(xp[:, :8].copy()), bf(wl), dev(d["lin_b"]), out_dtype=torch.float32).cpu().numpy()
+    check(y.ravel(), g["sparse_linear_output"], what="fixture linear")
+    wc = np.zeros((27, 4, 64), np.float32)
+    wc[:, :, :3] = d["conv_w"]
+    nbr = o.neighbor_map27(dev(c))
+    y = o.subm_conv3d(bf(xp), nbr, bf(wc), dev(d["conv_b"]), out_dtype=torch.float32).cpu().numpy()
+    check(y.ravel(), g["sparse_conv_output"], what="fixture conv")
+    y = o.layernorm_modulate(dev(d["x"]), 1e-5, dev(d["gamma"]), dev(d["beta"]), out_dtype=torch.float32)
+    check(y.cpu().numpy().ravel(), g["sparse_norm_output"], max_abs=1e-5, rel_l2=1e-6, what="fixture layernorm")
+    dc, parent, child, m = o.downsample_topology(dev(c), 2, (4, 4, 4), 2)
+    np.testing.assert_array_equal(dc.cpu().numpy().ravel(), g["sparse_downsample_coords"].astype(np.int32))
+    y = o.downsample_mean(dev(d["x"]), child, 2).cpu().numpy()
+    check(y.ravel(), g["sparse_downsample_output"], max_abs=1e-6, rel_l2=1e-7, what="fixture downsample")
+
+
+# ------------------------------------------------------------ elementwise
+
+def test_layernorm_modulate():
+    rng = np.random.default_rng(4)
+    n, C = 3001, 1024
+    x = (rng.standard_normal((n, C)) * 3 + 1).astype(np.float32)
+    offs = np.array([0, 1500, n], np.int32)
+    tmod = rng.standard_normal((2, 6 * C)).astype(np.float32) * 0.3
+    bmod = rng.standard_normal(6 * C).astype(np.float32) * 0.1
+    mod = (tmod + bmod[None, :]).astype(np.float32)
+    bidx = np.where(np.arange(n) < 1500, 0, 1)
+    o = ops()
+    for off in (0, 3 * C):
+        got = o.layernorm_modulate(dev(x), 1e-6, mod=dev(mod)[:, off:], batch_offsets=dev(offs)).float().cpu().numpy()
+        exp = O.affine_modulate(O.layer_norm(x, 1e-6), bmod, tmod.ravel(), bidx, C, off)
+        check(got, exp, what=f"ln+mod offset {off}")
+    gam = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
+    bet = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    got = o.layernorm_modulate(dev(x), 1e-6, dev(gam), dev(bet), out_dtype=torch.float32).cpu().numpy()
+    check(got, O.layer_norm(x, 1e-6, gam, bet), max_abs=1e-4, rel_l2=1e-6, what="ln affine f32")
+    # odd channel count (no vector path)
+    x3 = rng.standard_normal((17, 12)).astype(np.float32)
+    got = o.layernorm_modulate(dev(x3), 1e-5, out_dtype=torch.float32).cpu().numpy()
+    check(got, O.layer_norm(x3, 1e-5), max_abs=1e-5, rel_l2=1e-6, what="ln C=12")
+
+
+def test_qk_rmsnorm_rope():
+    rng = np.random.default_rng(8)
+    c = batched(shell_coords(32, 11.0, 1.0), 2)
+    n, H, hd = c.shape[0], 16, 64
+    q = rng.standard_normal((n, 3 * H * hd)).astype(np.float32)
+    gam = (1 + rng.standard_normal(H * hd) * 0.1).astype(np.float32)
+    t = bf(q)
+    o = ops()
+    o.qk_rmsnorm_rope(t[:, :H * hd], H, hd, dev(gam), dev(c))
+    o.qk_rmsnorm_rope(t[:, H * hd:2 * H * hd], H, hd, dev(gam), None)
+    got = t.float().cpu().numpy()
+    qr = rounded(q)
+    check(got[:, :H * hd], O.rope(c, O.rms_norm_heads(qr[:, :H * hd], H, hd, gam), H, hd), what="rms+rope")
+    check(got[:, H * hd:2 * H * hd], O.rms_norm_heads(qr[:, H * hd:2 * H * hd], H, hd, gam), what="rms only")
+    np.testing.assert_array_equal(got[:, 2 * H * hd:], qr[:, 2 * H * hd:])
+    # the fixture's RoPE (hd = 6, remainder pairs unrotated) and RMS outputs
+    d = FX.sparse_fixture()
+    g = FX.parse_golden("sparse_numeric_fixture")
+    t = bf(d["q"])
+    o.qk_rmsnorm_rope(t, 2, 6, None, dev(d["coords"]))
+    check(t.float().cpu().numpy().ravel(), g["sparse_rope_output"], what="fixture rope")
+    t = bf(d["q"])
+    o.qk_rmsnorm_rope(t, 2, 6, dev(d["rms_gamma"]), None)
+    check(t.float().cpu().numpy().ravel(), g["sparse_rms_output"], what="fixture rms")
+
+
+def _attn_case(rng, lq, lk, H=4):
+    q = rng.standard_normal((sum(lq), H * 64)).astype(np.float32)
+    k = rng.standard_normal((sum(lk), H * 64)).astype(np.float32)
+    v = rng.standard_normal((sum(lk), H * 64)).astype(np.float32)
+    cq = np.concatenate([[0], np.cumsum(lq)]).astype(np.int32)
+    ck = np.concatenate([[0], np.cumsum(lk)]).astype(np.int32)
+    return q, k, v, cq, ck
+
+
+@pytest.mark.parametrize("lq,lk", [([1, 77], [1, 77]), ([1000, 333], [1000, 333]), ([129], [1029]),
+                                   ([2048, 2048], [1029, 1029])])
+def test_varlen_attention(lq, lk):
+    rng = np.random.default_rng(sum(lq) + sum(lk))
+    H = 4
+    q, k, v, cq, ck = _attn_case(rng, lq, lk, H)
+    scale = 1.0 / 8.0
+    got = ops().varlen_attention(bf(q), bf(k), bf(v), dev(cq), dev(ck), max(lq), H, scale).float().cpu().numpy()
+    exp = O.varlen_attention(rounded(q), rounded(k), rounded(v), cq, ck, H, 64, scale)
+    check(got, exp, what="attention")
+
+
+def test_attention_strided_qkv_views():
+    """q/k/v as column slices of one packed [n, 3C] buffer (the qkv GEMM output)."""
+    rng = np.random.default_rng(12)
+    H, n = 16, 700
+    qkv = rng.standard_normal((n, 3 * H * 64)).astype(np.float32)
+    cu = np.array([0, 300, n], np.int32)
+    t = bf(qkv)
+    C = H * 64
+    got = ops().varlen_attention(t[:, :C], t[:, C:2 * C], t[:, 2 * C:], dev(cu), dev(cu), 400, H, 0.125)
+    r = rounded(qkv)
+    exp = O.varlen_attention(r[:, :C], r[:, C:2 * C], r[:, 2 * C:], cu, cu, H, 64, 0.125)
+    check(got.float().cpu().numpy(), exp, what="strided attention")
+
+
+def test_group_norm_silu():
+    rng = np.random.default_rng(21)
+    c = batched(shell_coords(24, 8.0, 1.0), 2)
+    n, C = c.shape[0], 256
+    x = (rng.standard_normal((n, C)) * 2 + 0.5).astype(np.float32)
+    gam = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
+    bet = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    o = ops()
+    offs = o.batch_offsets_of(dev(c), 2)
+    got = o.group_norm_silu(dev(x), 32, 1e-5, dev(gam), dev(bet), offs, True, torch.float32).cpu().numpy()
+    exp = O.silu(O.group_norm(c[:, 0].astype(np.int64), x, 32, 1e-5, gam, bet))
+    check(got, exp, max_abs=1e-4, rel_l2=1e-5, what="groupnorm+silu")
+
+
+@pytest.mark.parametrize("g,gr", [(1.0, 0.0), (3.0, 0.0), (2.35, 0.41)])
+def test_euler_cfg_step(g, gr):
+    rng = np.random.default_rng(2)
+    c = batched(shell_coords(16, 5.0, 1.0), 2)
+    n = c.shape[0]
+    x = rng.standard_normal((n, 8)).astype(np.float32)
+    vp = rng.standard_normal((n, 8)).astype(np.float32)
+    vn = rng.standard_normal((n, 8)).astype(np.float32)
+    cfg = O.SamplerConfig(steps=4, sigma_min=0.031, guidance_strength=g, guidance_rescale=gr)
+    t, tn = np.float32(0.7), np.float32(0.45)
+    bidx = c[:, 0].astype(np.int64)
+    pred = O.cfg_combine(x, t, vp, vn, np.float32(g), cfg, bidx, 2) if g != 1.0 else vp
+    exp = x - (t - tn) * pred
+    o = ops()
+    xt = dev(x.copy())
+    o.euler_cfg_step(xt, dev(vp), dev(vn) if g != 1.0 else None, o.batch_offsets_of(dev(c), 2), float(t), float(tn),
+                     g, gr, 0.031)
+    check(xt.cpu().numpy(), exp, max_abs=1e-5, rel_l2=1e-6, what="euler/cfg")
+
+
+# ------------------------------------------------------ f16 operand variants
+
+@pytest.mark.parametrize("m,n,k", [(130, 8, 8), (4133, 256, 64), (2000, 1024, 1024)])
+def test_linear_f16(m, n, k):
+    rng = np.random.default_rng(m * 3 + n + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32) * 0.1
+    o = ops()
+    y = o.linear(hf(x), hf(w), dev(b), out_dtype=torch.float32).cpu().numpy()
+    tight = rounded16(x) @ rounded16(w).T + b
+    check(y, tight, max_abs=1e-3 * max(1, np.abs(tight).max()), rel_l2=1e-5, what="f16 linear vs rounded fp32")
+    check(y, O.linear(x, w, b), max_abs=3e-3, rel_l2=1e-3, what="f16 linear vs oracle")
+    y16 = o.linear(hf(x), hf(w), dev(b), out_dtype=torch.float16).float().cpu().numpy()
+    check(y16, O.linear(x, w, b), max_abs=3e-3 * max(1, np.abs(tight).max()), rel_l2=1e-3, what="f16 out")
+
+
+def test_subm_conv3d_f16():
+    c = shell_coords()
+    x, w, b = _conv_case(c, 64, 64, 77)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    got = o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out_dtype=torch.float32).cpu().numpy()
+    nb = O.neighbor_map27(c)
+    check(got, O.subm_conv3d(c, rounded16(x), rounded16(w), b, nb), max_abs=1e-3, rel_l2=1e-4, what="f16 conv tight")
+    check(got, O.subm_conv3d(c, x, w, b, nb), max_abs=3e-3, rel_l2=1e-3, what="f16 conv vs oracle")
+
+
+def test_varlen_attention_f16():
+    rng = np.random.default_rng(99)
+    H = 4
+    q, k, v, cq, ck = _attn_case(rng, [700, 1300], [700, 1300], H)
+    got = ops().varlen_attention(hf(q), hf(k), hf(v), dev(cq), dev(ck), 1300, H, 0.125).float().cpu().numpy()
+    exp = O.varlen_attention(q, k, v, cq, ck, H, 64, 0.125)
+    check(got, exp, max_abs=5e-3, rel_l2=1e-3, what="f16 attention")
+
+
+def test_qk_rmsnorm_rope_f16():
+    rng = np.random.default_rng(18)
+    c = shell_coords(32, 11.0, 1.0)
+    n, H, hd = c.shape[0], 16, 64
+    q = rng.standard_normal((n, H * hd)).astype(np.float32)
+    gam = (1 + rng.standard_normal(H * hd) * 0.1).astype(np.float32)
+    t = hf(q)
+    ops().qk_rmsnorm_rope(t, H, hd, dev(gam), dev(c))
+    check(t.float().cpu().numpy(), O.rope(c, O.rms_norm_heads(q, H, hd, gam), H, hd), max_abs=1e-2, rel_l2=1e-3,
+          what="f16 rms+rope")

@@ -184,7 +184,7 @@ def test_live_reference_block_and_flow():
     C, H, ctxc, mlp = 32, 2, 24, 64
     hp = O.FlowHParams(in_channels=8, out_channels=8, model_channels=C, cond_channels=ctxc, num_blocks=2,
                        num_heads=H, mlp_ratio=2.0)
-    from tests.test_oracle_pin import random_flow_weights
+    from tests._models import random_flow_weights
     w = random_flow_weights(rng, hp)
     x = rng.standard_normal((n, 8)).astype(np.float32)
     offs = np.array([0, 7, 12], np.int64)
@@ -229,45 +229,3 @@ def test_live_reference_ops():
     rc, rf, _ = reflib.downsample_mean(c, x, 2)
     np.testing.assert_array_equal(oc, rc)
     close(of, rf, SPARSE_TOL)
-
-
-def random_flow_weights(rng, hp: O.FlowHParams, scale: float = 1.0):
-    """Xavier-uniform random weights for a flow model (benchmark configs use
-    random init).  Biases ~ N(0, 0.02); gammas ~ 1 + N(0, 0.05); modulation
-    ~ N(0, 0.1)."""
-    from pixal3d.cpp_b200.workloads import xavier
-    C = hp.model_channels
-    mlp = int(C * hp.mlp_ratio)
-
-    def bias(k):
-        return (rng.standard_normal(k) * 0.02).astype(np.float32)
-
-    def gamma(k):
-        return (1.0 + rng.standard_normal(k) * 0.05).astype(np.float32)
-
-    w = {
-        "input_weight": xavier(rng, C, hp.in_channels), "input_bias": bias(C),
-        "timestep_weight0": xavier(rng, C, 256), "timestep_bias0": bias(C),
-        "timestep_weight2": xavier(rng, C, C), "timestep_bias2": bias(C),
-        "modulation_weight": xavier(rng, 6 * C, C), "modulation_bias": bias(6 * C),
-        "output_weight": xavier(rng, hp.out_channels, C), "output_bias": bias(hp.out_channels),
-        "blocks": [],
-    }
-    for _ in range(hp.num_blocks):
-        bw = {
-            "modulation": (rng.standard_normal(6 * C) * 0.1).astype(np.float32),
-            "self_to_qkv_weight": xavier(rng, 3 * C, C), "self_to_qkv_bias": bias(3 * C),
-            "self_q_gamma": gamma(C), "self_k_gamma": gamma(C),
-            "self_to_out_weight": xavier(rng, C, C), "self_to_out_bias": bias(C),
-            "norm2_weight": gamma(C), "norm2_bias": bias(C),
-            "cross_to_q_weight": xavier(rng, C, C), "cross_to_q_bias": bias(C),
-            "cross_to_kv_weight": xavier(rng, 2 * C, hp.cond_channels), "cross_to_kv_bias": bias(2 * C),
-            "cross_q_gamma": gamma(C), "cross_k_gamma": gamma(C),
-            "cross_to_out_weight": xavier(rng, C, C), "cross_to_out_bias": bias(C),
-            "proj_weight": xavier(rng, C, max(hp.proj_in_channels, 1)) if hp.proj_in_channels else None,
-            "proj_bias": bias(C) if hp.proj_in_channels else None,
-            "mlp0_weight": xavier(rng, mlp, C), "mlp0_bias": bias(mlp),
-            "mlp2_weight": xavier(rng, C, mlp), "mlp2_bias": bias(C),
-        }
-        w["blocks"].append(bw)
-    return w
