@@ -1,0 +1,533 @@
+#!/usr/bin/env python
+"""Benchmark: SLat flow sampler steps/s at N=21,766 active voxels on B200.
+
+Workload ("Full SLat-flow sampler"): the config-0
+64^3 sphere shell (21,766 voxels), input linear 8->1024, two SparseResBlock3d
+(3x3x3 sparse conv C=1024, GroupNorm32, SiLU) at 64^3, 2x downsample to 32^3
+(4,092 voxels), 24 transformer blocks (16 heads x 64, MLP x4, qk RMS norm,
+3D RoPE, AdaLN, cross-attention to 1029 x 1024 condition tokens), nearest 2x
+upsample, two SparseResBlock3d, output linear to 8.  One step = one CFG-2
+forward (conditional + zeros condition, batched) + the Euler/CFG update.
+Weights random-init (seeded), condition tokens and noise N(0,1) (seeded).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1: launched by torchrun, one rank per GPU; every rank samples its own
+image (weak scaling); NCCL broadcasts the condition tokens before timing and
+gathers the results after it.  Rank 0 prints ONE JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+TRAFFIC_FILE = REPO / "profiles" / "traffic.json"
+METRIC = "SLat flow steps/s @N=20k voxels (CFG batch 2, 24 blocks, C=1024)"
+
+# config-2 shapes
+RES, RADIUS, HALF_WIDTH = 64, 24.0, 1.5
+C, HEADS, BLOCKS, CTX_TOKENS, CH = 1024, 16, 24, 1029, 8
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--blocks", type=int, default=BLOCKS, help=argparse.SUPPRESS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    if PEAKS_FILE.exists():
+        p = json.loads(PEAKS_FILE.read_text())
+        return p, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- our arm
+
+def make_weights(torch, dev, seed: int):
+    """Random-init config-2 weights on the device (f32, seeded).
+    Linears xavier-uniform; convs N(0, 1/sqrt(27 C)); biases N(0, .02);
+    norms 1 + N(0, .05); block modulation N(0, .1)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def xav(o, i):
+        b = math.sqrt(6.0 / (o + i))
+        return torch.empty((o, i), device=dev).uniform_(-b, b, generator=g)
+
+    def nrm(*shape, std=1.0, mean=0.0):
+        return torch.randn(*shape, device=dev, generator=g) * std + mean
+
+    mlp = 4 * C
+    w = {"input_weight": xav(C, CH), "input_bias": nrm(C, std=0.02),
+         "timestep_weight0": xav(C, 256), "timestep_bias0": nrm(C, std=0.02),
+         "timestep_weight2": xav(C, C), "timestep_bias2": nrm(C, std=0.02),
+         "modulation_weight": xav(6 * C, C), "modulation_bias": nrm(6 * C, std=0.02),
+         "output_weight": xav(CH, C), "output_bias": nrm(CH, std=0.02), "blocks": []}
+    for _ in range(BLOCKS_RUN):
+        w["blocks"].append({
+            "modulation": nrm(6 * C, std=0.1), "self_to_qkv_weight": xav(3 * C, C),
+            "self_to_qkv_bias": nrm(3 * C, std=0.02), "self_q_gamma": nrm(C, std=0.05, mean=1.0),
+            "self_k_gamma": nrm(C, std=0.05, mean=1.0), "self_to_out_weight": xav(C, C),
+            "self_to_out_bias": nrm(C, std=0.02), "norm2_weight": nrm(C, std=0.05, mean=1.0),
+            "norm2_bias": nrm(C, std=0.02), "cross_to_q_weight": xav(C, C), "cross_to_q_bias": nrm(C, std=0.02),
+            "cross_to_kv_weight": xav(2 * C, C), "cross_to_kv_bias": nrm(2 * C, std=0.02),
+            "cross_q_gamma": nrm(C, std=0.05, mean=1.0), "cross_k_gamma": nrm(C, std=0.05, mean=1.0),
+            "cross_to_out_weight": xav(C, C), "cross_to_out_bias": nrm(C, std=0.02),
+            "mlp0_weight": xav(mlp, C), "mlp0_bias": nrm(mlp, std=0.02),
+            "mlp2_weight": xav(C, mlp), "mlp2_bias": nrm(C, std=0.02)})
+    std = 1.0 / math.sqrt(27 * C)
+
+    def res():
+        return {"gn1_w": nrm(C, std=0.05, mean=1.0), "gn1_b": nrm(C, std=0.02), "conv1_w": nrm(27, C, C, std=std),
+                "conv1_b": nrm(C, std=0.02), "gn2_w": nrm(C, std=0.05, mean=1.0), "gn2_b": nrm(C, std=0.02),
+                "conv2_w": nrm(27, C, C, std=std), "conv2_b": nrm(C, std=0.02)}
+
+    w["io_in"] = [res(), res()]
+    w["io_out"] = [res(), res()]
+    return w
+
+
+BLOCKS_RUN = BLOCKS
+
+
+def algorithmic_flops(n_img: int, n_trunk_img: int, pairs_img: int) -> dict:
+    """Useful FLOPs of one CFG-2 step (2 x one image's forward)."""
+    mlp = 4 * C
+    lin_trunk = 2 * n_trunk_img * C * (3 * C + C + C + C + mlp + mlp)  # qkv, out, cross q, cross out, mlp0, mlp2
+    kv = 2 * CTX_TOKENS * C * 2 * C
+    attn_self = 4 * n_trunk_img * n_trunk_img * C
+    attn_cross = 4 * n_trunk_img * CTX_TOKENS * C
+    convs = 8 * 2 * pairs_img * C * C
+    io_lin = 2 * n_img * (CH * C + C * CH)
+    per_img = BLOCKS_RUN * (lin_trunk + kv + attn_self + attn_cross) + convs + io_lin
+    return {"total": 2 * per_img, "conv": 2 * convs, "trunk_linear": 2 * BLOCKS_RUN * (lin_trunk + kv),
+            "attention": 2 * BLOCKS_RUN * (attn_self + attn_cross)}
+
+
+def time_conv_kernel(torch, ops, coords_dev, reps=10):
+    """Average device time of the dominant kernel (gather-GEMM sparse conv,
+    C=1024, the config-2 fine level, batch 2) measured with CUDA events on
+    the launching stream."""
+    n = coords_dev.shape[0]
+    nbr = ops.neighbor_map27(coords_dev)
+    pairs = int((nbr < n).sum().item())
+    x = torch.randn((n, C), device="cuda").to(torch.float16)
+    w = (torch.randn((27, C, C), device="cuda") / math.sqrt(27 * C)).to(torch.float16)
+    b = torch.zeros(C, device="cuda")
+    out = torch.empty((n, C), device="cuda")
+    for _ in range(2):
+        ops.subm_conv3d(x, nbr, w, b, out=out)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        ops.subm_conv3d(x, nbr, w, b, out=out)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * pairs * C * C
+    del x, w, out
+    return ms, flops, pairs
+
+
+def time_conv_cfg0(torch, ops, reps=50):
+    """Config 0: one 64->64 submanifold conv on the 21,766-voxel shell.
+    Algorithmic bytes = read x (N*64*2) + weights (27*64*64*2) + neighbour map
+    (27*N*4) + write out f32 (N*64*4)."""
+    from pixal3d.cpp_b200.workloads import shell_coords
+    c = torch.from_numpy(shell_coords()).cuda()
+    n = c.shape[0]
+    nbr = ops.neighbor_map27(c)
+    pairs = int((nbr < n).sum().item())
+    x = torch.randn((n, 64), device="cuda").to(torch.float16)
+    w = (torch.randn((27, 64, 64), device="cuda") / math.sqrt(27 * 64)).to(torch.float16)
+    b = torch.zeros(64, device="cuda")
+    out = torch.empty((n, 64), device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    times = []
+    for i in range(reps + 3):
+        flush.zero_()  # evict L2 (> 126 MB) between launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.subm_conv3d(x, nbr, w, b, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    bytes_ = n * 64 * 2 + 27 * 64 * 64 * 2 + 27 * n * 4 + n * 64 * 4
+    return ms, bytes_, 2.0 * pairs * 64 * 64
+
+
+def cpu_baseline_sample(target_seconds: float = 20.0):
+    """The reference's own CPU path (oracle/_ref, compiled from the reference
+    sources) on this host's cores, on a bounded sample of the config-2 step:
+      - sparse_transformer_cross_block_f32 at 256 voxels per item (batch 2,
+        C=1024, 1029 condition tokens): its non-attention part scales
+        linearly to the trunk size N=4,092;
+      - the reference's (serial) sparse_scaled_dot_product_attention timed
+        alone at 512 voxels per item, scaled by N^2 to N=4,092;
+      - sparse_submanifold_conv3d 1024->1024 on a sub-slab of the shell,
+        scaled by neighbour pairs to the full shell (8 convs x batch 2).
+    Returns (extrapolated seconds per step, details)."""
+    import numpy as np
+    from oracle import reflib, oracle as O
+    from pixal3d.cpp_b200.workloads import shell_coords, batched
+    threads = os.cpu_count() or 1
+    reflib.set_threads(threads)
+    rng = np.random.default_rng(0)
+    cfg = O.BlockConfig(channels=C, num_heads=HEADS, mlp_hidden=4 * C, context_channels=C)
+    sc = 0.02
+    w = {"modulation": rng.standard_normal(6 * C).astype(np.float32) * 0.1}
+    for f, shp in [("self_to_qkv_weight", (3 * C, C)), ("self_to_out_weight", (C, C)), ("cross_to_q_weight", (C, C)),
+                   ("cross_to_kv_weight", (2 * C, C)), ("cross_to_out_weight", (C, C)), ("mlp0_weight", (4 * C, C)),
+                   ("mlp2_weight", (C, 4 * C))]:
+        w[f] = (rng.standard_normal(shp) * sc).astype(np.float32)
+        w[f.replace("weight", "bias")] = np.zeros(shp[0], np.float32)
+    for f in ("self_q_gamma", "self_k_gamma", "norm2_weight", "cross_q_gamma", "cross_k_gamma"):
+        w[f] = np.ones(C, np.float32)
+    w["norm2_bias"] = np.zeros(C, np.float32)
+    ctx = rng.standard_normal((2 * CTX_TOKENS, C)).astype(np.float32)
+    offs = np.array([0, CTX_TOKENS, 2 * CTX_TOKENS], np.int64)
+    tmod = (rng.standard_normal((2, 6 * C)) * 0.1).astype(np.float32)
+    full = shell_coords()
+    # block at ns voxels per item: its non-attention part scales with N
+    ns, na = 256, 512
+    cc = batched(full[:ns], 2)
+    x = rng.standard_normal((cc.shape[0], C)).astype(np.float32)
+    t0 = time.perf_counter()
+    reflib.transformer_block(cc, x, tmod, offs, ctx, None, cfg, w, 2, (RES, RES, RES))
+    t_b = time.perf_counter() - t0
+    q = rng.standard_normal((cc.shape[0], C)).astype(np.float32)
+    t0 = time.perf_counter()
+    reflib.sdpa(cc, q, q, q, HEADS, C // HEADS, 0.125, 2, (RES, RES, RES))
+    t_a = time.perf_counter() - t0
+    # the reference's serial attention, timed alone at na voxels per item, scales with N^2
+    ca = batched(full[:na], 2)
+    qa = rng.standard_normal((ca.shape[0], C)).astype(np.float32)
+    t0 = time.perf_counter()
+    reflib.sdpa(ca, qa, qa, qa, HEADS, C // HEADS, 0.125, 2, (RES, RES, RES))
+    t_a_big = time.perf_counter() - t0
+    nt = 4092
+    t_block = (t_b - t_a) * nt / ns + t_a_big * (nt / na) ** 2
+    times = [t_b, t_a, t_a_big]
+    # conv: a slab of the shell (x < 22) at C=1024, scaled by pairs
+    slab = full[full[:, 1] < 14]
+    xs = rng.standard_normal((slab.shape[0], C)).astype(np.float32)
+    wc = (rng.standard_normal((27, C, C)) / math.sqrt(27 * C)).astype(np.float32)
+    t0 = time.perf_counter()
+    reflib.subm_conv3d(slab, xs, wc, np.zeros(C, np.float32), 1, (RES, RES, RES))
+    t_slab = time.perf_counter() - t0
+    pairs_slab = int((O.neighbor_map27(slab) < slab.shape[0]).sum())
+    pairs_full = int((O.neighbor_map27(full) < full.shape[0]).sum())
+    t_conv = t_slab * pairs_full / pairs_slab
+    step = BLOCKS_RUN * t_block + 8 * 2 * t_conv
+    return step, {"threads": threads, "block_at_256x2_s": round(t_b, 3), "sdpa_at_256x2_s": round(t_a, 3),
+                  "sdpa_at_512x2_s": round(t_a_big, 3),
+                  "t_block_N4092_s": round(t_block, 2), "t_conv_c1024_s": round(t_conv, 2),
+                  "sample_seconds": round(sum(times) + t_slab, 1)}
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    from pixal3d.cpp_b200 import ops
+    from pixal3d.cpp_b200.flow import FlowModel, HParams
+    from pixal3d.cpp_b200.workloads import shell_coords, batched
+
+    global BLOCKS_RUN
+    BLOCKS_RUN = args.blocks
+    dev = torch.device("cuda", local)
+    peaks, peak_kind = load_peaks()
+    img = shell_coords(RES, RADIUS, HALF_WIDTH)
+    n_img = img.shape[0]
+    coords = torch.from_numpy(batched(img, 2)).to(dev)
+
+    # condition tokens: rank 0 draws them, NCCL broadcasts to every rank
+    g = torch.Generator(device=dev)
+    g.manual_seed(2024)
+    cond = torch.randn((CTX_TOKENS, C), device=dev, generator=g)
+    if world > 1:
+        dist.broadcast(cond, src=0)
+    ctx2 = torch.cat([cond, torch.zeros_like(cond)]).to(torch.float16)
+
+    hp = HParams(in_channels=CH, out_channels=CH, model_channels=C, cond_channels=C, num_blocks=BLOCKS_RUN,
+                 num_heads=HEADS, mlp_ratio=4.0, io_resblocks=2, groups=32, operand_dtype="f16")
+    w = make_weights(torch, dev, seed=1234)
+    model = FlowModel(hp, w)
+    del w
+    torch.cuda.empty_cache()
+    model.prepare(coords, 2, (RES, RES, RES), [0, CTX_TOKENS, 2 * CTX_TOKENS])
+    gn = torch.Generator(device=dev)
+    gn.manual_seed(7 + rank)
+    x = torch.randn((n_img, CH), device=dev, generator=gn)
+
+    # warm-up (also captures the per-step CUDA graph)
+    model.sample(x, ctx2, steps=max(args.warmup, 1), guidance_strength=3.0)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.ctx(local).launches
+    e0.record(s)
+    model.sample(x, ctx2, steps=args.steps, guidance_strength=3.0)
+    e1.record(s)
+    torch.cuda.synchronize()
+    launches = ops.ctx(local).launches - launches0
+    ms_local = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([ms_local], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    # NCCL gather of the sampled latents to rank 0 (outside the timed region)
+    if world > 1:
+        gathered = [torch.empty_like(x) for _ in range(world)] if rank == 0 else None
+        dist.gather(x, gathered, dst=0)
+
+    value = world * args.steps / (ms_max / 1000.0)
+    ms_per_step = ms_max / args.steps
+
+    result = None
+    if rank == 0:
+        nbr_pairs = int((ops.neighbor_map27(torch.from_numpy(img).to(dev)) < n_img).sum().item())
+        fl = algorithmic_flops(n_img, 4092, nbr_pairs)
+        conv_ms, conv_flops, _ = time_conv_kernel(torch, ops, coords)
+        conv_tflops = conv_flops / (conv_ms / 1000.0) / 1e12
+        peak_t = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        traffic = None
+        if TRAFFIC_FILE.exists():
+            traffic = json.loads(TRAFFIC_FILE.read_text()).get("conv_c1024_batch2_bytes_per_launch")
+        c0_ms, c0_bytes, c0_flops = time_conv_cfg0(torch, ops)
+        hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        result = {
+            "metric": METRIC, "value": round(value, 3), "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate/residual",
+            "data": "synthetic: seeded sphere shell, N(0,1) noise and condition tokens, random-init weights",
+            "config": {"workload": "config2: full SLat-flow sampler step, CFG batch 2",
+                       "voxels_per_image": n_img, "trunk_voxels_per_image": 4092, "model_channels": C,
+                       "blocks": BLOCKS_RUN, "heads": HEADS, "condition_tokens": CTX_TOKENS,
+                       "io_resblocks": 2, "images_per_gpu": 1, "parallelism": f"dp{world} (images)",
+                       "l2": "per-step working set (1.26 GB of weights streamed per step) exceeds the 126 MB L2",
+                       "cuda_graph": "one captured step replayed per step"},
+            "step_tflop": round(fl["total"] / 1e12, 3),
+            "achieved_tflops": round(fl["total"] / (ms_per_step / 1000.0) / 1e12, 1),
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "roofline": {"kernel": "gather-GEMM sparse conv 1024->1024 (tcgen05), fine level batch 2",
+                         "bound": "tensor", "achieved": round(conv_tflops, 1), "peak": peak_t,
+                         "peak_kind": f"{peak_kind} bf16 burst (f16 dense rate is identical)",
+                         "unit": "TFLOP/s", "frac": round(conv_tflops / peak_t, 4), "traffic": traffic,
+                         "avg_launch_ms": round(conv_ms, 4), "flops_per_launch": conv_flops},
+            "sparse_conv_cfg0": {"ms": round(c0_ms, 4), "algorithmic_bytes": c0_bytes,
+                                 "achieved_gbs": round(c0_bytes / (c0_ms / 1000.0) / 1e9, 1), "peak_gbs": hbm,
+                                 "frac_hbm": round(c0_bytes / (c0_ms / 1000.0) / 1e9 / hbm, 4),
+                                 "tflops": round(c0_flops / (c0_ms / 1000.0) / 1e12, 2),
+                                 "l2": "flushed (256 MB write) before each launch"},
+        }
+    # e2e: the public sampler call with HOST buffers (pinned), copies inside
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(torch, model, img, cond, args, dev, world, rank)
+    if rank == 0:
+        result["e2e"] = e2e
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                step_s, det = cpu_baseline_sample()
+                result["cpu_baseline"] = {"value": round(1.0 / step_s, 8), "unit": "steps/s",
+                                          "cores": det["threads"], "kind": "reference",
+                                          "sample": ("reference sparse_transformer_cross_block_f32 at 256 voxels "
+                                                     "x batch 2 (non-attention part scaled by N) + reference "
+                                                     "attention at 512 x 2 (scaled by N^2) to N=4092 + "
+                                                     "sparse_submanifold_conv3d 1024->1024 on a shell slab scaled "
+                                                     "by neighbour pairs; extrapolated to one step"),
+                                          "details": det}
+            except Exception as ex:  # reported, not fatal
+                result["cpu_baseline"] = {"value": None, "unit": "steps/s", "error": str(ex)[:200]}
+        print(json.dumps(result), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(torch, model, img, cond, args, dev, world, rank):
+    """End to end through the public API: per call, H2D of coords, noise and
+    condition from pinned host memory, prepare (topology), sample K steps,
+    D2H of the result; device-timed, max over ranks."""
+    import torch.distributed as dist
+    n_img = img.shape[0]
+    from pixal3d.cpp_b200.workloads import batched
+    h_coords = torch.from_numpy(batched(img, 2)).pin_memory()
+    h_noise = torch.randn((n_img, CH)).pin_memory()
+    h_cond = torch.cat([cond.cpu(), torch.zeros_like(cond.cpu())]).pin_memory()
+    h_out = torch.empty((n_img, CH)).pin_memory()
+    steps = args.steps
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(s)
+    d_coords = h_coords.to(dev, non_blocking=True)
+    d_x = h_noise.to(dev, non_blocking=True)
+    d_ctx = h_cond.to(dev, non_blocking=True)
+    model.prepare(d_coords, 2, (RES, RES, RES), [0, CTX_TOKENS, 2 * CTX_TOKENS])
+    model.sample(d_x, d_ctx, steps=steps, guidance_strength=3.0)
+    h_out.copy_(d_x, non_blocking=True)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    h2d = h_coords.numel() * 4 + h_noise.numel() * 4 + h_cond.numel() * 4
+    return {"value": round(world * steps / (ms / 1000.0), 3), "unit": "steps/s",
+            "h2d_bytes_per_step": int(h2d / steps), "d2h_bytes_per_step": int(h_out.numel() * 4 / steps),
+            "ms_per_call": round(ms, 2), "steps_per_call": steps,
+            "includes": "H2D coords/noise/condition, topology prepare (neighbour map, downsample), graph "
+                        "re-capture, K sampler steps, D2H latents"}
+
+
+# --------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import reflib
+    if not reflib.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libp3dref.so not built (needs the "
+                          "reference sources at build time)"}))
+        return
+    samples = []
+    det = None
+    for i in range(args.warmup + args.steps):
+        step_s, det = cpu_baseline_sample()
+        if i >= args.warmup:
+            samples.append(step_s)
+    step = statistics.median(samples)
+    value = 1.0 / step
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 8), "unit": "steps/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step * 1000.0, 1),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (as ours)",
+           "config": {"workload": "config2: full SLat-flow sampler step, CFG batch 2",
+                      "method": "extrapolated from bounded samples of the reference CPU ops"},
+           "cpu_baseline": {"value": round(value, 8), "unit": "steps/s", "cores": det["threads"],
+                            "kind": "reference",
+                            "sample": "reference block at 256 voxels x2 (scaled by N) + reference attention "
+                                      "at 512 x2 (scaled by N^2) to N=4092 + conv slab scaled by neighbour pairs",
+                            "details": det},
+           "e2e": {"value": round(value, 8), "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

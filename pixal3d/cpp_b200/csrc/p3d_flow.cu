@@ -252,7 +252,9 @@ struct p3d_flow {
     p3d_ctx *ctx = nullptr;
     p3d_flow_hparams hp{};
     int C = 0, in_pad = 0, cond_pad = 0, proj_pad = 0;
-    std::vector<void *> allocs;
+    std::vector<void *> allocs;       // weights: freed with the flow
+    std::vector<void *> prep_allocs;  // topology + workspaces: freed on re-prepare
+    bool in_prepare = false;
     // weights
     uint16_t *input_w = nullptr, *output_w = nullptr;
     float *input_b = nullptr, *output_b = nullptr, *t_w0 = nullptr, *t_b0 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr,
@@ -274,9 +276,16 @@ struct p3d_flow {
     int dt = P3D_F16;
     double *stats = nullptr;
     int *counter = nullptr;
+    float *x_state = nullptr, *proj_model = nullptr;  // sampler-owned copies of x / proj
     cudaStream_t stream = nullptr;
     std::string error;
     int64_t launches_per_step = 0;
+    std::vector<int32_t> h_fine_off, h_ctx_off;  // host copies of the batch / condition offsets
+    // Cached CUDA graph of one sampler step; it reads only the buffers above,
+    // so it stays valid across sample() calls until prepare() rebinds them or
+    // a captured scalar (rescale, sigma_min) changes.
+    cudaGraphExec_t step_graph = nullptr;
+    float graph_gr = -1.0f, graph_sigma = -1.0f;
 
     template <typename T>
     int alloc(T **p, int64_t count) {
@@ -284,11 +293,12 @@ struct p3d_flow {
         if (count <= 0) count = 1;
         cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * count);
         if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
-        allocs.push_back(*p);
+        (in_prepare ? prep_allocs : allocs).push_back(*p);
         return P3D_OK;
     }
     void free_prepared();
     ~p3d_flow() {
+        free_prepared();
         for (void *p : allocs) cudaFree(p);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -296,7 +306,6 @@ struct p3d_flow {
 
 namespace {
 
-std::vector<void *> *g_prep_allocs = nullptr;
 
 int upload16(p3d_flow *f, const float *src, int64_t rows, int64_t cols, int64_t cols_pad, uint16_t **dst) {
     if (!src) return set_error(f->ctx, P3D_ERR_INVALID, "missing SLat flow weight");
@@ -445,7 +454,20 @@ struct StreamSwap {
 
 }  // namespace
 
-void p3d_flow::free_prepared() {}
+void p3d_flow::free_prepared() {
+    if (stream) cudaStreamSynchronize(stream);
+    if (step_graph) cudaGraphExecDestroy(step_graph);
+    step_graph = nullptr;
+    for (void *p : prep_allocs) cudaFree(p);
+    prep_allocs.clear();
+    prepared = false;
+    n = nt = T = max_fine = max_trunk = max_ctx = 0;
+    coords = trunk_coords = fine_off = trunk_off = ctx_off = nbr = parent = child = nullptr;
+    h = hf = ftmp = tfreq = temb = temb2 = tmod = mods = x_model = vel = sched = ts = x_state = proj_model = nullptr;
+    xn = qkv = attn = mlp = kv = cq = ctx_bf = proj_bf = x_in = fbf = nullptr;
+    stats = nullptr;
+    counter = nullptr;
+}
 
 extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out) {
     if (!ctx || !hp || !w || !out) return P3D_ERR_INVALID;
@@ -555,8 +577,15 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
                                 const int64_t *ctx_offsets_host) {
     if (!f) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
-    P3D_REQUIRE(ctx, !f->prepared, "p3d_flow_prepare: already prepared (create a new flow per coordinate set)");
     P3D_REQUIRE(ctx, coords && ctx_offsets_host && n > 0 && batch > 0, "p3d_flow_prepare: bad argument");
+    // Rebinding releases the previous coordinate set's topology, workspaces
+    // and cached step graph; weights stay resident.
+    f->free_prepared();
+    struct PrepScope {
+        p3d_flow *f;
+        explicit PrepScope(p3d_flow *ff) : f(ff) { f->in_prepare = true; }
+        ~PrepScope() { f->in_prepare = false; }
+    } prep_scope(f);
     const p3d_flow_hparams &hp = f->hp;
     const int C = f->C;
     f->batch = batch;
@@ -582,6 +611,8 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         f->max_ctx = std::max<int64_t>(f->max_ctx, coff[b + 1] - coff[b]);
     }
     f->T = coff[batch];
+    f->h_fine_off = off;
+    f->h_ctx_off = coff;
     P3D_TRY(f->alloc(&f->coords, n * 4));
     P3D_CUDA(ctx, cudaMemcpy(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice));
     P3D_TRY(f->alloc(&f->fine_off, batch + 1));
@@ -656,6 +687,9 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     P3D_TRY(f->alloc(&f->vel, n * hp.out_channels));
     P3D_TRY(f->alloc(&f->ts, batch));
     P3D_TRY(f->alloc(&f->counter, 1));
+    P3D_TRY(f->alloc(&f->sched, 4 * 4096));
+    P3D_TRY(f->alloc(&f->x_state, n * hp.in_channels));
+    if (hp.proj_mode) P3D_TRY(f->alloc(&f->proj_model, n * hp.proj_in_channels));
     f->prepared = true;
     return P3D_OK;
 }
@@ -689,17 +723,16 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
     if (!f || !cfg) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
     P3D_REQUIRE(ctx, f->prepared, "p3d_flow_sample: call p3d_flow_prepare first");
+    P3D_REQUIRE(ctx, x && ctx_feats, "p3d_flow_sample: null pointer");
     P3D_REQUIRE(ctx, f->batch % 2 == 0, "p3d_flow_sample: batch must be 2 x images (conditional, unconditional)");
     P3D_REQUIRE(ctx, f->hp.in_channels == f->hp.out_channels, "p3d_flow_sample: in/out channels differ");
     P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
-    P3D_REQUIRE(ctx, cfg->steps > 0 && cfg->sigma_min >= 0.0f && cfg->sigma_min < 1.0f && cfg->rescale_t > 0.0f &&
-                         cfg->guidance_rescale >= 0.0f && cfg->guidance_interval_min <= cfg->guidance_interval_max,
+    P3D_REQUIRE(ctx, cfg->steps > 0 && cfg->steps < 4096 && cfg->sigma_min >= 0.0f && cfg->sigma_min < 1.0f &&
+                         cfg->rescale_t > 0.0f && cfg->guidance_rescale >= 0.0f &&
+                         cfg->guidance_interval_min <= cfg->guidance_interval_max,
                 "invalid flow Euler sampler configuration");
     const int I = f->batch / 2;
-    // Both halves must hold the same rows in the same order.
-    std::vector<int32_t> off(f->batch + 1);
-    P3D_CUDA(ctx, cudaMemcpy(off.data(), f->fine_off, sizeof(int32_t) * (f->batch + 1), cudaMemcpyDeviceToHost));
-    const int64_t half = off[I];
+    const int64_t half = f->h_fine_off[I];
     P3D_REQUIRE(ctx, 2 * half == f->n, "p3d_flow_sample: unconditional half must mirror the conditional half");
     const int ch = f->hp.in_channels;
     // t schedule (src/flow_sampler.cpp:268-286), computed in f32 like the reference
@@ -712,89 +745,103 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
         const float nl = 1.0f - static_cast<float>(s + 1) / steps;
         const float nden = 1.0f + (cfg->rescale_t - 1.0f) * nl;
         const float tn = cfg->rescale_t * nl / nden;
-        if (!(den > 0.0f) || !(nden > 0.0f)) return set_error(ctx, P3D_ERR_INVALID, "flow Euler timestep schedule is not finite");
+        if (!(den > 0.0f) || !(nden > 0.0f))
+            return set_error(ctx, P3D_ERR_INVALID, "flow Euler timestep schedule is not finite");
         const bool in_interval = t >= cfg->guidance_interval_min && t <= cfg->guidance_interval_max;
         sched[4 * s] = t;
         sched[4 * s + 1] = tn;
         sched[4 * s + 2] = in_interval ? cfg->guidance_strength : 1.0f;
     }
-    if (!f->sched) P3D_TRY(f->alloc(&f->sched, 4 * 4096));
-    P3D_REQUIRE(ctx, cfg->steps < 4096, "p3d_flow_sample: too many steps");
     StreamSwap swap(ctx, f->stream);
-    // order after the caller's stream
     cudaEvent_t ev;
     P3D_CUDA(ctx, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-    cudaEventRecord(ev, swap.saved);
+    cudaEventRecord(ev, swap.saved);  // order after the caller's stream
     cudaStreamWaitEvent(f->stream, ev, 0);
-    P3D_CUDA(ctx, cudaMemcpyAsync(f->sched, sched.data(), sizeof(float) * sched.size(), cudaMemcpyHostToDevice, f->stream));
-    P3D_CUDA(ctx, cudaMemsetAsync(f->counter, 0, sizeof(int), f->stream));
-    // condition: conditional tokens for items [0, I), zeros for [I, 2I)
-    P3D_TRY(load_ctx(f, ctx_feats, ctx_dtype));
-    {
-        std::vector<int32_t> coff(f->batch + 1);
-        P3D_CUDA(ctx, cudaMemcpy(coff.data(), f->ctx_off, sizeof(int32_t) * (f->batch + 1), cudaMemcpyDeviceToHost));
-        const int64_t z0 = coff[I], z1 = coff[f->batch];
+    int rc = P3D_OK;
+    auto body = [&]() -> int {
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->sched, sched.data(), sizeof(float) * sched.size(), cudaMemcpyHostToDevice,
+                                      f->stream));
+        P3D_CUDA(ctx, cudaMemsetAsync(f->counter, 0, sizeof(int), f->stream));
+        // condition: conditional tokens for items [0, I), zeros for [I, 2I)
+        P3D_TRY(load_ctx(f, ctx_feats, ctx_dtype));
+        const int64_t z0 = f->h_ctx_off[I], z1 = f->h_ctx_off[f->batch];
         P3D_CUDA(ctx, cudaMemsetAsync(f->ctx_bf + z0 * f->cond_pad, 0, sizeof(uint16_t) * (z1 - z0) * f->cond_pad,
                                       f->stream));
-    }
-    const float *proj_model = nullptr;
-    float *proj_buf = nullptr;
-    if (f->hp.proj_mode) {
-        P3D_TRY(f->alloc(&proj_buf, f->n * f->hp.proj_in_channels));
-        const int64_t hp_rows = half * f->hp.proj_in_channels;
-        P3D_CUDA(ctx, cudaMemcpyAsync(proj_buf, proj, sizeof(float) * hp_rows, cudaMemcpyDeviceToDevice, f->stream));
-        zero_f32_rows_kernel<<<blocks_for(hp_rows, 256), 256, 0, f->stream>>>(proj_buf + hp_rows, hp_rows);
-        P3D_TRY(check_launch(ctx, "zero_rows"));
-        proj_model = proj_buf;
-    }
-    // model input = [x; x]
-    P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
-    P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model + half * ch, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice,
-                                  f->stream));
-    const bool rescale = cfg->guidance_rescale > 0.0f;
-    auto one_step = [&]() -> int {
-        P3D_TRY(forward_impl(f, f->x_model, f->sched, 0, f->counter, 1000.0f, proj_model, f->vel));
-        const float *vp = f->vel, *vn = f->vel + half * ch;
-        if (rescale) {
-            P3D_CUDA(ctx, cudaMemsetAsync(f->stats, 0, sizeof(double) * 4 * I, f->stream));
-            euler_sched_stats_kernel<<<blocks_for(half, 8), 256, 0, f->stream>>>(
-                x, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, cfg->sigma_min, f->stats);
-            P3D_TRY(check_launch(ctx, "euler_stats"));
+        if (f->hp.proj_mode) {
+            const int64_t hp_rows = half * f->hp.proj_in_channels;
+            P3D_CUDA(ctx, cudaMemcpyAsync(f->proj_model, proj, sizeof(float) * hp_rows, cudaMemcpyDeviceToDevice,
+                                          f->stream));
+            P3D_CUDA(ctx, cudaMemsetAsync(f->proj_model + hp_rows, 0, sizeof(float) * hp_rows, f->stream));
         }
-        euler_sched_kernel<<<blocks_for(half * ch, 256), 256, 0, f->stream>>>(
-            x, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, cfg->guidance_rescale, cfg->sigma_min,
-            rescale ? f->stats : nullptr, f->x_model);
-        P3D_TRY(check_launch(ctx, "euler_sched"));
-        advance_kernel<<<1, 1, 0, f->stream>>>(f->counter);
-        return check_launch(ctx, "advance");
+        // sampler state and model input [x; x]
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->x_state, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model + half * ch, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice,
+                                      f->stream));
+        const bool rescale = cfg->guidance_rescale > 0.0f;
+        const float gr = cfg->guidance_rescale, sigma = cfg->sigma_min;
+        auto one_step = [&]() -> int {
+            P3D_TRY(forward_impl(f, f->x_model, f->sched, 0, f->counter, 1000.0f, f->proj_model, f->vel));
+            const float *vp = f->vel, *vn = f->vel + half * ch;
+            if (rescale) {
+                P3D_CUDA(ctx, cudaMemsetAsync(f->stats, 0, sizeof(double) * 4 * I, f->stream));
+                euler_sched_stats_kernel<<<blocks_for(half, 8), 256, 0, f->stream>>>(
+                    f->x_state, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, sigma, f->stats);
+                P3D_TRY(check_launch(ctx, "euler_stats"));
+            }
+            euler_sched_kernel<<<blocks_for(half * ch, 256), 256, 0, f->stream>>>(
+                f->x_state, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, gr, sigma,
+                rescale ? f->stats : nullptr, f->x_model);
+            P3D_TRY(check_launch(ctx, "euler_sched"));
+            advance_kernel<<<1, 1, 0, f->stream>>>(f->counter);
+            return check_launch(ctx, "advance");
+        };
+        int first = 0;
+        if (cfg->use_graph && f->step_graph && (f->graph_gr != gr || f->graph_sigma != sigma)) {
+            cudaGraphExecDestroy(f->step_graph);
+            f->step_graph = nullptr;
+        }
+        if (cfg->use_graph && !f->step_graph) {
+            // One eager step (first launches of every kernel happen outside
+            // capture), then capture one step for replay.
+            const int64_t l0 = ctx->launches;
+            P3D_TRY(one_step());
+            f->launches_per_step = ctx->launches - l0;
+            first = 1;
+            if (cfg->steps > 1) {
+                cudaGraph_t graph = nullptr;
+                P3D_CUDA(ctx, cudaStreamBeginCapture(f->stream, cudaStreamCaptureModeThreadLocal));
+                const int rc_cap = one_step();
+                const cudaError_t e = cudaStreamEndCapture(f->stream, &graph);
+                if (rc_cap) {
+                    if (graph) cudaGraphDestroy(graph);
+                    return rc_cap;
+                }
+                if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+                const cudaError_t ie = cudaGraphInstantiate(&f->step_graph, graph, 0);
+                cudaGraphDestroy(graph);
+                if (ie != cudaSuccess) {
+                    f->step_graph = nullptr;
+                    return set_error(ctx, P3D_ERR_CUDA, "cudaGraphInstantiate failed");
+                }
+                f->graph_gr = gr;
+                f->graph_sigma = sigma;
+            }
+        }
+        for (int s = first; s < cfg->steps; ++s) {
+            if (cfg->use_graph && f->step_graph) {
+                P3D_CUDA(ctx, cudaGraphLaunch(f->step_graph, f->stream));
+                ctx->launches += f->launches_per_step;
+            } else {
+                const int64_t l0 = ctx->launches;
+                P3D_TRY(one_step());
+                f->launches_per_step = ctx->launches - l0;
+            }
+        }
+        P3D_CUDA(ctx, cudaMemcpyAsync(x, f->x_state, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
+        return P3D_OK;
     };
-    const int64_t l0 = ctx->launches;
-    int rc = one_step();
-    f->launches_per_step = ctx->launches - l0;
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    if (!rc && cfg->steps > 1 && cfg->use_graph) {
-        if (cudaStreamBeginCapture(f->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-            rc = set_error(ctx, P3D_ERR_CUDA, "cudaStreamBeginCapture failed");
-        if (!rc) {
-            const int rc_cap = one_step();
-            const cudaError_t e = cudaStreamEndCapture(f->stream, &graph);
-            if (rc_cap) rc = rc_cap;
-            else if (e != cudaSuccess) rc = set_error(ctx, P3D_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
-        }
-        if (!rc && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
-            rc = set_error(ctx, P3D_ERR_CUDA, "cudaGraphInstantiate failed");
-    }
-    for (int s = 1; s < cfg->steps && !rc; ++s) {
-        if (exec) {
-            if (cudaGraphLaunch(exec, f->stream) != cudaSuccess) rc = set_error(ctx, P3D_ERR_CUDA, "cudaGraphLaunch failed");
-            ++ctx->launches;
-        } else {
-            rc = one_step();
-        }
-    }
-    if (exec) cudaGraphExecDestroy(exec);
-    if (graph) cudaGraphDestroy(graph);
+    rc = body();
     cudaEventRecord(ev, f->stream);
     cudaStreamWaitEvent(swap.saved, ev, 0);
     cudaEventDestroy(ev);
