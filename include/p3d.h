@@ -204,8 +204,9 @@ int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads,
 int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out);
 
 /* GroupNorm over the points of each batch item (no reference; benchmark
- * config 2 SparseResBlock3d), then optional SiLU; f32 in, bf16 out.
- * stats: caller scratch of nbatch*groups*2 doubles. */
+ * config 2 SparseResBlock3d), then optional SiLU; f32 in, f32/bf16/f16 out.
+ * channels/groups must be a multiple of 4; x/out 16-byte aligned.
+ * stats: caller scratch of nbatch*groups*3 doubles. */
 int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int channels, int groups, float eps,
                         const float *gamma, const float *beta, const int32_t *batch_offsets, int nbatch,
                         int silu, double *stats, void *out, int out_dtype);

@@ -126,70 +126,92 @@ __global__ void activation_kernel(const T *__restrict__ x, int64_t n, int act, T
 }
 
 // ------------------------------------------------------------- GroupNorm
-// Stats: block (b, g, slice) accumulates sum / sum of squares of its rows
-// of batch b over the channels of group g, in double, then one atomicAdd.
-__global__ void groupnorm_stats_kernel(const float *__restrict__ x, int C, int groups, const int32_t *__restrict__ offsets,
-                                       int slices, double *__restrict__ stats) {
-    const int bg = blockIdx.x;
-    const int b = bg / groups, g = bg % groups;
-    const int gs = C / groups;
-    const int64_t r0 = offsets[b], r1 = offsets[b + 1];
-    const int64_t rows = r1 - r0;
-    const int64_t per = (rows + slices - 1) / slices;
-    const int64_t s0 = r0 + per * blockIdx.y;
-    const int64_t s1 = min(r1, s0 + per);
-    double sum = 0.0, sq = 0.0;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int64_t r = s0 + warp; r < s1; r += nw) {
-        const float *xr = x + r * C + g * gs;
-        for (int c = lane; c < gs; c += 32) {
-            const double v = xr[c];
-            sum += v;
-            sq += v * v;
+// Stats: each block walks a contiguous row range with one float4 per thread
+// per row step (C/4 threads span a row, coalesced), accumulating sum and
+// sum of squares of its group in double; the group's threads reduce by
+// shuffles and one lane per group issues an atomicAdd whenever the batch item
+// changes or the range ends.  Requires C % 4 == 0 and (C/groups) % 4 == 0.
+__global__ void groupnorm_stats_kernel(const float *__restrict__ x, int64_t n, int C, int groups,
+                                       const int32_t *__restrict__ offsets, int nbatch, int rows_per_block,
+                                       double *__restrict__ stats) {
+    const int c4 = C / 4;
+    const int tpr = blockDim.x < c4 ? blockDim.x : c4;  // threads per row
+    const int rows_step = blockDim.x / tpr;
+    const int t = threadIdx.x;
+    const int col4 = t % tpr, rsub = t / tpr;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+    const int64_t r1 = min(n, r0 + rows_per_block);
+    const int gs4 = (C / groups) / 4;  // float4 per group
+    for (int cb = col4; cb < c4; cb += tpr) {
+        const int g = cb / gs4;
+        double sum = 0.0, sq = 0.0;
+        int cur_b = -1;
+        for (int64_t r = r0 + rsub; r < r1; r += rows_step) {
+            const int b = batch_of_row(offsets, nbatch, r);
+            if (b != cur_b) {
+                if (cur_b >= 0 && (sum != 0.0 || sq != 0.0)) {
+                    atomicAdd(stats + 2 * (cur_b * groups + g), sum);
+                    atomicAdd(stats + 2 * (cur_b * groups + g) + 1, sq);
+                }
+                sum = sq = 0.0;
+                cur_b = b;
+            }
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + r * C) + cb);
+            sum += static_cast<double>(v.x) + v.y + v.z + v.w;
+            sq += static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
+                  static_cast<double>(v.w) * v.w;
         }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    }
-    __shared__ double red[2][32];
-    if (lane == 0) {
-        red[0][warp] = sum;
-        red[1][warp] = sq;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double a = 0.0, q = 0.0;
-        for (int w = 0; w < nw; ++w) {
-            a += red[0][w];
-            q += red[1][w];
+        if (cur_b >= 0) {
+            atomicAdd(stats + 2 * (cur_b * groups + g), sum);
+            atomicAdd(stats + 2 * (cur_b * groups + g) + 1, sq);
         }
-        atomicAdd(stats + 2 * bg, a);
-        atomicAdd(stats + 2 * bg + 1, q);
     }
 }
 
-template <typename TO>
-__global__ void groupnorm_apply_kernel(const float *__restrict__ x, int64_t n, int C, int groups, float eps,
-                                       const float *__restrict__ gamma, const float *__restrict__ beta,
-                                       const int32_t *__restrict__ offsets, int nbatch, const double *__restrict__ stats,
-                                       int silu, TO *__restrict__ out) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= n) return;
-    const int lane = threadIdx.x & 31;
-    const int b = batch_of_row(offsets, nbatch, row);
+// mean / rstd per (batch, group) from the double sums.
+__global__ void groupnorm_finalize_kernel(const double *__restrict__ stats, const int32_t *__restrict__ offsets,
+                                          int nbatch, int groups, int C, float eps, float *__restrict__ mr) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nbatch * groups) return;
+    const int b = i / groups;
     const double cnt = static_cast<double>(offsets[b + 1] - offsets[b]) * (C / groups);
-    const int gs = C / groups;
-    for (int c = lane; c < C; c += 32) {
-        const int g = c / gs;
-        const double mean = stats[2 * (b * groups + g)] / cnt;
-        const double var = fmax(stats[2 * (b * groups + g) + 1] / cnt - mean * mean, 0.0);
-        const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
-        float v = (x[row * C + c] - static_cast<float>(mean)) * rstd;
-        if (gamma) v = v * gamma[c] + beta[c];
-        if (silu) v = silu_f(v);
-        store_val(out + row * C + c, v);
+    const double mean = cnt > 0 ? stats[2 * i] / cnt : 0.0;
+    const double var = cnt > 0 ? fmax(stats[2 * i + 1] / cnt - mean * mean, 0.0) : 0.0;
+    mr[2 * i] = static_cast<float>(mean);
+    mr[2 * i + 1] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+}
+
+// y = silu((x - mean) * rstd * gamma + beta): one float4 per thread.
+template <typename TO>
+__global__ void groupnorm_apply_kernel(const float *__restrict__ x, int64_t n, int C, int groups,
+                                       const float *__restrict__ gamma, const float *__restrict__ beta,
+                                       const int32_t *__restrict__ offsets, int nbatch, const float *__restrict__ mr,
+                                       int silu, TO *__restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int c4 = C / 4;
+    if (i >= n * c4) return;
+    const int64_t row = i / c4;
+    const int cb = static_cast<int>(i - row * c4);
+    const int b = batch_of_row(offsets, nbatch, row);
+    const int g = (cb * 4) / (C / groups);
+    const float mean = mr[2 * (b * groups + g)], rstd = mr[2 * (b * groups + g) + 1];
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    float y[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int c = cb * 4 + e;
+        float t = (y[e] - mean) * rstd;
+        if (gamma) t = t * __ldg(gamma + c) + __ldg(beta + c);
+        y[e] = silu ? silu_f(t) : t;
+    }
+    TO *o = out + i * 4;
+    if constexpr (sizeof(TO) == 2) {
+        uint2 pk;
+        pk.x = pack2<TO>(y[0], y[1]);
+        pk.y = pack2<TO>(y[2], y[3]);
+        *reinterpret_cast<uint2 *>(o) = pk;
+    } else {
+        *reinterpret_cast<float4 *>(o) = make_float4(y[0], y[1], y[2], y[3]);
     }
 }
 
@@ -322,17 +344,26 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
                                    int silu, double *stats, void *out, int out_dtype) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && out && stats && batch_offsets && nbatch > 0, "p3d_group_norm_silu: null pointer");
-    P3D_REQUIRE(ctx, groups > 0 && channels % groups == 0, "p3d_group_norm_silu: channels % groups != 0");
+    P3D_REQUIRE(ctx, groups > 0 && channels % groups == 0 && (channels / groups) % 4 == 0,
+                "p3d_group_norm_silu: channels/groups must be a multiple of 4");
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                "p3d_group_norm_silu: x/out must be 16-byte aligned");
+    // stats scratch: [nbatch*groups*2] double sums, then [nbatch*groups*2] float mean/rstd
     P3D_CUDA(ctx, cudaMemsetAsync(stats, 0, sizeof(double) * 2 * nbatch * groups, ctx->stream));
     if (n == 0) return P3D_OK;
-    dim3 sgrid(nbatch * groups, 16);
-    groupnorm_stats_kernel<<<sgrid, 256, 0, ctx->stream>>>(x, channels, groups, batch_offsets, 16, stats);
+    const int rows_per_block = 64;
+    groupnorm_stats_kernel<<<blocks_for(n, rows_per_block), 256, 0, ctx->stream>>>(
+        x, n, channels, groups, batch_offsets, nbatch, rows_per_block, stats);
     int rc = check_launch(ctx, "groupnorm_stats");
     if (rc) return rc;
+    float *mr = reinterpret_cast<float *>(stats + 2 * nbatch * groups);
+    groupnorm_finalize_kernel<<<blocks_for(nbatch * groups, 128), 128, 0, ctx->stream>>>(
+        stats, batch_offsets, nbatch, groups, channels, eps, mr);
+    if ((rc = check_launch(ctx, "groupnorm_finalize"))) return rc;
+    const int64_t count4 = n * (channels / 4);
     P3D_DISPATCH(out_dtype, TO,
-                 groupnorm_apply_kernel<TO><<<blocks_for(n, 8), 256, 0, ctx->stream>>>(
-                     x, n, channels, groups, eps, gamma, beta, batch_offsets, nbatch, stats, silu,
-                     static_cast<TO *>(out)));
+                 groupnorm_apply_kernel<TO><<<blocks_for(count4, 256), 256, 0, ctx->stream>>>(
+                     x, n, channels, groups, gamma, beta, batch_offsets, nbatch, mr, silu, static_cast<TO *>(out)));
     return check_launch(ctx, "groupnorm_apply");
 }
 

@@ -659,7 +659,7 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         P3D_TRY(f->alloc(&f->hf, n * C));
         P3D_TRY(f->alloc(&f->ftmp, n * C));
         P3D_TRY(f->alloc(&f->fbf, n * C));
-        P3D_TRY(f->alloc(&f->stats, 2 * batch * hp.groups + 4 * batch));
+        P3D_TRY(f->alloc(&f->stats, 3 * batch * hp.groups + 4 * batch));
     } else {
         f->nt = n;
         f->trunk_coords = f->coords;

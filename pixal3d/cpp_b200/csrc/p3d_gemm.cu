@@ -96,16 +96,23 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int64_t row, in
             g = p.gate + static_cast<int64_t>(b) * p.gate_ld + col0;
         }
         if (ncols == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+            // All 8 residual (and gate) loads are issued before any store so
+            // they overlap: one DRAM round trip per chunk, not eight.
+            float4 cur[8], gg[8];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-                float4 cur = *reinterpret_cast<float4 *>(o + i);
-                float4 gg = g ? *reinterpret_cast<const float4 *>(g + i) : make_float4(1.f, 1.f, 1.f, 1.f);
-                cur.x += gg.x * v[i];
-                cur.y += gg.y * v[i + 1];
-                cur.z += gg.z * v[i + 2];
-                cur.w += gg.w * v[i + 3];
-                *reinterpret_cast<float4 *>(o + i) = cur;
+            for (int i = 0; i < 8; ++i) cur[i] = __ldcg(reinterpret_cast<const float4 *>(o) + i);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                gg[i] = g ? __ldg(reinterpret_cast<const float4 *>(g) + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                cur[i].x += gg[i].x * v[4 * i];
+                cur[i].y += gg[i].y * v[4 * i + 1];
+                cur[i].z += gg[i].z * v[4 * i + 2];
+                cur[i].w += gg[i].w * v[4 * i + 3];
             }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) reinterpret_cast<float4 *>(o)[i] = cur[i];
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)

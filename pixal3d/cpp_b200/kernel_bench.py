@@ -1,0 +1,99 @@
+"""Micro-benchmarks of single kernels of the SLat path (device time, CUDA events).
+
+    python -m pixal3d.cpp_b200.kernel_bench --kernel conv1024 [--reps 10]
+
+Kernels (config-2 shapes unless noted):
+  conv1024   gather-GEMM sparse conv 1024->1024 on the 64^3 shell, batch 2
+  conv64     config-0 conv 64->64 on the shell (21,766 voxels)
+  qkv        trunk qkv linear, 8,184 x 1024 -> 3072
+  mlp0       trunk MLP up-projection with GELU, 8,184 x 1024 -> 4096
+  attn       trunk self-attention, 2 sequences x 4,092, 16 heads x 64
+  cross      trunk cross-attention, 2 x 4,092 queries x 1,029 keys
+Each run is small enough for an ncu capture (a few hundred MB on the
+device) while its inputs exceed the 126 MB L2.  Prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import ops
+from . import _lib as L
+from .workloads import shell_coords, batched
+
+C = 1024
+
+
+def _time(fn, reps):
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run(kernel: str, reps: int) -> dict:
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    h = torch.float16
+    if kernel in ("conv1024", "conv64"):
+        cc = shell_coords()
+        ch = 1024 if kernel == "conv1024" else 64
+        coords = torch.from_numpy(batched(cc, 2) if ch == 1024 else cc).to(dev)
+        n = coords.shape[0]
+        nbr = ops.neighbor_map27(coords)
+        pairs = int((nbr < n).sum().item())
+        x = torch.randn((n, ch), device=dev, generator=g).to(h)
+        w = (torch.randn((27, ch, ch), device=dev, generator=g) / math.sqrt(27 * ch)).to(h)
+        b = torch.zeros(ch, device=dev)
+        out = torch.empty((n, ch), device=dev)
+        ms = _time(lambda: ops.subm_conv3d(x, nbr, w, b, out=out), reps)
+        flops = 2.0 * pairs * ch * ch
+        bytes_ = n * ch * 2 + 27 * ch * ch * 2 + 27 * n * 4 + n * ch * 4
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6,
+                "flops": flops, "bytes": bytes_, "rows": n, "pairs": pairs}
+    if kernel in ("qkv", "mlp0"):
+        m = 2 * 4092
+        nout = 3 * C if kernel == "qkv" else 4 * C
+        x = torch.randn((m, C), device=dev, generator=g).to(h)
+        w = (torch.randn((nout, C), device=dev, generator=g) / 32).to(h)
+        b = torch.zeros(nout, device=dev)
+        out = torch.empty((m, nout), device=dev, dtype=h)
+        epi = L.EPI_GELU_TANH if kernel == "mlp0" else L.EPI_NONE
+        ms = _time(lambda: ops.linear(x, w, b, out=out, epilogue=epi), reps)
+        flops = 2.0 * m * C * nout
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "m": m, "n": nout, "k": C}
+    if kernel in ("attn", "cross"):
+        nq = 4092
+        nk = nq if kernel == "attn" else 1029
+        q = torch.randn((2 * nq, C), device=dev, generator=g).to(h)
+        k = torch.randn((2 * nk, C), device=dev, generator=g).to(h)
+        v = torch.randn((2 * nk, C), device=dev, generator=g).to(h)
+        cq = torch.tensor([0, nq, 2 * nq], dtype=torch.int32, device=dev)
+        ck = torch.tensor([0, nk, 2 * nk], dtype=torch.int32, device=dev)
+        out = torch.empty((2 * nq, C), device=dev, dtype=h)
+        ms = _time(lambda: ops.varlen_attention(q, k, v, cq, ck, nq, 16, 0.125, out=out), reps)
+        flops = 2 * 4.0 * nq * nk * C
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
+    raise SystemExit(f"unknown kernel {kernel}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", required=True)
+    ap.add_argument("--reps", type=int, default=10)
+    a = ap.parse_args()
+    print(json.dumps(run(a.kernel, a.reps)))
+
+
+if __name__ == "__main__":
+    main()

@@ -248,7 +248,7 @@ def group_norm_silu(x: torch.Tensor, groups: int, eps: float, gamma, beta, batch
     c = ctx(x.device)
     n, ch = x.shape
     nb = batch_offsets.shape[0] - 1
-    stats = torch.empty(2 * nb * groups, dtype=torch.float64, device=x.device)
+    stats = torch.empty(3 * nb * groups, dtype=torch.float64, device=x.device)
     out = torch.empty((n, ch), dtype=out_dtype, device=x.device)
     c.check(L.lib.p3d_group_norm_silu(c.h, _p(x), n, ch, groups, eps, _p(gamma), _p(beta), _p(batch_offsets), nb,
                                       int(silu), _p(stats), _p(out), _dt(out)))

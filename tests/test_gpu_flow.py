@@ -139,3 +139,36 @@ def test_flow_forward_bf16_operands():
     got = model.forward(torch.from_numpy(x).cuda(), torch.from_numpy(ts).cuda(), torch.from_numpy(ctx).cuda())
     check(got.cpu().numpy(), exp, "flow forward [bf16 operands]", max_abs=6e-2, rel_l2=1e-2)
     model.close()
+
+
+def test_flow_sample_cached_graph_and_reprepare():
+    """A second sample() replays the cached step graph bit for bit; prepare()
+    on a new coordinate set rebuilds topology and workspaces, and the result
+    still matches the oracle."""
+    hp = O.FlowHParams(in_channels=8, out_channels=8, model_channels=128, cond_channels=64, num_blocks=2,
+                       num_heads=2)
+    w, model = make(hp, seed=9)
+    rng = np.random.default_rng(10)
+    ctx = rng.standard_normal((21, 64)).astype(np.float32)
+    ctx2 = torch.from_numpy(np.concatenate([ctx, ctx])).cuda()
+    results = []
+    for c0 in (shell_coords(16, 5.5, 1.0), shell_coords(20, 7.0, 1.1)):
+        model.prepare(torch.from_numpy(batched(c0, 2)).cuda(), 2, (20, 20, 20), np.array([0, 21, 42]))
+        noise = rng.standard_normal((c0.shape[0], 8)).astype(np.float32)
+        outs = []
+        for _ in range(2):
+            xt = torch.from_numpy(noise.copy()).cuda()
+            model.sample(xt, ctx2, steps=3, guidance_strength=3.0, use_graph=True)
+            outs.append(xt.cpu().numpy())
+        np.testing.assert_array_equal(outs[0], outs[1])
+        sc = O.SamplerConfig(steps=3, guidance_strength=3.0)
+        zctx = np.zeros_like(ctx)
+
+        def ref_model(state, t, cond):
+            return O.slat_flow_forward(c0, state, np.array([t], np.float32), np.array([0, 21]), ctx if cond else zctx,
+                                       None, hp, w)
+
+        exp = O.flow_euler_sample(noise, sc, ref_model, c0[:, 0].astype(np.int64), 1)
+        check(outs[0], exp, f"re-prepared sample n={c0.shape[0]}")
+        results.append(outs[0])
+    model.close()
