@@ -170,15 +170,17 @@ int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const i
                     int out_dtype, int epilogue, const float *gate, int64_t gate_ld,
                     const int32_t *batch_offsets, int nbatch);
 
-/* Varlen flash attention, head_dim 64, 16-bit in/out (dtype), f32 softmax/accum.
+/* Varlen flash attention on tcgen05 tensor cores, head_dim 64, 16-bit in/out
+ * (dtype), f32 softmax/accumulation.  rows_q / rows_k: total rows of the q and
+ * k/v views (cu_q[nseq], cu_k[nseq]); q/k/v/out rows 16-byte aligned.
  * Sequence s covers q rows [cu_q[s], cu_q[s+1]) and k/v rows
  * [cu_k[s], cu_k[s+1]).  Replaces sparse_scaled_dot_product_attention
  * (src/sparse.cpp:704-783), sparse_cross_attention (:785-859) and the
  * chunked ggml sdpa of src/slat_flow.cpp:947-1001. */
 int p3d_varlen_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k, int64_t ldk,
                          const void *v, int64_t ldv, void *out, int64_t ldo, const int32_t *cu_q,
-                         const int32_t *cu_k, int nseq, int64_t max_q, int heads, int head_dim,
-                         float scale, int dtype);
+                         const int32_t *cu_k, int nseq, int64_t max_q, int64_t rows_q, int64_t rows_k,
+                         int heads, int head_dim, float scale, int dtype);
 
 /* ------------------------------------------------------ fused elementwise */
 

@@ -143,6 +143,17 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
 }
+// TMA row gather: 4 rows (row0..row3) x box-width columns starting at column
+// c0, box one row high, written as 4 consecutive box rows at smem_dst.  A row
+// index outside the tensor reads the fill value (zero).  No multicast.
+__device__ __forceinline__ void tma_gather4(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int r0,
+                                            int r1, int r2, int r3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+        : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -216,12 +227,27 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory descriptor for an MN-major operand in 128-byte-swizzled
+// atoms: 64 16-bit elements of the MN dimension per 128-byte row, K rows at
+// a 128-byte pitch, 8-row groups SBO = 1024 bytes apart.  Used for V in
+// O = P V (V stored [key][dim], dims contiguous).  LBO (stride between
+// 64-element MN groups) is set to lbo_bytes.
+__device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B of the
 // same 16-bit type (format 0 = f16, 1 = bf16 at bits 7-9 and 10-12), both
 // K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
-__host__ __device__ constexpr uint32_t idesc_f32acc(int m, int n, bool bf16) {
-    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-           (static_cast<uint32_t>(m >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f32acc(int m, int n, bool bf16, bool b_mn_major = false) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---- 16-bit element helpers (bf16 / f16)

@@ -393,7 +393,7 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
                                         rope_coords, hp.rope_freq_min, hp.rope_freq_base, dt));
         }
         P3D_TRY(p3d_varlen_attention(ctx, f->qkv, 3 * C, f->qkv + C, 3 * C, f->qkv + 2 * C, 3 * C, f->attn, C,
-                                     f->trunk_off, f->trunk_off, B, f->max_trunk, H, C / H, attn_scale, dt));
+                                     f->trunk_off, f->trunk_off, B, f->max_trunk, nt, nt, H, C / H, attn_scale, dt));
         P3D_TRY(p3d_linear(ctx, f->attn, C, bw.out_w, dt, bw.out_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL,
                            f->mods + 2 * C, 6 * C, f->trunk_off, B));
         // cross-attention branch (:237-275)
@@ -408,7 +408,7 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         if (hp.qk_rms_norm_cross)
             P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->kv, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f, dt));
         P3D_TRY(p3d_varlen_attention(ctx, f->cq, C, f->kv, 2 * C, f->kv + C, 2 * C, f->attn, C, f->trunk_off,
-                                     f->ctx_off, B, f->max_trunk, H, C / H, attn_scale, dt));
+                                     f->ctx_off, B, f->max_trunk, nt, f->T, H, C / H, attn_scale, dt));
         P3D_TRY(p3d_linear(ctx, f->attn, C, bw.co_w, dt, bw.co_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL, nullptr, 0,
                            nullptr, 0));
         if (hp.proj_mode && proj)

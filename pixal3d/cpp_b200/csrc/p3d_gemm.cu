@@ -57,13 +57,18 @@ struct GemmParams {
     int *fault;
 };
 
-template <int BN>
+// MT = 128-row M sub-tiles per CTA tile; they share every B stage, which
+// halves the B operand stream per FLOP when MT = 2.
+template <int BN, int MT>
 struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int A_BYTES = MT * BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr int ACC_COLS = MT * BN;                 // one accumulator buffer
+    static constexpr int ACC_BUFS = 2 * ACC_COLS <= 512 ? 2 : 1;
+    static constexpr int TMEM_COLS = ACC_BUFS * ACC_COLS <= 128 ? 128 : (ACC_BUFS * ACC_COLS <= 256 ? 256 : 512);
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <typename T>
@@ -137,11 +142,12 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int64_t row, in
     }
 }
 
-template <int BN, bool GATHER>
+template <int BN, bool GATHER, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const GemmParams p) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, MT>;
+    constexpr int BMT = BM * MT;  // rows per CTA tile
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const int64_t m_tiles = (p.M + BM - 1) / BM;
+    const int64_t m_tiles = (p.M + BMT - 1) / BMT;
     const int64_t n_tiles = (p.N + BN - 1) / BN;
     const int64_t num_tiles = m_tiles * n_tiles;
     const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
@@ -194,10 +200,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int64_t m0 = (tile / n_tiles) * BM;
+            const int64_t m0 = (tile / n_tiles) * BMT;
             const int64_t n0 = (tile % n_tiles) * BN;
             for (int kb = 0; kb < num_kb; ++kb) {
-                if (GATHER || t == 0) {
+                if (GATHER) {
+                    // warp-uniform bounded wait (lane 0 polls, the warp follows)
+                    int w_ok = 1;
+                    if ((t & 31) == 0) w_ok = mbar_wait(&empty_bar[stage], phase ^ 1, p.fault) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+                        ok = false;
+                        break;
+                    }
+                } else if (t == 0) {
                     if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.fault)) {
                         ok = false;
                         break;
@@ -208,18 +222,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (GATHER) {
                     const int tap = kb / kblocks_per_tap;
                     const int kc = (kb % kblocks_per_tap) * BK;
-                    const int64_t row = m0 + t;
-                    int32_t src = -1;
-                    if (row < p.M) {
-                        src = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
-                        if (src >= p.M || src < 0) src = -1;  // sentinel
-                    }
-                    const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc : 0);
-                    const uint32_t bytes = src >= 0 ? 16u : 0u;
-                    uint8_t *dst_row = sa + t * 128;
+                    // Warp w owns tile rows [w*32*MT, (w+1)*32*MT).  Per 32-row
+                    // slice, lane l fetches the source row of slice row l;
+                    // each cp.async instruction then copies 4 whole rows, 8
+                    // lanes per 128-byte row: coalesced global reads and
+                    // conflict-free swizzled shared-memory writes.
+                    const int lane_ = t & 31;
+                    const int chunk = lane_ & 7;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        cp_async16(dst_row + ((j ^ (t & 7)) << 4), g + j * 8, bytes);
+                    for (int sl = 0; sl < MT; ++sl) {
+                        const int wrow0 = ((t >> 5) * MT + sl) * 32;
+                        const int64_t row = m0 + wrow0 + lane_;
+                        int32_t my_src = -1;
+                        if (row < p.M) {
+                            my_src = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
+                            if (my_src >= p.M || my_src < 0) my_src = -1;  // sentinel -> zero row
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = wrow0 + i * 4 + (lane_ >> 3);
+                            const int32_t src = __shfl_sync(0xffffffffu, my_src, i * 4 + (lane_ >> 3));
+                            const uint16_t *g =
+                                p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
+                            cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
+                        }
                     }
                     if (t == 0) {
                         mbar_arrive_expect_tx(&full_bar[stage], C::B_BYTES);
@@ -229,7 +255,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     cp_async_mbar_arrive_noinc(&full_bar[stage]);
                 } else if (t == 0) {
                     mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
-                    tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, static_cast<int>(m0));
+#pragma unroll
+                    for (int sl = 0; sl < MT; ++sl)
+                        tma_load_2d(sa + sl * (BM * 128), &tmap_a, &full_bar[stage], kb * BK,
+                                    static_cast<int>(m0 + sl * BM));
                     tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, static_cast<int>(n0));
                 }
                 if (++stage == STAGES) {
@@ -254,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&full_bar[stage], phase, p.fault)) {
                         ok = false;
@@ -266,8 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
-                        umma_f16(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                                 (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                        for (int sl = 0; sl < MT; ++sl)
+                            umma_f16(d_tmem + sl * BN, sw128_desc(a_addr + sl * (BM * 128) + kk * 32),
+                                     sw128_desc(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                     issued = true;
                     umma_commit(&empty_bar[stage]);
@@ -278,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 umma_commit(&tfull_bar[acc]);
-                if (++acc == 2) {
+                if (++acc == C::ACC_BUFS) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
@@ -296,15 +327,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int64_t m0 = (tile / n_tiles) * BM;
+            const int64_t m0 = (tile / n_tiles) * BMT;
             const int64_t n0 = (tile % n_tiles) * BN;
             if (!mbar_wait(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            const int64_t row = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int cs = 0; cs < MT * BN; cs += 32) {
+                const int sl = cs / BN, c0 = cs % BN;
+                const int64_t row = m0 + sl * BM + q * 32 + lane;
                 float v[32];
-                tmem_ld32(tmem_base + acc * BN + c0 + (static_cast<uint32_t>(q * 32) << 16), v);
+                tmem_ld32(tmem_base + acc * C::ACC_COLS + cs + (static_cast<uint32_t>(q * 32) << 16), v);
                 tmem_ld_wait();
                 const int64_t col0 = n0 + c0;
                 if (col0 < p.N && row < p.M) {
@@ -327,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-            if (++acc == 2) {
+            if (++acc == C::ACC_BUFS) {
                 acc = 0;
                 acc_phase ^= 1;
             }
@@ -358,18 +390,18 @@ EncodeFn get_encode_fn() {
     return fn;
 }
 
-template <int BN, bool GATHER>
+template <int BN, bool GATHER, int MT>
 int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, MT>;
     static bool attr_set = false;
     if (!attr_set) {
-        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm_tc_kernel<BN, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           C::SMEM));
+        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm_tc_kernel<BN, GATHER, MT>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set = true;
     }
-    const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
+    const int64_t tiles = ceil_div(p.M, BM * MT) * ceil_div(p.N, BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
-    gemm_tc_kernel<BN, GATHER><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    gemm_tc_kernel<BN, GATHER, MT><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
@@ -384,13 +416,18 @@ int run_gemm(p3d_ctx *ctx, const CUtensorMap *ta, const CUtensorMap &tb, const G
     CUtensorMap dummy = tb;
     const CUtensorMap &a = ta ? *ta : dummy;
     if (gather) {
-        if (bn == 64) return launch_gemm<64, true>(ctx, a, tb, p);
-        if (bn == 128) return launch_gemm<128, true>(ctx, a, tb, p);
-        return launch_gemm<256, true>(ctx, a, tb, p);
+        // Long K loops (27 taps x Cin/64): two 128-row sub-tiles per CTA share
+        // every B stage once there are enough 256-row tiles to fill the GPU.
+        // Measured on B200: MT = 2 (3 stages) is slower than MT = 1 (4 stages) for
+        // the config-2 conv (3.13 vs 2.55 ms), so the gather path uses MT = 1.
+        const bool mt2 = false;
+        if (bn == 64) return mt2 ? launch_gemm<64, true, 2>(ctx, a, tb, p) : launch_gemm<64, true, 1>(ctx, a, tb, p);
+        if (bn == 128) return mt2 ? launch_gemm<128, true, 2>(ctx, a, tb, p) : launch_gemm<128, true, 1>(ctx, a, tb, p);
+        return mt2 ? launch_gemm<256, true, 2>(ctx, a, tb, p) : launch_gemm<256, true, 1>(ctx, a, tb, p);
     }
-    if (bn == 64) return launch_gemm<64, false>(ctx, a, tb, p);
-    if (bn == 128) return launch_gemm<128, false>(ctx, a, tb, p);
-    return launch_gemm<256, false>(ctx, a, tb, p);
+    if (bn == 64) return launch_gemm<64, false, 1>(ctx, a, tb, p);
+    if (bn == 128) return launch_gemm<128, false, 1>(ctx, a, tb, p);
+    return launch_gemm<256, false, 1>(ctx, a, tb, p);
 }
 
 }  // namespace

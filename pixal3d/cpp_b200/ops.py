@@ -205,7 +205,8 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: to
     if out is None:
         out = torch.empty((q.shape[0], heads * 64), dtype=q.dtype, device=q.device)
     c.check(L.lib.p3d_varlen_attention(c.h, _p(q), _rows(q), _p(k), _rows(k), _p(v), _rows(v), _p(out), _rows(out),
-                                       _p(cu_q), _p(cu_k), cu_q.shape[0] - 1, max_q, heads, 64, scale, _dt(q)))
+                                       _p(cu_q), _p(cu_k), cu_q.shape[0] - 1, max_q, q.shape[0], k.shape[0], heads,
+                                       64, scale, _dt(q)))
     return out
 
 
