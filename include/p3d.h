@@ -159,6 +159,20 @@ int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_d
                int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue,
                const float *gate, int64_t gate_ld, const int32_t *batch_offsets, int nbatch);
 
+/* p3d_linear with the per-head query/key normalisation of the attention
+ * blocks fused into its epilogue (head_dim 64): after the bias, columns
+ * [0, norm_cols) are RMS-normalised per 64-column head with gamma[col]
+ * (sparse_multihead_rms_norm, src/sparse.cpp:919-954), and columns
+ * [0, rope_cols) are rotated by the interleaved 3D RoPE with
+ * rope_table[row][32] = (cos, sin) from p3d_rope_table
+ * (sparse_rotary_position_embedding, src/sparse.cpp:861-917).  Normalises
+ * the f32 accumulators before rounding to out_dtype.  n, norm_cols and
+ * rope_cols must be multiples of 64. */
+int p3d_linear_headnorm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype,
+                        const float *bias, int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
+                        int out_dtype, int64_t norm_cols, const float *gamma, int64_t rope_cols,
+                        const float *rope_table);
+
 /* Submanifold 3x3x3 sparse conv as one gather-GEMM on tcgen05 tiles:
  * out[p] = epilogue(bias + sum_k W[k] x[nbr[k][p]]).  Replaces
  * sparse_submanifold_conv3d (src/sparse.cpp:999-1055) and the ggml
@@ -200,6 +214,11 @@ int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, int channels
 int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads, int head_dim,
                         const float *gamma, const int32_t *coords, float freq_min, float freq_base,
                         int dtype);
+/* Per-point RoPE cos/sin table for p3d_linear_headnorm
+ * (src/sparse.cpp:881-906): table[i][p] = (cos, sin) of pair p of point i,
+ * head_dim/2 pairs; pairs past 3*floor(head_dim/6) get (1, 0). */
+int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, int head_dim, float freq_min,
+                   float freq_base, float *table);
 
 /* out = act(x) elementwise (gelu_tanh_in_place src/sparse_transformer.cpp:123-134;
  * silu src/slat_decoder.cpp:68-78).  dtype applies to x and out. */

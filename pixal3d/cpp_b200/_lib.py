@@ -117,6 +117,8 @@ _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp
      i32)
 _sig("p3d_layernorm_modulate", i32, vp, vp, i64, i32, f32, vp, vp, vp, i64, vp, i32, vp, i32)
 _sig("p3d_qk_rmsnorm_rope", i32, vp, vp, i64, i64, i32, i32, vp, vp, f32, f32, i32)
+_sig("p3d_linear_headnorm", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i64, vp, i64, vp)
+_sig("p3d_rope_table", i32, vp, vp, i64, i32, f32, f32, vp)
 _sig("p3d_activation", i32, vp, vp, i64, i32, i32, vp)
 _sig("p3d_group_norm_silu", i32, vp, vp, i64, i32, i32, f32, vp, vp, vp, i32, i32, vp, vp, i32)
 _sig("p3d_euler_cfg_step", i32, vp, vp, vp, vp, i64, i32, vp, i32, f32, f32, f32, f32, f32, vp)

@@ -66,6 +66,72 @@ __global__ void layernorm_mod_kernel(const float *__restrict__ x, int64_t n, int
     }
 }
 
+// Register-resident variant for C = 128*NV: each lane holds its NV float4
+// slices of the row, so x is read from HBM once; the same two-pass
+// statistics, vectorised 16-byte parameter loads and 8/16-byte stores.
+template <typename TO>
+__device__ __forceinline__ void store4(TO *p, float a, float b, float c, float d) {
+    if constexpr (sizeof(TO) == 4) {
+        *reinterpret_cast<float4 *>(p) = make_float4(a, b, c, d);
+    } else {
+        *reinterpret_cast<uint2 *>(p) = make_uint2(pack2<TO>(a, b), pack2<TO>(c, d));
+    }
+}
+
+template <typename TO, int NV>
+__global__ void __launch_bounds__(256) layernorm_reg_kernel(const float *__restrict__ x, int64_t n, float eps,
+                                                            const float *__restrict__ gamma,
+                                                            const float *__restrict__ beta,
+                                                            const float *__restrict__ mod, int64_t mod_ld,
+                                                            const int32_t *__restrict__ offsets, int nbatch,
+                                                            TO *__restrict__ out) {
+    constexpr int C = 128 * NV;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + row * C);
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + i * 32 + lane);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) / static_cast<float>(C);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        v[i].x -= mean;
+        v[i].y -= mean;
+        v[i].z -= mean;
+        v[i].w -= mean;
+        ss += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(C) + eps);
+    const float4 *shift = nullptr, *scale = nullptr;
+    if (mod) {
+        const int b = batch_of_row(offsets, nbatch, row);
+        shift = reinterpret_cast<const float4 *>(mod + static_cast<int64_t>(b) * mod_ld);
+        scale = shift + C / 4;
+    }
+    TO *o = out + row * C;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c4 = i * 32 + lane;
+        float4 y = make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+        if (gamma) {
+            const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + c4);
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(beta) + c4);
+            y = make_float4(y.x * g.x + bb.x, y.y * g.y + bb.y, y.z * g.z + bb.z, y.w * g.w + bb.w);
+        }
+        if (mod) {
+            const float4 sc = __ldg(scale + c4), sh = __ldg(shift + c4);
+            y = make_float4(y.x * (1.0f + sc.x) + sh.x, y.y * (1.0f + sc.y) + sh.y, y.z * (1.0f + sc.z) + sh.z,
+                            y.w * (1.0f + sc.w) + sh.w);
+        }
+        store4(o + 4 * c4, y.x, y.y, y.z, y.w);
+    }
+}
+
 // ------------------------------------------------ per-head RMS + 3D RoPE
 // One warp per row; lane p owns rotation pair p (elements 2p, 2p+1) of
 // every head.  head_dim <= 64.
@@ -114,6 +180,26 @@ __global__ void qk_rms_rope_kernel(T *__restrict__ x, int64_t n, int64_t ld, int
             *pp = pack2<T>(re, ro);
         }
     }
+}
+
+// One thread per (point, pair): the cos/sin that qk_rms_rope_kernel computes
+// on the fly, stored once per coordinate set.
+__global__ void rope_table_kernel(const int4 *__restrict__ coords, int64_t n, int pairs, float fmin, float fbase,
+                                  float2 *__restrict__ table) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * pairs) return;
+    const int64_t row = i / pairs;
+    const int pr = static_cast<int>(i - row * pairs);
+    const int fd = pairs / 3;
+    float cs = 1.0f, sn = 0.0f;
+    if (pr < 3 * fd) {
+        const int4 c = coords[row];
+        const int axis = pr / fd;
+        const int coord = axis == 0 ? c.y : (axis == 1 ? c.z : c.w);
+        const float freq = fmin / powf(fbase, static_cast<float>(pr % fd) / static_cast<float>(fd));
+        sincosf(static_cast<float>(coord) * freq, &sn, &cs);
+    }
+    table[i] = make_float2(cs, sn);
 }
 
 // ------------------------------------------------------------ activations
@@ -296,6 +382,25 @@ extern "C" int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, i
     if (n == 0) return P3D_OK;
     const bool vec = channels % 128 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const unsigned grid = blocks_for(n, 8);
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const int nv = channels / 128;
+    const bool reg = vec && al16(out) && al16(gamma) && al16(beta) && al16(mod) && mod_ld % 4 == 0 &&
+                     (nv == 1 || nv == 2 || nv == 3 || nv == 4 || nv == 6 || nv == 8 || nv == 12 || nv == 16);
+    if (reg) {
+#define P3D_LN_REG(NVV)                                                                                         \
+    case NVV:                                                                                                  \
+        layernorm_reg_kernel<TO, NVV><<<grid, 256, 0, ctx->stream>>>(x, n, eps, gamma, beta, mod, mod_ld,      \
+                                                                      batch_offsets, nbatch, static_cast<TO *>(out)); \
+        break;
+        P3D_DISPATCH(out_dtype, TO, {
+            switch (nv) {
+                P3D_LN_REG(1) P3D_LN_REG(2) P3D_LN_REG(3) P3D_LN_REG(4) P3D_LN_REG(6) P3D_LN_REG(8) P3D_LN_REG(12)
+                P3D_LN_REG(16)
+            }
+        });
+#undef P3D_LN_REG
+        return check_launch(ctx, "layernorm_mod");
+    }
     P3D_DISPATCH(out_dtype, TO, {
         if (vec)
             layernorm_mod_kernel<TO, true><<<grid, 256, 0, ctx->stream>>>(
@@ -327,6 +432,17 @@ extern "C" int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld,
             static_cast<__half *>(x), n, ld, heads, head_dim, gamma, reinterpret_cast<const int4 *>(coords), freq_min,
             freq_base);
     return check_launch(ctx, "qk_rms_rope");
+}
+
+extern "C" int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, int head_dim, float freq_min,
+                              float freq_base, float *table) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, coords && table && head_dim >= 2 && head_dim % 2 == 0 && n >= 0, "p3d_rope_table: bad argument");
+    if (n == 0) return P3D_OK;
+    const int pairs = head_dim / 2;
+    rope_table_kernel<<<blocks_for(n * pairs, 256), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const int4 *>(coords), n, pairs, freq_min, freq_base, reinterpret_cast<float2 *>(table));
+    return check_launch(ctx, "rope_table");
 }
 
 extern "C" int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out) {

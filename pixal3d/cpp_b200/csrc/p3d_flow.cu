@@ -15,7 +15,7 @@
 //   - the sampler keeps its t schedule and a step counter on the device, so
 //     one step (forward + update) is captured once as a CUDA graph and
 //     replayed for every remaining step.
-// Residual stream h is f32; GEMM inputs bf16; accumulation f32.
+// Residual stream h is f32; GEMM operands f16 (or bf16); accumulation f32.
 #include <cmath>
 #include <vector>
 
@@ -275,6 +275,7 @@ struct p3d_flow {
              *ctx_bf = nullptr, *proj_bf = nullptr, *x_in = nullptr, *fbf = nullptr;
     int dt = P3D_F16;
     double *stats = nullptr;
+    float *rope = nullptr;  // [nt][32] (cos, sin) of the trunk coordinates, head_dim 64 only
     int *counter = nullptr;
     float *x_state = nullptr, *proj_model = nullptr;  // sampler-owned copies of x / proj
     cudaStream_t stream = nullptr;
@@ -371,7 +372,8 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
                                                                         nt, C);
         P3D_TRY(check_launch(ctx, "ape_add"));
     }
-    const float attn_scale = 1.0f / sqrtf(static_cast<float>(C / H));
+    const int hd = C / H;
+    const float attn_scale = 1.0f / sqrtf(static_cast<float>(hd));
     const int mlp = hp.mlp_hidden;
     if (hp.proj_mode && proj) {
         P3D_TRY(pad16(ctx, proj, nt, hp.proj_in_channels, f->proj_pad, f->proj_bf, dt));
@@ -383,10 +385,17 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         // self-attention branch (src/sparse_transformer.cpp:194-235)
         P3D_TRY(p3d_layernorm_modulate(ctx, f->h, nt, C, hp.norm_eps, nullptr, nullptr, f->mods, 6 * C, f->trunk_off,
                                        B, f->xn, dt));
-        P3D_TRY(p3d_linear(ctx, f->xn, C, bw.qkv_w, dt, bw.qkv_b, nt, 3 * C, C, f->qkv, 3 * C, dt, P3D_EPI_NONE,
-                           nullptr, 0, nullptr, 0));
         const int32_t *rope_coords = hp.pe_mode == 0 ? f->trunk_coords : nullptr;
-        if (hp.qk_rms_norm || rope_coords) {
+        const bool fuse_heads = hd == 64;
+        if (fuse_heads && (hp.qk_rms_norm || rope_coords)) {
+            // q/k RMS norm and RoPE in the GEMM epilogue, from the f32 accumulators
+            P3D_TRY(p3d_linear_headnorm(ctx, f->xn, C, bw.qkv_w, dt, bw.qkv_b, nt, 3 * C, C, f->qkv, 3 * C, dt,
+                                        hp.qk_rms_norm ? 2 * C : 0, bw.q_gamma, rope_coords ? 2 * C : 0, f->rope));
+        } else {
+            P3D_TRY(p3d_linear(ctx, f->xn, C, bw.qkv_w, dt, bw.qkv_b, nt, 3 * C, C, f->qkv, 3 * C, dt, P3D_EPI_NONE,
+                               nullptr, 0, nullptr, 0));
+        }
+        if (!fuse_heads && (hp.qk_rms_norm || rope_coords)) {
             P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->qkv, nt, 3 * C, H, C / H, hp.qk_rms_norm ? bw.q_gamma : nullptr,
                                         rope_coords, hp.rope_freq_min, hp.rope_freq_base, dt));
             P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->qkv + C, nt, 3 * C, H, C / H, hp.qk_rms_norm ? bw.k_gamma : nullptr,
@@ -399,14 +408,22 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         // cross-attention branch (:237-275)
         P3D_TRY(p3d_layernorm_modulate(ctx, f->h, nt, C, hp.norm_eps, bw.norm2_w, bw.norm2_b, nullptr, 0, nullptr, 0,
                                        f->xn, dt));
-        P3D_TRY(p3d_linear(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, P3D_EPI_NONE, nullptr, 0,
-                           nullptr, 0));
-        if (hp.qk_rms_norm_cross)
-            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->cq, nt, C, H, C / H, bw.cq_gamma, nullptr, 1.0f, 10000.0f, dt));
-        P3D_TRY(p3d_linear(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad, f->kv, 2 * C,
-                           dt, P3D_EPI_NONE, nullptr, 0, nullptr, 0));
-        if (hp.qk_rms_norm_cross)
-            P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->kv, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f, dt));
+        if (fuse_heads && hp.qk_rms_norm_cross) {
+            P3D_TRY(p3d_linear_headnorm(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, C, bw.cq_gamma, 0,
+                                        nullptr));
+            P3D_TRY(p3d_linear_headnorm(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad,
+                                        f->kv, 2 * C, dt, C, bw.ck_gamma, 0, nullptr));
+        } else {
+            P3D_TRY(p3d_linear(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, P3D_EPI_NONE, nullptr, 0,
+                               nullptr, 0));
+            if (hp.qk_rms_norm_cross)
+                P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->cq, nt, C, H, C / H, bw.cq_gamma, nullptr, 1.0f, 10000.0f, dt));
+            P3D_TRY(p3d_linear(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad, f->kv,
+                               2 * C, dt, P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            if (hp.qk_rms_norm_cross)
+                P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->kv, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f,
+                                            dt));
+        }
         P3D_TRY(p3d_varlen_attention(ctx, f->cq, C, f->kv, 2 * C, f->kv + C, 2 * C, f->attn, C, f->trunk_off,
                                      f->ctx_off, B, f->max_trunk, nt, f->T, H, C / H, attn_scale, dt));
         P3D_TRY(p3d_linear(ctx, f->attn, C, bw.co_w, dt, bw.co_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL, nullptr, 0,
@@ -514,8 +531,17 @@ extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p
         if ((rc = copy_f32(f, s.modulation, 6 * C, &d.modulation))) return fail(rc);
         if ((rc = upload16(f, s.qkv_w, 3 * C, C, C, &d.qkv_w))) return fail(rc);
         if ((rc = copy_f32(f, s.qkv_b, 3 * C, &d.qkv_b))) return fail(rc);
-        if ((rc = copy_f32(f, s.q_gamma, C, &d.q_gamma, hp->qk_rms_norm != 0))) return fail(rc);
-        if ((rc = copy_f32(f, s.k_gamma, C, &d.k_gamma, hp->qk_rms_norm != 0))) return fail(rc);
+        if (hp->qk_rms_norm) {
+            // q and k gammas side by side: one [2C] vector for the fused qkv epilogue
+            if (!s.q_gamma || !s.k_gamma) return fail(set_error(ctx, P3D_ERR_INVALID, "missing SLat flow tensor"));
+            if ((rc = f->alloc(&d.q_gamma, 2 * C))) return fail(rc);
+            d.k_gamma = d.q_gamma + C;
+            if (cudaMemcpyAsync(d.q_gamma, s.q_gamma, sizeof(float) * C, cudaMemcpyDeviceToDevice, ctx->stream) !=
+                    cudaSuccess ||
+                cudaMemcpyAsync(d.k_gamma, s.k_gamma, sizeof(float) * C, cudaMemcpyDeviceToDevice, ctx->stream) !=
+                    cudaSuccess)
+                return fail(set_error(ctx, P3D_ERR_CUDA, "p3d_flow_create: gamma copy failed"));
+        }
         if ((rc = upload16(f, s.out_w, C, C, C, &d.out_w))) return fail(rc);
         if ((rc = copy_f32(f, s.out_b, C, &d.out_b))) return fail(rc);
         if ((rc = copy_f32(f, s.norm2_w, C, &d.norm2_w))) return fail(rc);
@@ -690,6 +716,10 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     P3D_TRY(f->alloc(&f->sched, 4 * 4096));
     P3D_TRY(f->alloc(&f->x_state, n * hp.in_channels));
     if (hp.proj_mode) P3D_TRY(f->alloc(&f->proj_model, n * hp.proj_in_channels));
+    if (hp.pe_mode == 0 && C / hp.num_heads == 64) {
+        P3D_TRY(f->alloc(&f->rope, nt * 64));
+        P3D_TRY(p3d_rope_table(ctx, f->trunk_coords, nt, 64, hp.rope_freq_min, hp.rope_freq_base, f->rope));
+    }
     f->prepared = true;
     return P3D_OK;
 }

@@ -55,6 +55,12 @@ struct GemmParams {
     uint32_t idesc;   // tcgen05 instruction descriptor (operand type, M, N)
     int epi;
     int *fault;
+    // Per-head RMS norm + RoPE epilogue (head_dim 64): columns [0, norm_cols)
+    // are normalised per 64-column head with gamma[col]; columns
+    // [0, rope_cols) are then rotated with rope[row][pair] = (cos, sin).
+    int64_t norm_cols, rope_cols;
+    const float *norm_gamma;
+    const float2 *rope;
 };
 
 // MT = 128-row M sub-tiles per CTA tile; they share every B stage, which
@@ -331,6 +337,62 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n0 = (tile % n_tiles) * BN;
             if (!mbar_wait(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
+            if (p.norm_cols > 0 || p.rope_cols > 0) {
+                // 64-column groups = one head: bias, per-head RMS norm with gamma,
+                // interleaved RoPE from the per-row cos/sin table, then store.
+#pragma unroll 1
+                for (int cs = 0; cs < MT * BN; cs += 64) {
+                    const int sl = cs / BN, c0 = cs % BN;
+                    const int64_t row = m0 + sl * BM + q * 32 + lane;
+                    float v[64];
+                    {
+                        float a[32], b[32];
+                        const uint32_t ta = tmem_base + acc * C::ACC_COLS + cs + (static_cast<uint32_t>(q * 32) << 16);
+                        tmem_ld32(ta, a);
+                        tmem_ld32(ta + 32, b);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            v[i] = a[i];
+                            v[32 + i] = b[i];
+                        }
+                    }
+                    const int64_t col0 = n0 + c0;
+                    if (col0 < p.N && row < p.M) {
+                        if (p.bias) {
+#pragma unroll
+                            for (int i = 0; i < 64; ++i) v[i] += __ldg(p.bias + col0 + i);
+                        }
+                        if (col0 < p.norm_cols) {
+                            float ss = 0.0f;
+#pragma unroll
+                            for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
+                            const float inv = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) / max(||v||, eps)
+#pragma unroll
+                            for (int i = 0; i < 64; ++i) v[i] = v[i] * inv * __ldg(p.norm_gamma + col0 + i);
+                        }
+                        if (col0 < p.rope_cols) {
+                            const float2 *cs2 = p.rope + row * 32;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                const float2 r = __ldg(cs2 + i);
+                                const float e = v[2 * i], o = v[2 * i + 1];
+                                v[2 * i] = e * r.x - o * r.y;
+                                v[2 * i + 1] = e * r.y + o * r.x;
+                            }
+                        }
+                        float lo[32], hi[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            lo[i] = v[i];
+                            hi[i] = v[32 + i];
+                        }
+                        store_chunk(p, row, col0, lo, 32);
+                        store_chunk(p, row, col0 + 32, hi, 32);
+                    }
+                    __syncwarp();
+                }
+            } else {
 #pragma unroll 1
             for (int cs = 0; cs < MT * BN; cs += 32) {
                 const int sl = cs / BN, c0 = cs % BN;
@@ -355,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     store_chunk(p, row, col0, v, ncols);
                 }
                 __syncwarp();  // reconverge before the next tcgen05.ld (.sync.aligned)
+            }
             }
             tc_fence_before();
             __syncwarp();
@@ -455,9 +518,41 @@ int make_tmap_16bit_2d(p3d_ctx *ctx, CUtensorMap *map, const void *base, int dty
 
 using namespace p3d;
 
-extern "C" int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, const float *bias, int64_t m,
-                          int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue,
+namespace {
+int linear_impl(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, const float *bias, int64_t m,
+                int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue, const float *gate,
+                int64_t gate_ld, const int32_t *batch_offsets, int nbatch, int64_t norm_cols, const float *norm_gamma,
+                int64_t rope_cols, const float *rope);
+}
+
+extern "C" int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, const float *bias,
+                          int64_t m, int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue,
                           const float *gate, int64_t gate_ld, const int32_t *batch_offsets, int nbatch) {
+    return linear_impl(ctx, x, ldx, w, ab_dtype, bias, m, n, k, out, ldo, out_dtype, epilogue, gate, gate_ld,
+                       batch_offsets, nbatch, 0, nullptr, 0, nullptr);
+}
+
+extern "C" int p3d_linear_headnorm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype,
+                                   const float *bias, int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
+                                   int out_dtype, int64_t norm_cols, const float *gamma, int64_t rope_cols,
+                                   const float *rope_table) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, norm_cols >= 0 && norm_cols % 64 == 0 && norm_cols <= n && rope_cols >= 0 && rope_cols % 64 == 0 &&
+                         rope_cols <= n,
+                "p3d_linear_headnorm: norm/rope column counts must be multiples of the 64-wide head");
+    P3D_REQUIRE(ctx, norm_cols == 0 || gamma, "p3d_linear_headnorm: gamma required");
+    P3D_REQUIRE(ctx, rope_cols == 0 || rope_table, "p3d_linear_headnorm: rope table required");
+    P3D_REQUIRE(ctx, n % 64 == 0, "p3d_linear_headnorm: n must be a multiple of 64");
+    P3D_REQUIRE(ctx, norm_cols > 0 || rope_cols > 0, "p3d_linear_headnorm: nothing to fuse (use p3d_linear)");
+    return linear_impl(ctx, x, ldx, w, ab_dtype, bias, m, n, k, out, ldo, out_dtype, P3D_EPI_NONE, nullptr, 0,
+                       nullptr, 0, norm_cols, gamma, rope_cols, rope_table);
+}
+
+namespace {
+int linear_impl(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, const float *bias, int64_t m,
+                int64_t n, int64_t k, void *out, int64_t ldo, int out_dtype, int epilogue, const float *gate,
+                int64_t gate_ld, const int32_t *batch_offsets, int nbatch, int64_t norm_cols, const float *norm_gamma,
+                int64_t rope_cols, const float *rope) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && w && out, "p3d_linear: null pointer");
     P3D_REQUIRE(ctx, m >= 0 && n > 0 && k > 0, "p3d_linear: bad shape");
@@ -491,8 +586,13 @@ extern "C" int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *
     p.idesc = idesc_f32acc(BM, bn, ab_dtype == P3D_BF16);
     p.epi = epilogue;
     p.fault = ctx->fault;
+    p.norm_cols = norm_cols;
+    p.norm_gamma = norm_gamma;
+    p.rope_cols = rope_cols;
+    p.rope = reinterpret_cast<const float2 *>(rope);
     return run_gemm(ctx, &ta, tb, p, false);
 }
+}  // namespace
 
 extern "C" int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const int32_t *nbr,
                                const void *w, int ab_dtype, const float *bias, int64_t cout, void *out, int64_t ldo,

@@ -7,6 +7,8 @@ Kernels (config-2 shapes unless noted):
   conv64     config-0 conv 64->64 on the shell (21,766 voxels)
   qkv        trunk qkv linear, 8,184 x 1024 -> 3072
   mlp0       trunk MLP up-projection with GELU, 8,184 x 1024 -> 4096
+  qkvn       qkv linear with the fused q/k head RMS norm + RoPE epilogue
+  ln         trunk LayerNorm + AdaLN modulation, 8,184 x 1024 f32 -> f16
   attn       trunk self-attention, 2 sequences x 4,092, 16 heads x 64
   cross      trunk cross-attention, 2 x 4,092 queries x 1,029 keys
 Each run is small enough for an ncu capture (a few hundred MB on the
@@ -72,6 +74,27 @@ def run(kernel: str, reps: int) -> dict:
         ms = _time(lambda: ops.linear(x, w, b, out=out, epilogue=epi), reps)
         flops = 2.0 * m * C * nout
         return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "m": m, "n": nout, "k": C}
+    if kernel == "qkvn":
+        m = 2 * 4092
+        coords = torch.from_numpy(batched(shell_coords(), 2)[:m]).to(dev)
+        x = torch.randn((m, C), device=dev, generator=g).to(h)
+        w = (torch.randn((3 * C, C), device=dev, generator=g) / 32).to(h)
+        b = torch.zeros(3 * C, device=dev)
+        gam = torch.ones(2 * C, device=dev)
+        table = ops.rope_table(coords, 64)
+        out = torch.empty((m, 3 * C), device=dev, dtype=h)
+        ms = _time(lambda: ops.linear_headnorm(x, w, b, 2 * C, gam, 2 * C, table, out=out), reps)
+        flops = 2.0 * m * C * 3 * C
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "m": m, "n": 3 * C, "k": C}
+    if kernel == "ln":
+        m = 2 * 4092
+        x = torch.randn((m, C), device=dev, generator=g)
+        mod = torch.randn((2, 6 * C), device=dev, generator=g)
+        offs = torch.tensor([0, 4092, m], dtype=torch.int32, device=dev)
+        out = torch.empty((m, C), device=dev, dtype=h)
+        ms = _time(lambda: ops.layernorm_modulate(x, 1e-6, mod=mod, batch_offsets=offs, out=out), reps)
+        bytes_ = m * C * 4 + m * C * 2
+        return {"kernel": kernel, "ms": ms, "gbs": bytes_ / ms / 1e6, "bytes": bytes_}
     if kernel in ("attn", "cross"):
         nq = 4092
         nk = nq if kernel == "attn" else 1029

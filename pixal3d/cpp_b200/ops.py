@@ -177,6 +177,33 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, o
     return out
 
 
+def linear_headnorm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, norm_cols: int,
+                    gamma: torch.Tensor | None, rope_cols: int = 0, rope: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """x W^T + b with per-64-column-head RMS norm (columns < norm_cols, gamma
+    per column) and interleaved RoPE (columns < rope_cols, rope from
+    rope_table) applied to the f32 accumulators; 16-bit out of x's type."""
+    assert x.dtype in HALF and w.dtype == x.dtype and w.is_contiguous()
+    c = ctx(x.device)
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    c.check(L.lib.p3d_linear_headnorm(c.h, _p(x), _rows(x), _p(w), _dt(x), _p(bias), m, n, k, _p(out), _rows(out),
+                                      _dt(out), norm_cols, _p(gamma), rope_cols, _p(rope)))
+    return out
+
+
+def rope_table(coords: torch.Tensor, head_dim: int = 64, freq_min: float = 1.0,
+               freq_base: float = 10000.0) -> torch.Tensor:
+    """[n, head_dim/2, 2] f32 (cos, sin) per point and rotation pair."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    t = torch.empty((n, head_dim // 2, 2), dtype=torch.float32, device=coords.device)
+    c.check(L.lib.p3d_rope_table(c.h, _p(coords), n, head_dim, freq_min, freq_base, _p(t)))
+    return t
+
+
 def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32,
                 epilogue: int = L.EPI_NONE, gate: torch.Tensor | None = None,

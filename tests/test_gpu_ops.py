@@ -282,6 +282,14 @@ def test_layernorm_modulate():
     x3 = rng.standard_normal((17, 12)).astype(np.float32)
     got = o.layernorm_modulate(dev(x3), 1e-5, out_dtype=torch.float32).cpu().numpy()
     check(got, O.layer_norm(x3, 1e-5), max_abs=1e-5, rel_l2=1e-6, what="ln C=12")
+    # C = 640: float4 loads but no register-resident instance; C = 384: register path, f16 out
+    for cc, dt in ((640, torch.float32), (384, torch.float16)):
+        xc = (rng.standard_normal((999, cc)) * 2).astype(np.float32)
+        gc = (1 + rng.standard_normal(cc) * 0.1).astype(np.float32)
+        bc = (rng.standard_normal(cc) * 0.1).astype(np.float32)
+        got = o.layernorm_modulate(dev(xc), 1e-6, dev(gc), dev(bc), out_dtype=dt).float().cpu().numpy()
+        tol = 1e-4 if dt == torch.float32 else 4e-3
+        check(got, O.layer_norm(xc, 1e-6, gc, bc), max_abs=tol, rel_l2=1e-3, what=f"ln C={cc}")
 
 
 def test_qk_rmsnorm_rope():
@@ -426,3 +434,43 @@ def test_qk_rmsnorm_rope_f16():
     ops().qk_rmsnorm_rope(t, H, hd, dev(gam), dev(c))
     check(t.float().cpu().numpy(), O.rope(c, O.rms_norm_heads(q, H, hd, gam), H, hd), max_abs=1e-2, rel_l2=1e-3,
           what="f16 rms+rope")
+
+
+# ------------------------------------------- fused per-head norm + RoPE GEMM
+
+def test_rope_table():
+    c = batched(shell_coords(32, 11.0, 1.0), 2)
+    t = ops().rope_table(dev(c), 64, 1.0, 10000.0).cpu().numpy()
+    cos, sin = O.rope_tables(c, 64, 1.0, 10000.0)
+    check(t[..., 0], cos, max_abs=2e-5, rel_l2=1e-5, what="rope cos")
+    check(t[..., 1], sin, max_abs=2e-5, rel_l2=1e-5, what="rope sin")
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("norm,rope", [(2, 2), (0, 2), (1, 0)])
+def test_linear_headnorm(dtype, norm, rope):
+    """qkv-style GEMM with the q/k head RMS norm and RoPE in the epilogue ==
+    rope(rms_norm_heads(x W^T + b)) on the same rounded operands; columns
+    past the fused range are the plain linear output."""
+    rng = np.random.default_rng(31 + norm * 3 + rope)
+    c = batched(shell_coords(24, 8.0, 1.2), 2)
+    m, H, hd, k = c.shape[0], 4, 64, 256
+    C = H * hd
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((3 * C, k)) / math.sqrt(k)).astype(np.float32)
+    b = (rng.standard_normal(3 * C) * 0.1).astype(np.float32)
+    gam = (1 + rng.standard_normal(3 * C) * 0.1).astype(np.float32)
+    to16, rnd = (hf, rounded16) if dtype == "f16" else (bf, rounded)
+    o = ops()
+    table = o.rope_table(dev(c), 64)
+    got = o.linear_headnorm(to16(x), to16(w), dev(b), norm * C, dev(gam), rope * C, table).float().cpu().numpy()
+    y = rnd(x) @ rnd(w).T + b
+    exp = y.copy()
+    if norm:
+        exp[:, :norm * C] = O.rms_norm_heads(y[:, :norm * C], norm * H, hd, gam[:norm * C])
+    for j in range(rope):
+        exp[:, j * C:(j + 1) * C] = O.rope(c, exp[:, j * C:(j + 1) * C], H, hd)
+    if dtype == "f16":
+        check(got, exp, max_abs=4e-3 * max(1.0, float(np.abs(exp).max())), rel_l2=1e-3, what="f16 headnorm")
+    else:
+        check(got, exp, max_abs=bf16_out_tol(exp), rel_l2=REL_L2, what="bf16 headnorm")
