@@ -108,6 +108,24 @@ size_t p3d_neighbor_map27_workspace(int64_t n);
 int p3d_neighbor_map27_ws(p3d_ctx *ctx, const int32_t *coords, int64_t n, void *ws, size_t ws_bytes,
                           int32_t *nbr_out);
 
+/* No counterpart in the reference.  The output of p3d_neighbor_map27_ws,
+ * for callers that cannot allocate device memory: a device node inside a
+ * planned graph (a ggml custom op, whose graph allocator sizes every tensor
+ * before compute and hands the node only its inputs and outputs), or a host
+ * that binds only this C ABI and owns no device allocator.  The hash table
+ * is a 12 MiB file-scope device array (2^20 slots) that every GPU which
+ * loads the library holds until the process exits; the call makes no
+ * cudaMalloc/cudaFree and no allocating library call.
+ *   - n above P3D_NBR_STATIC_MAX_POINTS is rejected with P3D_ERR_INVALID.
+ *   - The first call on a device looks up the array's address there
+ *     (cudaGetSymbolAddress, with ctx's device current); make that first
+ *     call before any stream capture.
+ *   - Every call shares the one array and clears the slots it uses; calls
+ *     that overlap on the GPU (other streams, contexts or threads on the
+ *     same device) race on it and must be serialised by the caller. */
+#define P3D_NBR_STATIC_MAX_POINTS 524288
+int p3d_neighbor_map27_static(p3d_ctx *ctx, const int32_t *coords, int64_t n, int32_t *nbr_out);
+
 /* Downsample topology (sparse_downsample_mean, src/sparse.cpp:536-602):
  * parents = coords / factor (per batch), output rows sorted
  * lexicographically by (b,x,y,z) like the reference.  Uses a dense

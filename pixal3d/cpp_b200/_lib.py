@@ -105,6 +105,7 @@ _sig("p3d_coord_hash_build", i32, vp, vp, i64, vp, vp, i64)
 _sig("p3d_neighbor_map27", i32, vp, vp, i64, vp, vp, i64, vp)
 _sig("p3d_neighbor_map27_workspace", sz, i64)
 _sig("p3d_neighbor_map27_ws", i32, vp, vp, i64, vp, sz, vp)
+_sig("p3d_neighbor_map27_static", i32, vp, vp, i64, vp)
 _sig("p3d_downsample_grid_ints", i64, i32, i32, i32, i32, i32)
 _sig("p3d_downsample_topology", i32, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp)
 _sig("p3d_downsample_mean", i32, vp, vp, i64, i32, i32, vp, i32, vp)
