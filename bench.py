@@ -482,8 +482,9 @@ def run_e2e(torch, model, img, cond, args, dev, world, rank):
     return {"value": round(world * steps / (ms / 1000.0), 3), "unit": "steps/s",
             "h2d_bytes_per_step": int(h2d / steps), "d2h_bytes_per_step": int(h_out.numel() * 4 / steps),
             "ms_per_call": round(ms, 2), "steps_per_call": steps,
-            "includes": "H2D coords/noise/condition, topology prepare (neighbour map, downsample), graph "
-                        "re-capture, K sampler steps, D2H latents"}
+            "includes": "H2D coords/noise/condition, topology prepare (neighbour map, downsample, RoPE table; "
+                        "workspaces and the step graph reused when the topology's shape is unchanged), "
+                        "K sampler steps, D2H latents"}
 
 
 # --------------------------------------------------------- reference arm

@@ -17,6 +17,7 @@
 //     replayed for every remaining step.
 // Residual stream h is f32; GEMM operands f16 (or bf16); accumulation f32.
 #include <cmath>
+#include <unordered_map>
 #include <vector>
 
 #include "p3d_common.cuh"
@@ -252,8 +253,16 @@ struct p3d_flow {
     p3d_ctx *ctx = nullptr;
     p3d_flow_hparams hp{};
     int C = 0, in_pad = 0, cond_pad = 0, proj_pad = 0;
-    std::vector<void *> allocs;       // weights: freed with the flow
-    std::vector<void *> prep_allocs;  // topology + workspaces: freed on re-prepare
+    std::vector<void *> allocs;  // weights: freed with the flow
+    // Topology + workspaces, one buffer per member pointer (keyed by its
+    // address).  prepare() reuses a buffer while it is large enough, so a new
+    // coordinate set of the same or smaller size rebinds no pointer.
+    struct PoolBuf {
+        void *ptr = nullptr;
+        size_t bytes = 0;
+    };
+    std::unordered_map<void *, PoolBuf> pool;
+    bool pool_grew = false;
     bool in_prepare = false;
     // weights
     uint16_t *input_w = nullptr, *output_w = nullptr;
@@ -281,7 +290,11 @@ struct p3d_flow {
     cudaStream_t stream = nullptr;
     std::string error;
     int64_t launches_per_step = 0;
-    std::vector<int32_t> h_fine_off, h_ctx_off;  // host copies of the batch / condition offsets
+    std::vector<int32_t> h_fine_off, h_ctx_off, h_trunk_off;  // host copies of the batch / condition offsets
+    int32_t *hash_ws = nullptr, *down_grid = nullptr;  // prepare-time scratch (pooled)
+    int64_t *down_m = nullptr;
+    // Shape of the topology the cached step graph was captured for.
+    std::vector<int64_t> graph_shape;
     // Cached CUDA graph of one sampler step; it reads only the buffers above,
     // so it stays valid across sample() calls until prepare() rebinds them or
     // a captured scalar (rescale, sigma_min) changes.
@@ -290,16 +303,39 @@ struct p3d_flow {
 
     template <typename T>
     int alloc(T **p, int64_t count) {
-        *p = nullptr;
         if (count <= 0) count = 1;
-        cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * count);
+        const size_t bytes = sizeof(T) * static_cast<size_t>(count);
+        if (in_prepare) {
+            PoolBuf &b = pool[reinterpret_cast<void *>(p)];
+            if (b.bytes < bytes) {
+                if (b.ptr) cudaFree(b.ptr);
+                b.ptr = nullptr;
+                b.bytes = 0;
+                pool_grew = true;
+                cudaError_t e = cudaMalloc(&b.ptr, bytes);
+                if (e != cudaSuccess)
+                    return set_error(ctx, P3D_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+                b.bytes = bytes;
+            }
+            *p = static_cast<T *>(b.ptr);
+            return P3D_OK;
+        }
+        *p = nullptr;
+        cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), bytes);
         if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
-        (in_prepare ? prep_allocs : allocs).push_back(*p);
+        allocs.push_back(*p);
         return P3D_OK;
     }
-    void free_prepared();
+    void reset_topology();
+    void drop_graph() {
+        if (step_graph) cudaGraphExecDestroy(step_graph);
+        step_graph = nullptr;
+        graph_shape.clear();
+    }
     ~p3d_flow() {
-        free_prepared();
+        if (stream) cudaStreamSynchronize(stream);
+        drop_graph();
+        for (auto &kv : pool) cudaFree(kv.second.ptr);
         for (void *p : allocs) cudaFree(p);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -471,12 +507,7 @@ struct StreamSwap {
 
 }  // namespace
 
-void p3d_flow::free_prepared() {
-    if (stream) cudaStreamSynchronize(stream);
-    if (step_graph) cudaGraphExecDestroy(step_graph);
-    step_graph = nullptr;
-    for (void *p : prep_allocs) cudaFree(p);
-    prep_allocs.clear();
+void p3d_flow::reset_topology() {
     prepared = false;
     n = nt = T = max_fine = max_trunk = max_ctx = 0;
     coords = trunk_coords = fine_off = trunk_off = ctx_off = nbr = parent = child = nullptr;
@@ -484,6 +515,10 @@ void p3d_flow::free_prepared() {
     xn = qkv = attn = mlp = kv = cq = ctx_bf = proj_bf = x_in = fbf = nullptr;
     stats = nullptr;
     counter = nullptr;
+    rope = nullptr;
+    hash_ws = down_grid = nullptr;
+    down_m = nullptr;
+    h_trunk_off.clear();
 }
 
 extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out) {
@@ -604,9 +639,12 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     if (!f) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
     P3D_REQUIRE(ctx, coords && ctx_offsets_host && n > 0 && batch > 0, "p3d_flow_prepare: bad argument");
-    // Rebinding releases the previous coordinate set's topology, workspaces
-    // and cached step graph; weights stay resident.
-    f->free_prepared();
+    // Rebinding reuses the previous coordinate set's buffers where they are
+    // large enough; the cached step graph survives only if no buffer moved and
+    // the topology's sizes and offsets are unchanged.  Weights stay resident.
+    if (f->stream) P3D_CUDA(ctx, cudaStreamSynchronize(f->stream));
+    f->reset_topology();
+    f->pool_grew = false;
     struct PrepScope {
         p3d_flow *f;
         explicit PrepScope(p3d_flow *ff) : f(ff) { f->in_prepare = true; }
@@ -618,7 +656,8 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     f->n = n;
     // host copies of coords -> batch offsets (rows contiguous by batch)
     std::vector<int32_t> hc(static_cast<size_t>(n) * 4);
-    P3D_CUDA(ctx, cudaMemcpy(hc.data(), coords, sizeof(int32_t) * hc.size(), cudaMemcpyDeviceToHost));
+    P3D_CUDA(ctx, cudaMemcpyAsync(hc.data(), coords, sizeof(int32_t) * hc.size(), cudaMemcpyDeviceToHost, ctx->stream));
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     std::vector<int32_t> off(batch + 1, 0);
     for (int64_t i = 0; i < n; ++i) {
         const int b = hc[i * 4];
@@ -640,40 +679,37 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     f->h_fine_off = off;
     f->h_ctx_off = coff;
     P3D_TRY(f->alloc(&f->coords, n * 4));
-    P3D_CUDA(ctx, cudaMemcpy(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice));
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
     P3D_TRY(f->alloc(&f->fine_off, batch + 1));
-    P3D_CUDA(ctx, cudaMemcpy(f->fine_off, off.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->fine_off, off.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
+                                  ctx->stream));
     P3D_TRY(f->alloc(&f->ctx_off, batch + 1));
-    P3D_CUDA(ctx, cudaMemcpy(f->ctx_off, coff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->ctx_off, coff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
+                                  ctx->stream));
     const bool io = hp.io_resblocks > 0;
     if (io) {
         // fine-level neighbour map and 2x downsample topology
         P3D_TRY(f->alloc(&f->nbr, 27 * n));
-        size_t wsb = p3d_neighbor_map27_workspace(n);
-        void *ws = nullptr;
-        P3D_CUDA(ctx, cudaMalloc(&ws, wsb));
-        int rc = p3d_neighbor_map27_ws(ctx, f->coords, n, ws, wsb, f->nbr);
+        const size_t wsb = p3d_neighbor_map27_workspace(n);
+        P3D_TRY(f->alloc(&f->hash_ws, static_cast<int64_t>((wsb + 3) / 4)));
+        P3D_TRY(p3d_neighbor_map27_ws(ctx, f->coords, n, f->hash_ws, wsb, f->nbr));
         const int64_t gints = p3d_downsample_grid_ints(batch, sx, sy, sz, 2);
-        int32_t *grid = nullptr;
-        int64_t *dm = nullptr;
-        if (!rc) rc = f->alloc(&f->trunk_coords, n * 4);
-        if (!rc) rc = f->alloc(&f->parent, n);
-        if (!rc) rc = f->alloc(&f->child, n * 8);
-        if (!rc && cudaMalloc(&grid, sizeof(int32_t) * gints) != cudaSuccess) rc = P3D_ERR_CUDA;
-        if (!rc && cudaMalloc(&dm, sizeof(int64_t)) != cudaSuccess) rc = P3D_ERR_CUDA;
-        if (!rc)
-            rc = p3d_downsample_topology(ctx, f->coords, n, batch, sx, sy, sz, 2, grid, f->trunk_coords, f->parent,
-                                         f->child, dm);
+        P3D_TRY(f->alloc(&f->trunk_coords, n * 4));
+        P3D_TRY(f->alloc(&f->parent, n));
+        P3D_TRY(f->alloc(&f->child, n * 8));
+        P3D_TRY(f->alloc(&f->down_grid, gints));
+        P3D_TRY(f->alloc(&f->down_m, 1));
+        P3D_TRY(p3d_downsample_topology(ctx, f->coords, n, batch, sx, sy, sz, 2, f->down_grid, f->trunk_coords,
+                                        f->parent, f->child, f->down_m));
         int64_t m = 0;
-        if (!rc && cudaMemcpy(&m, dm, sizeof(int64_t), cudaMemcpyDeviceToHost) != cudaSuccess) rc = P3D_ERR_CUDA;
-        cudaFree(ws);
-        cudaFree(grid);
-        cudaFree(dm);
-        if (rc) return rc;
+        P3D_CUDA(ctx, cudaMemcpyAsync(&m, f->down_m, sizeof(int64_t), cudaMemcpyDeviceToHost, ctx->stream));
+        P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
         P3D_TRY(p3d_ctx_check(ctx));
         f->nt = m;
         std::vector<int32_t> tc(static_cast<size_t>(m) * 4);
-        P3D_CUDA(ctx, cudaMemcpy(tc.data(), f->trunk_coords, sizeof(int32_t) * tc.size(), cudaMemcpyDeviceToHost));
+        P3D_CUDA(ctx, cudaMemcpyAsync(tc.data(), f->trunk_coords, sizeof(int32_t) * tc.size(), cudaMemcpyDeviceToHost,
+                                      ctx->stream));
+        P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
         std::vector<int32_t> toff(batch + 1, 0);
         for (int64_t i = 0; i < m; ++i) toff[tc[i * 4] + 1]++;
         for (int b = 0; b < batch; ++b) {
@@ -681,7 +717,9 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
             f->max_trunk = std::max<int64_t>(f->max_trunk, toff[b + 1] - toff[b]);
         }
         P3D_TRY(f->alloc(&f->trunk_off, batch + 1));
-        P3D_CUDA(ctx, cudaMemcpy(f->trunk_off, toff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice));
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->trunk_off, toff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
+                                      ctx->stream));
+        f->h_trunk_off = toff;
         P3D_TRY(f->alloc(&f->hf, n * C));
         P3D_TRY(f->alloc(&f->ftmp, n * C));
         P3D_TRY(f->alloc(&f->fbf, n * C));
@@ -691,6 +729,7 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         f->trunk_coords = f->coords;
         f->trunk_off = f->fine_off;
         f->max_trunk = f->max_fine;
+        f->h_trunk_off = off;
         P3D_TRY(f->alloc(&f->stats, 4 * batch));
     }
     const int64_t nt = f->nt;
@@ -720,6 +759,15 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         P3D_TRY(f->alloc(&f->rope, nt * 64));
         P3D_TRY(p3d_rope_table(ctx, f->trunk_coords, nt, 64, hp.rope_freq_min, hp.rope_freq_base, f->rope));
     }
+    // The host copies above were issued on ctx->stream; the flow's own stream
+    // must not run ahead of them.
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    std::vector<int64_t> shape = {n, f->nt, f->T, batch, f->max_fine, f->max_trunk, f->max_ctx};
+    shape.insert(shape.end(), off.begin(), off.end());
+    shape.insert(shape.end(), coff.begin(), coff.end());
+    shape.insert(shape.end(), f->h_trunk_off.begin(), f->h_trunk_off.end());
+    if (f->pool_grew || shape != f->graph_shape) f->drop_graph();
+    f->graph_shape = shape;
     f->prepared = true;
     return P3D_OK;
 }

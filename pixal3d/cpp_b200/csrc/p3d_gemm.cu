@@ -20,11 +20,16 @@
 // Tile 128 x BN (BN in {64,128,256}), BK = 64 (one 128-byte swizzle atom),
 // UMMA 128 x BN x 16; accumulators double-buffered in TMEM (2*BN columns) so
 // the epilogue of tile i overlaps the main loop of tile i+1.
+// When N is a multiple of 256 the CTA-pair kernel runs instead: a cluster of
+// two CTAs on two SMs computes a 256 x (NSUB*256) tile with
+// tcgen05.mma.cta_group::2, each SM staging its own A rows and half of B, so
+// each SM streams half the B bytes per FLOP from L2 (the conv's bound).
 // Every mbarrier wait is bounded (p3d_common.cuh): a stuck pipeline latches
 // P3D_ERR_TIMEOUT and the kernel still frees its TMEM and exits.
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "p3d_common.cuh"
@@ -63,18 +68,34 @@ struct GemmParams {
     const float2 *rope;
 };
 
-// MT = 128-row M sub-tiles per CTA tile; they share every B stage, which
-// halves the B operand stream per FLOP when MT = 2.
-template <int BN, int MT>
+// 1-CTA tile: 128 x BN, BK = 64; accumulators double-buffered in TMEM.
+template <int BN>
 struct Cfg {
-    static constexpr int A_BYTES = MT * BM * BK * 2;
+    static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
-    static constexpr int ACC_COLS = MT * BN;                 // one accumulator buffer
-    static constexpr int ACC_BUFS = 2 * ACC_COLS <= 512 ? 2 : 1;
-    static constexpr int TMEM_COLS = ACC_BUFS * ACC_COLS <= 128 ? 128 : (ACC_BUFS * ACC_COLS <= 256 ? 256 : 512);
+    static constexpr int ACC_COLS = BN;
+    static constexpr int ACC_BUFS = 2;
+    static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// CTA-pair tile: 256 x (NSUB * 256).  Each CTA of the pair stages its own 128
+// A rows and its 128-row half of each N = 256 slice of B, so the B stream per
+// FLOP is half that of the 1-CTA tile; NSUB = 2 halves it again (one TMEM
+// accumulator buffer of 512 columns, for long K loops such as the conv).
+template <int NSUB>
+struct Cfg2 {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_SUB = 128 * BK * 2;
+    static constexpr int B_BYTES = NSUB * B_SUB;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr int ACC_COLS = NSUB * 256;
+    static constexpr int ACC_BUFS = NSUB == 1 ? 2 : 1;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <typename T>
@@ -148,12 +169,133 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int64_t row, in
     }
 }
 
-template <int BN, bool GATHER, int MT>
+// Epilogue of one warp for one accumulator buffer: lane l owns output row
+// `row`; tacc addresses this warp's TMEM lane quarter at accumulator column
+// 0; accumulator column c is output column n0 + c.  Bias, then per-head RMS
+// norm + RoPE (64-column heads) or the activation, then the store / gated
+// residual add.  Every tcgen05.ld is issued by the whole (converged) warp.
+template <int COLS>
+__device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc, int64_t row, int64_t n0) {
+    if (p.norm_cols > 0 || p.rope_cols > 0) {
+#pragma unroll 1
+        for (int cs = 0; cs < COLS; cs += 64) {
+            float v[64];
+            {
+                float a[32], b[32];
+                tmem_ld32(tacc + cs, a);
+                tmem_ld32(tacc + cs + 32, b);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    v[i] = a[i];
+                    v[32 + i] = b[i];
+                }
+            }
+            const int64_t col0 = n0 + cs;
+            if (col0 < p.N && row < p.M) {
+                if (p.bias) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) v[i] += __ldg(p.bias + col0 + i);
+                }
+                if (col0 < p.norm_cols) {
+                    float ss = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
+                    const float inv = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) / max(||v||, eps)
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) v[i] = v[i] * inv * __ldg(p.norm_gamma + col0 + i);
+                }
+                if (col0 < p.rope_cols) {
+                    const float2 *cs2 = p.rope + row * 32;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float2 r = __ldg(cs2 + i);
+                        const float e = v[2 * i], o = v[2 * i + 1];
+                        v[2 * i] = e * r.x - o * r.y;
+                        v[2 * i + 1] = e * r.y + o * r.x;
+                    }
+                }
+                float lo[32], hi[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    lo[i] = v[i];
+                    hi[i] = v[32 + i];
+                }
+                store_chunk(p, row, col0, lo, 32);
+                store_chunk(p, row, col0 + 32, hi, 32);
+            }
+            __syncwarp();
+        }
+        return;
+    }
+#pragma unroll 1
+    for (int cs = 0; cs < COLS; cs += 32) {
+        float v[32];
+        tmem_ld32(tacc + cs, v);
+        tmem_ld_wait();
+        const int64_t col0 = n0 + cs;
+        if (col0 < p.N && row < p.M) {
+            const int ncols = static_cast<int>(p.N - col0 < 32 ? p.N - col0 : 32);
+            if (p.bias) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += (i < ncols) ? __ldg(p.bias + col0 + i) : 0.0f;
+            }
+            if (p.epi & P3D_EPI_GELU_TANH) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
+            } else if (p.epi & P3D_EPI_SILU) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = silu_f(v[i]);
+            }
+            store_chunk(p, row, col0, v, ncols);
+        }
+        __syncwarp();  // reconverge before the next tcgen05.ld (.sync.aligned)
+    }
+}
+
+// Source row of tile row m0 + (t & 127) for tap `tap` (sentinel or out of
+// range -> -1, i.e. zero fill).  Loaded one tap ahead of its use so the
+// gather's issue never waits on this load.
+__device__ __forceinline__ int32_t gather_src(const GemmParams &p, int t, int64_t m0, int tap) {
+    const int64_t row = m0 + t;
+    if (tap >= 27 || row >= p.M) return -1;
+    const int32_t s = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
+    return (s >= p.M || s < 0) ? -1 : s;
+}
+
+// One producer stage of the gather variant, issued by the 128 producer
+// threads: A rows [m0, m0+128), columns [kc, kc+64) of x[src(row)], where
+// thread t holds src of row m0 + t.  Warp w owns tile rows [32w, 32w+32);
+// each cp.async instruction copies 4 whole rows, 8 lanes per 128-byte row
+// (source indices exchanged by shuffles): coalesced global reads and
+// conflict-free swizzled shared writes.
+__device__ __forceinline__ void gather_stage_a(const GemmParams &p, uint8_t *sa, int t, int32_t my_src, int kc) {
+    const int lane_ = t & 31;
+    const int chunk = lane_ & 7;
+    const int wrow0 = (t >> 5) * 32;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = wrow0 + i * 4 + (lane_ >> 3);
+        const int32_t src = __shfl_sync(0xffffffffu, my_src, i * 4 + (lane_ >> 3));
+        const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
+        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
+    }
+}
+
+// Warp-uniform bounded wait: lane 0 polls, the warp follows its verdict.
+template <bool CLUSTER>
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *fault) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0)
+        ok = (CLUSTER ? mbar_wait_cluster(bar, parity, fault) : mbar_wait(bar, parity, fault)) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <int BN, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const GemmParams p) {
-    using C = Cfg<BN, MT>;
-    constexpr int BMT = BM * MT;  // rows per CTA tile
+    using C = Cfg<BN>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -170,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const int64_t m_tiles = (p.M + BMT - 1) / BMT;
+    const int64_t m_tiles = (p.M + BM - 1) / BM;
     const int64_t n_tiles = (p.N + BN - 1) / BN;
     const int64_t num_tiles = m_tiles * n_tiles;
     const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
@@ -206,14 +348,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int64_t m0 = (tile / n_tiles) * BMT;
+            const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
+            int32_t cur_src = 0, next_src = 0;
+            if (GATHER) {
+                cur_src = gather_src(p, t, m0, 0);
+                next_src = gather_src(p, t, m0, 1);
+            }
             for (int kb = 0; kb < num_kb; ++kb) {
                 if (GATHER) {
-                    // warp-uniform bounded wait (lane 0 polls, the warp follows)
-                    int w_ok = 1;
-                    if ((t & 31) == 0) w_ok = mbar_wait(&empty_bar[stage], phase ^ 1, p.fault) ? 1 : 0;
-                    if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+                    if (!warp_wait<false>(&empty_bar[stage], phase ^ 1, p.fault)) {
                         ok = false;
                         break;
                     }
@@ -228,31 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (GATHER) {
                     const int tap = kb / kblocks_per_tap;
                     const int kc = (kb % kblocks_per_tap) * BK;
-                    // Warp w owns tile rows [w*32*MT, (w+1)*32*MT).  Per 32-row
-                    // slice, lane l fetches the source row of slice row l;
-                    // each cp.async instruction then copies 4 whole rows, 8
-                    // lanes per 128-byte row: coalesced global reads and
-                    // conflict-free swizzled shared-memory writes.
-                    const int lane_ = t & 31;
-                    const int chunk = lane_ & 7;
-#pragma unroll
-                    for (int sl = 0; sl < MT; ++sl) {
-                        const int wrow0 = ((t >> 5) * MT + sl) * 32;
-                        const int64_t row = m0 + wrow0 + lane_;
-                        int32_t my_src = -1;
-                        if (row < p.M) {
-                            my_src = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
-                            if (my_src >= p.M || my_src < 0) my_src = -1;  // sentinel -> zero row
-                        }
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int r = wrow0 + i * 4 + (lane_ >> 3);
-                            const int32_t src = __shfl_sync(0xffffffffu, my_src, i * 4 + (lane_ >> 3));
-                            const uint16_t *g =
-                                p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
-                            cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
-                        }
+                    if (kc == 0 && tap > 0) {
+                        cur_src = next_src;
+                        next_src = gather_src(p, t, m0, tap + 1);
                     }
+                    gather_stage_a(p, sa, t, cur_src, kc);
                     if (t == 0) {
                         mbar_arrive_expect_tx(&full_bar[stage], C::B_BYTES);
                         // Tap t's weights are rows [t*N, (t+1)*N) of the stacked [27*N, K] map.
@@ -261,10 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     cp_async_mbar_arrive_noinc(&full_bar[stage]);
                 } else if (t == 0) {
                     mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
-#pragma unroll
-                    for (int sl = 0; sl < MT; ++sl)
-                        tma_load_2d(sa + sl * (BM * 128), &tmap_a, &full_bar[stage], kb * BK,
-                                    static_cast<int>(m0 + sl * BM));
+                    tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, static_cast<int>(m0));
                     tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, static_cast<int>(n0));
                 }
                 if (++stage == STAGES) {
@@ -300,12 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-#pragma unroll
-                        for (int sl = 0; sl < MT; ++sl)
-                            umma_f16(d_tmem + sl * BN, sw128_desc(a_addr + sl * (BM * 128) + kk * 32),
-                                     sw128_desc(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                    }
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                                 (kb > 0 || kk > 0) ? 1u : 0u);
                     issued = true;
                     umma_commit(&empty_bar[stage]);
                     if (++stage == STAGES) {
@@ -333,92 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int64_t m0 = (tile / n_tiles) * BMT;
+            const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
-            if (!mbar_wait(&tfull_bar[acc], acc_phase, p.fault)) break;
+            if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            if (p.norm_cols > 0 || p.rope_cols > 0) {
-                // 64-column groups = one head: bias, per-head RMS norm with gamma,
-                // interleaved RoPE from the per-row cos/sin table, then store.
-#pragma unroll 1
-                for (int cs = 0; cs < MT * BN; cs += 64) {
-                    const int sl = cs / BN, c0 = cs % BN;
-                    const int64_t row = m0 + sl * BM + q * 32 + lane;
-                    float v[64];
-                    {
-                        float a[32], b[32];
-                        const uint32_t ta = tmem_base + acc * C::ACC_COLS + cs + (static_cast<uint32_t>(q * 32) << 16);
-                        tmem_ld32(ta, a);
-                        tmem_ld32(ta + 32, b);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            v[i] = a[i];
-                            v[32 + i] = b[i];
-                        }
-                    }
-                    const int64_t col0 = n0 + c0;
-                    if (col0 < p.N && row < p.M) {
-                        if (p.bias) {
-#pragma unroll
-                            for (int i = 0; i < 64; ++i) v[i] += __ldg(p.bias + col0 + i);
-                        }
-                        if (col0 < p.norm_cols) {
-                            float ss = 0.0f;
-#pragma unroll
-                            for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
-                            const float inv = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) / max(||v||, eps)
-#pragma unroll
-                            for (int i = 0; i < 64; ++i) v[i] = v[i] * inv * __ldg(p.norm_gamma + col0 + i);
-                        }
-                        if (col0 < p.rope_cols) {
-                            const float2 *cs2 = p.rope + row * 32;
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                const float2 r = __ldg(cs2 + i);
-                                const float e = v[2 * i], o = v[2 * i + 1];
-                                v[2 * i] = e * r.x - o * r.y;
-                                v[2 * i + 1] = e * r.y + o * r.x;
-                            }
-                        }
-                        float lo[32], hi[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            lo[i] = v[i];
-                            hi[i] = v[32 + i];
-                        }
-                        store_chunk(p, row, col0, lo, 32);
-                        store_chunk(p, row, col0 + 32, hi, 32);
-                    }
-                    __syncwarp();
-                }
-            } else {
-#pragma unroll 1
-            for (int cs = 0; cs < MT * BN; cs += 32) {
-                const int sl = cs / BN, c0 = cs % BN;
-                const int64_t row = m0 + sl * BM + q * 32 + lane;
-                float v[32];
-                tmem_ld32(tmem_base + acc * C::ACC_COLS + cs + (static_cast<uint32_t>(q * 32) << 16), v);
-                tmem_ld_wait();
-                const int64_t col0 = n0 + c0;
-                if (col0 < p.N && row < p.M) {
-                    const int ncols = static_cast<int>(p.N - col0 < 32 ? p.N - col0 : 32);
-                    if (p.bias) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] += (i < ncols) ? __ldg(p.bias + col0 + i) : 0.0f;
-                    }
-                    if (p.epi & P3D_EPI_GELU_TANH) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
-                    } else if (p.epi & P3D_EPI_SILU) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = silu_f(v[i]);
-                    }
-                    store_chunk(p, row, col0, v, ncols);
-                }
-                __syncwarp();  // reconverge before the next tcgen05.ld (.sync.aligned)
-            }
-            }
+            epilogue_rows<BN>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
+                              m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -429,10 +467,248 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == kMmaWarp) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// CTA-pair (cluster of 2) variant: tcgen05.mma.cta_group::2 with M = 256, the
+// even CTA (rank 0) issuing for both.  Per stage each CTA fills its own
+// shared memory (A rows m0 + 128*rank, B rows of its half).  Both CTAs' TMA
+// loads count their bytes on the even CTA's `full` barrier (the even CTA
+// posts the expected bytes of both).  Gather variant: row gathers arrive on
+// their own CTA's `full` barrier through cp.async.mbarrier.arrive, and the
+// odd CTA's warp 8 forwards that completion to the even CTA's `full`
+// barrier (release, cluster scope).  The issuer's tcgen05.commit arrives on the
+// `empty` / `tfull` barriers of both CTAs (one commit per CTA,
+// shared::cluster addresses); both epilogues release the accumulator to the
+// even CTA's `tempty` barrier (count 8).  No TMA multicast.  All waits are
+// bounded; the pair meets at cluster barriers before the first remote
+// arrival and before freeing TMEM.
+template <int NSUB, bool GATHER>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const GemmParams p) {
+    using C = Cfg2<NSUB>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int PAIR_N = NSUB * 256;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint8_t *smem_a = smem;
+    uint8_t *smem_b = smem + STAGES * C::A_BYTES;
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_b + STAGES * C::B_BYTES);
+    uint64_t *empty_bar = full_bar + STAGES;
+    uint64_t *tfull_bar = empty_bar + STAGES;  // [2]
+    uint64_t *tempty_bar = tfull_bar + 2;      // [2]
+    uint64_t *done_bar = tempty_bar + 2;       // [1]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done_bar + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const int64_t pair = blockIdx.x >> 1;
+    const int64_t npairs = gridDim.x >> 1;
+
+    const int64_t m_tiles = (p.M + 2 * BM - 1) / (2 * BM);
+    const int64_t n_tiles = (p.N + PAIR_N - 1) / PAIR_N;
+    const int64_t num_tiles = m_tiles * n_tiles;
+    const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
+    const int num_kb = GATHER ? 27 * kblocks_per_tap : kblocks_per_tap;
+
+    if (threadIdx.x == 0) {
+        // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
+        // the odd CTA's forwarded gather completion); odd CTA (gather): its
+        // 128 row-gather threads, forwarded by its warp 8.
+        const uint32_t full_count = GATHER ? (rank == 0 ? kProducerThreads + 2 : kProducerThreads) : 1;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], full_count);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 8);
+        }
+        mbar_init(done_bar, 1);
+        fence_barrier_init();
+        if (!GATHER) prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc2(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp < 4) {
+        // ------------------------------------------------------------ producer
+        const int t = threadIdx.x;
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+            const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
+            const int64_t n0 = (tile % n_tiles) * PAIR_N;
+            int32_t cur_src = 0, next_src = 0;
+            if (GATHER) {
+                cur_src = gather_src(p, t, m0, 0);
+                next_src = gather_src(p, t, m0, 1);
+            }
+            for (int kb = 0; kb < num_kb; ++kb) {
+                if (GATHER) {
+                    if (!warp_wait<true>(&empty_bar[stage], phase ^ 1, p.fault)) {
+                        ok = false;
+                        break;
+                    }
+                } else if (t == 0) {
+                    if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, p.fault)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                uint8_t *sa = smem_a + stage * C::A_BYTES;
+                uint8_t *sb = smem_b + stage * C::B_BYTES;
+                const int tap = GATHER ? kb / kblocks_per_tap : 0;
+                const int kc = GATHER ? (kb % kblocks_per_tap) * BK : kb * BK;
+                if (GATHER) {
+                    if (kc == 0 && tap > 0) {
+                        cur_src = next_src;
+                        next_src = gather_src(p, t, m0, tap + 1);
+                    }
+                    gather_stage_a(p, sa, t, cur_src, kc);
+                }
+                if (t == 0) {
+                    const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+                    if (rank == 0)
+                        mbar_arrive_expect_tx(&full_bar[stage], 2 * (GATHER ? C::B_BYTES : C::A_BYTES + C::B_BYTES));
+                    if (!GATHER) tma_load_2d_pair(sa, &tmap_a, fb, kc, static_cast<int>(m0));
+#pragma unroll
+                    for (int j = 0; j < NSUB; ++j)
+                        tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
+                                         static_cast<int>(tap * p.N + n0 + j * 256 + rank * 128));
+                }
+                if (GATHER) cp_async_mbar_arrive_noinc(&full_bar[stage]);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0 && rank == 0) {
+            // ------------------------------------------------ pair MMA issue
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool issued = false;
+            const uint32_t idesc = p.idesc;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1, p.fault)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&full_bar[stage], phase, p.fault)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (GATHER) fence_proxy_async_smem();
+                    const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
+                    const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+#pragma unroll
+                        for (int j = 0; j < NSUB; ++j)
+                            umma2_f16(d_tmem + j * 256, sw128_desc(a_addr + kk * 32),
+                                      sw128_desc(b_addr + j * C::B_SUB + kk * 32), idesc,
+                                      (kb > 0 || kk > 0) ? 1u : 0u);
+                    issued = true;
+                    const uint32_t e = smem_u32(&empty_bar[stage]);
+                    umma_commit2(e);
+                    umma_commit2(mapa_shared(e, peer));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t f = smem_u32(&tfull_bar[acc]);
+                umma_commit2(f);
+                umma_commit2(mapa_shared(f, peer));
+                if (++acc == C::ACC_BUFS) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            if (issued) {
+                umma_commit2(smem_u32(done_bar));
+                mbar_wait(done_bar, 0, p.fault);
+            }
+        } else if (GATHER && lane == 0) {
+            // ------------ odd CTA: forward its row-gather completion to rank 0
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full_bar[stage], phase, p.fault)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), peer));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
+            const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
+            const int64_t n0 = (tile % n_tiles) * PAIR_N;
+            if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
+            tc_fence_after();
+            epilogue_rows<C::ACC_COLS>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
+                                       m0 + q * 32 + lane, n0);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t te = smem_u32(&tempty_bar[acc]);
+                if (rank == 0)
+                    mbar_arrive(&tempty_bar[acc]);
+                else
+                    mbar_arrive_cluster(mapa_shared(te, peer));
+            }
+            if (++acc == C::ACC_BUFS) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all();  // no remote arrival or pair MMA is pending past here
+    tc_fence_after();
+    if (warp == kMmaWarp) tmem_dealloc2(tmem_base, C::TMEM_COLS);
 }
 
 using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -453,19 +729,47 @@ EncodeFn get_encode_fn() {
     return fn;
 }
 
-template <int BN, bool GATHER, int MT>
+template <int BN, bool GATHER>
 int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
-    using C = Cfg<BN, MT>;
+    using C = Cfg<BN>;
     static bool attr_set = false;
     if (!attr_set) {
-        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm_tc_kernel<BN, GATHER, MT>,
+        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm_tc_kernel<BN, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::SMEM));
+        attr_set = true;
+    }
+    const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
+    gemm_tc_kernel<BN, GATHER><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    return check_launch(ctx, "gemm_tc_kernel");
+}
+
+template <int NSUB, bool GATHER>
+int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
+    using C = Cfg2<NSUB>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm2_tc_kernel<NSUB, GATHER>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set = true;
     }
-    const int64_t tiles = ceil_div(p.M, BM * MT) * ceil_div(p.N, BN);
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
-    gemm_tc_kernel<BN, GATHER, MT><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
-    return check_launch(ctx, "gemm_tc_kernel");
+    // Persistent grid: as many pairs as can be co-resident (not every SM
+    // can be paired into a cluster), so no pair waits for a second wave.
+    static int max_pairs = 0;
+    if (max_pairs == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (ctx->num_sms / 2), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.stream = ctx->stream;
+        int n = 0;
+        P3D_CUDA(ctx, cudaOccupancyMaxActiveClusters(&n, gemm2_tc_kernel<NSUB, GATHER>, &cfg));
+        max_pairs = std::max(1, std::min(n, ctx->num_sms / 2));
+    }
+    const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
+    const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
+    gemm2_tc_kernel<NSUB, GATHER><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    return check_launch(ctx, "gemm2_tc_kernel");
 }
 
 int pick_bn(int64_t n) {
@@ -474,23 +778,62 @@ int pick_bn(int64_t n) {
     return 256;
 }
 
-int run_gemm(p3d_ctx *ctx, const CUtensorMap *ta, const CUtensorMap &tb, const GemmParams &p, bool gather) {
-    const int bn = pick_bn(p.N);
-    CUtensorMap dummy = tb;
-    const CUtensorMap &a = ta ? *ta : dummy;
-    if (gather) {
-        // Long K loops (27 taps x Cin/64): two 128-row sub-tiles per CTA share
-        // every B stage once there are enough 256-row tiles to fill the GPU.
-        // Measured on B200: MT = 2 (3 stages) is slower than MT = 1 (4 stages) for
-        // the config-2 conv (3.13 vs 2.55 ms), so the gather path uses MT = 1.
-        const bool mt2 = false;
-        if (bn == 64) return mt2 ? launch_gemm<64, true, 2>(ctx, a, tb, p) : launch_gemm<64, true, 1>(ctx, a, tb, p);
-        if (bn == 128) return mt2 ? launch_gemm<128, true, 2>(ctx, a, tb, p) : launch_gemm<128, true, 1>(ctx, a, tb, p);
-        return mt2 ? launch_gemm<256, true, 2>(ctx, a, tb, p) : launch_gemm<256, true, 1>(ctx, a, tb, p);
+// Pair kernels on (default) unless P3D_GEMM_PAIR=0 selects the 1-CTA kernels.
+bool pair_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("P3D_GEMM_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// P3D_GEMM_PAIR_DENSE=1 also routes dense linears with N % 256 == 0 to the pair kernel.
+bool pair_dense() {
+    static const bool on = [] {
+        const char *e = std::getenv("P3D_GEMM_PAIR_DENSE");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+// x == nullptr selects the gather (sparse conv) variant, whose B operand is
+// the [27 * N, K] tap stack.  Builds the tensor maps and instruction
+// descriptor for the chosen kernel and launches it.
+int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dtype, GemmParams p) {
+    const bool gather = x == nullptr;
+    const bool bf16 = ab_dtype == P3D_BF16;
+    const int64_t w_rows = gather ? 27 * p.N : p.N;
+    CUtensorMap ta, tb;
+    // The pair kernel serves the gather (conv) path, whose 27*Cin-long K loop
+    // streams the most B bytes per output tile; for the dense linears
+    // (K <= 4096) it measured no faster than the 1-CTA kernel on B200
+    // (qkv 8184x3072x1024: 69.0 vs 69.0 us; MLP-up 99.5 vs 96.6 us).
+    if (pair_enabled() && p.N % 256 == 0 && (gather || pair_dense())) {
+        // Gather: two N = 256 MMAs per pair tile when N allows (long K loops
+        // hide the unbuffered epilogue); dense: one, double-buffered.
+        const int nsub = (gather && p.N % 512 == 0) ? 2 : 1;
+        int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, 128);
+        if (rc) return rc;
+        if (!gather && (rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM))) return rc;
+        if (gather) ta = tb;
+        p.idesc = idesc_f32acc(2 * BM, 256, bf16);
+        if (gather) return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, p) : launch_gemm2<1, true>(ctx, ta, tb, p);
+        return launch_gemm2<1, false>(ctx, ta, tb, p);
     }
-    if (bn == 64) return launch_gemm<64, false, 1>(ctx, a, tb, p);
-    if (bn == 128) return launch_gemm<128, false, 1>(ctx, a, tb, p);
-    return launch_gemm<256, false, 1>(ctx, a, tb, p);
+    const int bn = pick_bn(p.N);
+    int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, bn);
+    if (rc) return rc;
+    if (!gather && (rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM))) return rc;
+    if (gather) ta = tb;
+    p.idesc = idesc_f32acc(BM, bn, bf16);
+    if (gather) {
+        if (bn == 64) return launch_gemm<64, true>(ctx, ta, tb, p);
+        if (bn == 128) return launch_gemm<128, true>(ctx, ta, tb, p);
+        return launch_gemm<256, true>(ctx, ta, tb, p);
+    }
+    if (bn == 64) return launch_gemm<64, false>(ctx, ta, tb, p);
+    if (bn == 128) return launch_gemm<128, false>(ctx, ta, tb, p);
+    return launch_gemm<256, false>(ctx, ta, tb, p);
 }
 
 }  // namespace
@@ -563,12 +906,6 @@ int linear_impl(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_
                 "p3d_linear: residual epilogue needs f32 out");
     P3D_REQUIRE(ctx, !gate || (batch_offsets && nbatch > 0), "p3d_linear: gate needs batch offsets");
     if (m == 0) return P3D_OK;
-    const int bn = pick_bn(n);
-    CUtensorMap ta, tb;
-    int rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, m, k, ldx, BM);
-    if (rc) return rc;
-    rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, n, k, k, bn);
-    if (rc) return rc;
     GemmParams p{};
     p.x = static_cast<const uint16_t *>(x);
     p.ldx = ldx;
@@ -583,14 +920,13 @@ int linear_impl(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_
     p.N = n;
     p.K = k;
     p.out_dtype = out_dtype;
-    p.idesc = idesc_f32acc(BM, bn, ab_dtype == P3D_BF16);
     p.epi = epilogue;
     p.fault = ctx->fault;
     p.norm_cols = norm_cols;
     p.norm_gamma = norm_gamma;
     p.rope_cols = rope_cols;
     p.rope = reinterpret_cast<const float2 *>(rope);
-    return run_gemm(ctx, &ta, tb, p, false);
+    return run_gemm(ctx, x, ldx, w, ab_dtype, p);
 }
 }  // namespace
 
@@ -610,14 +946,8 @@ extern "C" int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t c
     P3D_REQUIRE(ctx, !gate || (batch_offsets && nbatch > 0), "p3d_subm_conv3d: gate needs batch offsets");
     P3D_REQUIRE(ctx, n < (int64_t(1) << 31), "p3d_subm_conv3d: too many points");
     if (n == 0) return P3D_OK;
-    const int bn = pick_bn(cout);
     // B operand: the 27 taps stacked as [27*cout, cin]; tap t occupies rows
-    // [t*cout, (t+1)*cout).  The kernel addresses tap t with row coordinate
-    // n0 + t*cout through a per-tap map, so encode one map per launch over
-    // the whole stack and offset rows in-kernel.
-    CUtensorMap tb;
-    int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, 27 * cout, cin, cin, bn);
-    if (rc) return rc;
+    // [t*cout, (t+1)*cout), addressed in-kernel as row t*cout + n.
     GemmParams p{};
     p.x = static_cast<const uint16_t *>(x);
     p.ldx = cin;
@@ -633,8 +963,7 @@ extern "C" int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t c
     p.N = cout;
     p.K = cin;
     p.out_dtype = out_dtype;
-    p.idesc = idesc_f32acc(BM, bn, ab_dtype == P3D_BF16);
     p.epi = epilogue;
     p.fault = ctx->fault;
-    return run_gemm(ctx, nullptr, tb, p, true);
+    return run_gemm(ctx, nullptr, cin, w, ab_dtype, p);
 }

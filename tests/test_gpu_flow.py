@@ -142,9 +142,10 @@ def test_flow_forward_bf16_operands():
 
 
 def test_flow_sample_cached_graph_and_reprepare():
-    """A second sample() replays the cached step graph bit for bit; prepare()
-    on a new coordinate set rebuilds topology and workspaces, and the result
-    still matches the oracle."""
+    """A second sample() replays the cached step graph bit for bit.  prepare()
+    on a larger coordinate set grows the workspaces; back on the smaller set
+    the buffers are reused (new shape, graph re-captured); the same set again
+    keeps the cached graph.  Every result matches the oracle."""
     hp = O.FlowHParams(in_channels=8, out_channels=8, model_channels=128, cond_channels=64, num_blocks=2,
                        num_heads=2)
     w, model = make(hp, seed=9)
@@ -152,7 +153,8 @@ def test_flow_sample_cached_graph_and_reprepare():
     ctx = rng.standard_normal((21, 64)).astype(np.float32)
     ctx2 = torch.from_numpy(np.concatenate([ctx, ctx])).cuda()
     results = []
-    for c0 in (shell_coords(16, 5.5, 1.0), shell_coords(20, 7.0, 1.1)):
+    ca, cb = shell_coords(16, 5.5, 1.0), shell_coords(20, 7.0, 1.1)
+    for c0 in (ca, cb, ca, ca):
         model.prepare(torch.from_numpy(batched(c0, 2)).cuda(), 2, (20, 20, 20), np.array([0, 21, 42]))
         noise = rng.standard_normal((c0.shape[0], 8)).astype(np.float32)
         outs = []

@@ -217,6 +217,56 @@ def test_subm_conv3d(cin, cout):
     check(got, O.subm_conv3d(c, x, w, b, nb), what="conv vs oracle")
 
 
+@pytest.mark.parametrize("cin,cout,npts", [(64, 512, None), (128, 256, None), (64, 512, 100)])
+def test_subm_conv3d_pair_tiles(cin, cout, npts):
+    """Cout a multiple of 256 runs the CTA-pair kernel (two N = 256 MMAs per
+    pair tile when Cout % 512 == 0); 5,530 points leave the odd CTA of the last
+    pair partly empty, 100 points leave it empty."""
+    c = shell_coords(40, 14.0, 1.3)
+    if npts is not None:
+        c = np.ascontiguousarray(c[:npts])
+    x, w, b = _conv_case(c, cin, cout, cin * 7 + cout)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    got = o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out_dtype=torch.float32).cpu().numpy()
+    nb = O.neighbor_map27(c)
+    tight = O.subm_conv3d(c, rounded16(x), rounded16(w), b, nb)
+    check(got, tight, max_abs=1e-3, rel_l2=1e-4, what="pair conv vs f16-rounded fp32")
+    res = np.random.default_rng(2).standard_normal(tight.shape).astype(np.float32)
+    out = dev(res.copy())
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out, epilogue=L().EPI_RESIDUAL)
+    check(out.cpu().numpy(), res + tight, max_abs=1e-3, rel_l2=1e-4, what="pair conv residual")
+
+
+def test_linear_pair_kernel_subprocess():
+    """The CTA-pair kernel on dense linears (selected by P3D_GEMM_PAIR_DENSE=1,
+    read once per process, hence a child process): M below one CTA's 128 rows
+    (the odd CTA loads only zero-filled rows) and ragged last pairs."""
+    import subprocess
+    import sys
+    import os
+    code = r"""
+import math, numpy as np, torch
+from pixal3d.cpp_b200 import ops
+def h(a): return torch.from_numpy(np.ascontiguousarray(a.astype(np.float32))).cuda().half()
+def r16(a): return a.astype(np.float32).astype(np.float16).astype(np.float32)
+rng = np.random.default_rng(12)
+for m, n, k in ((100, 512, 128), (1000, 768, 256), (4133, 1024, 1024)):
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    y = ops.linear(h(x), h(w), torch.from_numpy(b).cuda(), out_dtype=torch.float32).cpu().numpy()
+    e = r16(x) @ r16(w).T + b
+    err = float(np.abs(y - e).max()); rel = float(np.linalg.norm(y - e) / np.linalg.norm(e))
+    assert err <= 1e-3 * max(1.0, float(np.abs(e).max())) and rel <= 1e-5, (m, n, k, err, rel)
+print("ok")
+"""
+    env = dict(os.environ, P3D_GEMM_PAIR_DENSE="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600,
+                       cwd=str(FX.GOLDEN.parent.parent))
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
 def test_subm_conv3d_residual_bf16():
     c = shell_coords(32, 10.0, 1.2)
     x, w, b = _conv_case(c, 64, 128, 9)
