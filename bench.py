@@ -19,6 +19,7 @@ gathers the results after it.  Rank 0 prints ONE JSON line.
 from __future__ import annotations
 
 import argparse
+import re
 import json
 import math
 import os
@@ -34,7 +35,9 @@ sys.path.insert(0, str(REPO))
 
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-TRAFFIC_FILE = REPO / "profiles" / "traffic.json"
+# ncu summary of the roofline kernel on this exact workload (one launch);
+# its "traffic_bytes_per_launch = N" line is dram read + write bytes.
+TRAFFIC_FILE = REPO / "profiles" / "gemm2_conv1024_fine_batch2.md"
 METRIC = "SLat flow steps/s @N=20k voxels (CFG batch 2, 24 blocks, C=1024)"
 
 # config-2 shapes
@@ -392,7 +395,8 @@ def run_ours(args):
         peak_t = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
         traffic = None
         if TRAFFIC_FILE.exists():
-            traffic = json.loads(TRAFFIC_FILE.read_text()).get("conv_c1024_batch2_bytes_per_launch")
+            mt = re.search(r"traffic_bytes_per_launch\s*=\s*(\d+)", TRAFFIC_FILE.read_text())
+            traffic = int(mt.group(1)) if mt else None
         c0_ms, c0_bytes, c0_flops = time_conv_cfg0(torch, ops)
         hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         result = {
