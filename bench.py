@@ -321,6 +321,7 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
+    from pixal3d.cpp_b200 import dist as D
     from pixal3d.cpp_b200 import ops
     from pixal3d.cpp_b200.flow import FlowModel, HParams
     from pixal3d.cpp_b200.workloads import shell_coords, batched
@@ -337,14 +338,13 @@ def run_ours(args):
     g = torch.Generator(device=dev)
     g.manual_seed(2024)
     cond = torch.randn((CTX_TOKENS, C), device=dev, generator=g)
-    if world > 1:
-        dist.broadcast(cond, src=0)
+    D.broadcast_(cond, src=0)
     ctx2 = torch.cat([cond, torch.zeros_like(cond)]).to(torch.float16)
 
     hp = HParams(in_channels=CH, out_channels=CH, model_channels=C, cond_channels=C, num_blocks=BLOCKS_RUN,
                  num_heads=HEADS, mlp_ratio=4.0, io_resblocks=2, groups=32, operand_dtype="f16")
     w = make_weights(torch, dev, seed=1234)
-    model = FlowModel(hp, w)
+    model = FlowModel(hp, w, device=local)
     del w
     torch.cuda.empty_cache()
     model.prepare(coords, 2, (RES, RES, RES), [0, CTX_TOKENS, 2 * CTX_TOKENS])
@@ -374,14 +374,9 @@ def run_ours(args):
     clk = clocks.stop()
     if world > 1:
         dist.barrier()
-    t = torch.tensor([ms_local], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = D.max_over_ranks(ms_local, dev)
     # NCCL gather of the sampled latents to rank 0 (outside the timed region)
-    if world > 1:
-        gathered = [torch.empty_like(x) for _ in range(world)] if rank == 0 else None
-        dist.gather(x, gathered, dst=0)
+    D.gather_rows(x, dst=0)
 
     value = world * args.steps / (ms_max / 1000.0)
     ms_per_step = ms_max / args.steps
@@ -477,11 +472,8 @@ def run_e2e(torch, model, img, cond, args, dev, world, rank):
     h_out.copy_(d_x, non_blocking=True)
     e1.record(s)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    from pixal3d.cpp_b200 import dist as D
+    ms = D.max_over_ranks(e0.elapsed_time(e1), dev)
     h2d = h_coords.numel() * 4 + h_noise.numel() * 4 + h_cond.numel() * 4
     return {"value": round(world * steps / (ms / 1000.0), 3), "unit": "steps/s",
             "h2d_bytes_per_step": int(h2d / steps), "d2h_bytes_per_step": int(h_out.numel() * 4 / steps),

@@ -67,7 +67,10 @@ typedef struct p3d_ctx p3d_ctx;
 
 /* Create a context on `device` using `stream` (cudaStream_t, may be NULL for
  * the legacy default stream).  No reference counterpart: replaces the
- * ggml backend/scheduler plumbing of src/backend.cpp for this path. */
+ * ggml backend/scheduler plumbing of src/backend.cpp for this path.
+ * The caller's current device is left unchanged.  Kernel entry points
+ * expect ctx's device to be current (as CUDA runtime calls do); the
+ * p3d_flow_* entry points make it current themselves for their duration. */
 int p3d_ctx_create(int device, void *stream, p3d_ctx **out);
 int p3d_ctx_destroy(p3d_ctx *ctx);
 int p3d_ctx_set_stream(p3d_ctx *ctx, void *stream);

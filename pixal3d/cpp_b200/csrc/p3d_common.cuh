@@ -37,6 +37,19 @@ int check_launch(p3d_ctx *ctx, const char *what);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Makes `device` current for the guard's scope and restores the caller's.
+struct DeviceGuard {
+    int prev = -1;
+    bool switched = false;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != device && cudaSetDevice(device) == cudaSuccess)
+            switched = true;
+    }
+    ~DeviceGuard() {
+        if (switched) cudaSetDevice(prev);
+    }
+};
+
 #define P3D_REQUIRE(ctx, cond, msg)                                                   \
     do {                                                                              \
         if (!(cond)) return ::p3d::set_error((ctx), P3D_ERR_INVALID, (msg));          \

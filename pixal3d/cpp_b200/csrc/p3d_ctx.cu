@@ -40,12 +40,19 @@ extern "C" int p3d_ctx_create(int device, void *stream, p3d_ctx **out) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return P3D_ERR_NO_DEVICE;
     if (prop.major != 10) return P3D_ERR_NO_DEVICE;  // built for sm_100a only
-    if (cudaSetDevice(device) != cudaSuccess) return P3D_ERR_CUDA;
+    // The fault flag lives on `device`; the caller's current device is restored.
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return P3D_ERR_CUDA;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return P3D_ERR_CUDA;
     p3d_ctx *ctx = new p3d_ctx();
     ctx->device = device;
     ctx->stream = static_cast<cudaStream_t>(stream);
     ctx->num_sms = prop.multiProcessorCount;
-    if (cudaMalloc(&ctx->fault, sizeof(int)) != cudaSuccess || cudaMemset(ctx->fault, 0, sizeof(int)) != cudaSuccess) {
+    const bool ok =
+        cudaMalloc(&ctx->fault, sizeof(int)) == cudaSuccess && cudaMemset(ctx->fault, 0, sizeof(int)) == cudaSuccess;
+    if (prev != device) cudaSetDevice(prev);
+    if (!ok) {
+        if (ctx->fault) cudaFree(ctx->fault);
         delete ctx;
         return P3D_ERR_CUDA;
     }

@@ -523,6 +523,7 @@ void p3d_flow::reset_topology() {
 
 extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out) {
     if (!ctx || !hp || !w || !out) return P3D_ERR_INVALID;
+    DeviceGuard dg(ctx->device);
     *out = nullptr;
     const int C = hp->model_channels;
     P3D_REQUIRE(ctx, C > 0 && hp->num_heads > 0 && C % hp->num_heads == 0 && C / hp->num_heads == 64,
@@ -628,6 +629,7 @@ extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p
 
 extern "C" int p3d_flow_destroy(p3d_flow *flow) {
     if (flow) {
+        DeviceGuard dg(flow->ctx->device);
         cudaStreamSynchronize(flow->stream);
         delete flow;
     }
@@ -638,6 +640,7 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
                                 const int64_t *ctx_offsets_host) {
     if (!f) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
+    DeviceGuard dg(ctx->device);
     P3D_REQUIRE(ctx, coords && ctx_offsets_host && n > 0 && batch > 0, "p3d_flow_prepare: bad argument");
     // Rebinding reuses the previous coordinate set's buffers where they are
     // large enough; the cached step graph survives only if no buffer moved and
@@ -789,6 +792,7 @@ extern "C" int p3d_flow_forward(p3d_flow *f, const float *x, const float *timest
                                 int ctx_dtype, const float *proj, float *out) {
     if (!f) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
+    DeviceGuard dg(ctx->device);
     P3D_REQUIRE(ctx, f->prepared, "p3d_flow_forward: call p3d_flow_prepare first");
     P3D_REQUIRE(ctx, x && timesteps && ctx_feats && out, "SLat flow input, timestep, or context shape mismatch");
     P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
@@ -800,6 +804,7 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
                                const p3d_sampler_config *cfg) {
     if (!f || !cfg) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
+    DeviceGuard dg(ctx->device);
     P3D_REQUIRE(ctx, f->prepared, "p3d_flow_sample: call p3d_flow_prepare first");
     P3D_REQUIRE(ctx, x && ctx_feats, "p3d_flow_sample: null pointer");
     P3D_REQUIRE(ctx, f->batch % 2 == 0, "p3d_flow_sample: batch must be 2 x images (conditional, unconditional)");

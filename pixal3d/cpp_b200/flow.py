@@ -72,9 +72,10 @@ def _ptr(t):
 class FlowModel:
     """Weights resident on one device; prepare() binds a coordinate set."""
 
-    def __init__(self, hp: HParams, weights: dict, device: int = 0):
+    def __init__(self, hp: HParams, weights: dict, device: int | None = None):
         self.hp = hp
-        self.device = device
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        device = self.device
         self._keep = []
         dev = torch.device("cuda", device)
 
