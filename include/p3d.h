@@ -83,6 +83,17 @@ int p3d_ctx_check(p3d_ctx *ctx);
 int64_t p3d_ctx_launch_count(const p3d_ctx *ctx);
 int p3d_version(void);
 
+/* Device buffers and copies on ctx's device and stream (the "device sparse
+ * tensor create/upload/download" of the boundary; no reference counterpart:
+ * the reference's tensors are host std::vectors).  p3d_copy_to_device is
+ * stream-ordered; p3d_copy_to_host returns after the data has arrived. */
+int p3d_device_alloc(p3d_ctx *ctx, size_t bytes, void **out);
+int p3d_device_free(p3d_ctx *ctx, void *ptr);
+int p3d_copy_to_device(p3d_ctx *ctx, void *dst, const void *src, size_t bytes);
+int p3d_copy_to_host(p3d_ctx *ctx, void *dst, const void *src, size_t bytes);
+/* Wait for ctx's stream, then report (and clear) a latched device fault. */
+int p3d_ctx_synchronize(p3d_ctx *ctx);
+
 /* ------------------------------------------------------ coordinates/hash */
 
 /* Table slots for n keys (power of two >= 2n).  Keys are uint64, values
@@ -110,6 +121,20 @@ size_t p3d_neighbor_map27_workspace(int64_t n);
  * p3d_neighbor_map27_workspace(n) bytes (256-byte aligned). */
 int p3d_neighbor_map27_ws(p3d_ctx *ctx, const int32_t *coords, int64_t n, void *ws, size_t ws_bytes,
                           int32_t *nbr_out);
+
+/* Device validity probe of a sparse tensor (SparseTensorF32::valid,
+ * src/sparse.cpp:261-335; VarLenTensorF32::valid's finiteness scan,
+ * :213-239 when coords is NULL).  Writes to *first_bad (device int64) the
+ * first failing row and check as (row << 2 | code), code 0 = coordinate
+ * outside [0,batch) x [0,sx) x [0,sy) x [0,sz), 1 = duplicate of an earlier
+ * row, 2 = batch index decreasing, 3 = non-finite feature; or a value
+ * >= 0x7F7F7F7F7F7F7F7F when the tensor is valid.  This is the error the
+ * reference's sequential scan reports.  feats may be NULL (coordinates
+ * only).  ws: p3d_sparse_validate_workspace(n) bytes, 256-byte aligned
+ * (unused when coords is NULL). */
+size_t p3d_sparse_validate_workspace(int64_t n);
+int p3d_sparse_validate(p3d_ctx *ctx, const int32_t *coords, int64_t n, const float *feats, int channels,
+                        int batch, int sx, int sy, int sz, void *ws, size_t ws_bytes, int64_t *first_bad);
 
 /* No counterpart in the reference.  The output of p3d_neighbor_map27_ws,
  * for callers that cannot allocate device memory: a device node inside a
@@ -241,6 +266,14 @@ int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads,
 int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, int head_dim, float freq_min,
                    float freq_base, float *table);
 
+/* Head-width repack (no reference counterpart; layout plumbing for head_dim
+ * below the attention kernel's 64): out[r][h][c] = x[r][h][c] for
+ * c < min(hd_in, hd_out), 0 for the rest of the hd_out columns, and the
+ * row padding out[r][heads*hd_out .. ldo) = 0 (whole rows of out written).
+ * x and out must not overlap. */
+int p3d_repack_heads(p3d_ctx *ctx, const void *x, int64_t ldx, int64_t n, int heads, int hd_in, int hd_out,
+                     void *out, int64_t ldo, int dtype);
+
 /* out = act(x) elementwise (gelu_tanh_in_place src/sparse_transformer.cpp:123-134;
  * silu src/slat_decoder.cpp:68-78).  dtype applies to x and out. */
 int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out);
@@ -257,10 +290,12 @@ int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int channels, i
  * pred = g*v_pos + (1-g)*v_neg (or v_pos when v_neg NULL), optional guidance
  * rescale (src/flow_sampler.cpp:200-241) with per-batch population std,
  * then x -= (t - t_next) * pred.  x, v_*: f32 [n][c]; stats scratch of
- * nbatch*4 doubles. */
+ * nbatch*4 doubles.  x0_out (optional, [n][c]): the step's predicted x0,
+ * pred_to_xstart(x, t, pred) (src/flow_sampler.cpp:139-147), for trajectories. */
 int p3d_euler_cfg_step(p3d_ctx *ctx, float *x, const float *v_pos, const float *v_neg, int64_t n,
                        int channels, const int32_t *batch_offsets, int nbatch, float t, float t_next,
-                       float guidance, float guidance_rescale, float sigma_min, double *stats);
+                       float guidance, float guidance_rescale, float sigma_min, double *stats,
+                       float *x0_out);
 
 /* Precision conversion between any two p3d_dtype element types. */
 int p3d_convert(p3d_ctx *ctx, const void *x, int x_dtype, int64_t count, void *out, int out_dtype);
@@ -307,6 +342,15 @@ typedef struct p3d_flow_weights {
 
 typedef struct p3d_flow p3d_flow;
 
+/* Timestep conditioning of the flow model (timestep_embedding +
+ * timestep_embed_mlp, src/flow.cpp:92-180, then SiLU and the adaLN
+ * modulation linear, src/slat_flow.cpp:208-222): tmod[b] (6*channels) from
+ * the model timestep timesteps[b].  f32 device weights: w0 [C][256], w2
+ * [C][C], mod_w [6C][C].  scratch: batch * (256 + 2 * channels) floats. */
+int p3d_timestep_mlp(p3d_ctx *ctx, const float *timesteps, int batch, int channels, const float *w0,
+                     const float *b0, const float *w2, const float *b2, const float *mod_w, const float *mod_b,
+                     float *scratch, float *tmod);
+
 /* Upload/convert weights into the device layout (16-bit GEMM operands).
  * Replaces SLatFlowModel::load's tensor upload (src/slat_flow.cpp:578-663). */
 int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out);
@@ -335,11 +379,13 @@ typedef struct p3d_sampler_config {
 
 /* SLatFlowModel::sample (src/slat_flow.cpp:1401-1447) with flow_euler_sample_f32
  * (src/flow_sampler.cpp:245-343) entirely on device.  The flow must have been
- * prepared with batch = 2*images: rows of image i appear as batch 2i
- * (conditional) and 2i+1 (unconditional, zeros condition), contiguous per
- * batch item, same coordinates.  ctx layout: conditional tokens of image i
- * in batch 2i, zeros (or anything; they are cleared) in 2i+1.
- * x: f32 [n/2 rows: image-major, the conditional copy's rows] in/out. */
+ * prepared with batch = 2*images: image i appears as batch item i
+ * (conditional) and again as item images + i (unconditional, zeros
+ * condition), with the same coordinates; rows contiguous per item.  ctx
+ * layout: conditional tokens of image i in item i; items images.. are
+ * cleared to zeros.  proj (proj mode): f32 [n/2][proj_in] for the
+ * conditional rows (the unconditional copy uses zeros).  x: f32 [n/2][in],
+ * the conditional rows, in/out. */
 int p3d_flow_sample(p3d_flow *flow, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
                     const p3d_sampler_config *cfg);
 /* Kernel launches one sampler step issued (forward + update), for reporting. */

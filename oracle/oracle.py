@@ -78,25 +78,41 @@ def coords_fingerprint(coords: np.ndarray) -> int:
     return h
 
 
+VALID_ERRORS = ("sparse coordinate is outside its shape", "sparse coordinates contain a duplicate point",
+                "sparse coordinates must be contiguous by batch", "sparse features contain a non-finite value")
+
+
+def validate_first(coords, feats, batch, shape) -> tuple[int, int] | None:
+    """First failing (row, check) of SparseTensorF32::valid's sequential scan
+    (src/sparse.cpp:286-334): for each row in order, 0 = outside the shape,
+    1 = same coordinate as an earlier row, 2 = batch index lower than the
+    previous row's, 3 = a non-finite feature.  None when every row passes."""
+    c = np.asarray(coords, np.int64).reshape(-1, 4)
+    n = c.shape[0]
+    code = np.full(n, 4, np.int64)
+    if n:
+        oob = (c[:, 0] < 0) | (c[:, 0] >= batch) | (c[:, 1] < 0) | (c[:, 1] >= shape[0]) | \
+              (c[:, 2] < 0) | (c[:, 2] >= shape[1]) | (c[:, 3] < 0) | (c[:, 3] >= shape[2])
+        _, first_idx, inv = np.unique(c, axis=0, return_index=True, return_inverse=True)
+        dup = first_idx[inv.ravel()] != np.arange(n)
+        dec = np.zeros(n, bool)
+        dec[1:] = c[:-1, 0] > c[1:, 0]
+        nonfinite = ~np.isfinite(np.asarray(feats, np.float32).reshape(n, -1)).all(axis=1) if feats is not None \
+            else np.zeros(n, bool)
+        for k, m in enumerate((oob, dup, dec, nonfinite)):
+            code[(code == 4) & m] = k
+    bad = np.nonzero(code < 4)[0]
+    return None if bad.size == 0 else (int(bad[0]), int(code[bad[0]]))
+
+
 def validate(coords, feats, batch, shape) -> str | None:
-    """SparseTensorF32::valid (src/sparse.cpp:241-335): shape, bounds,
-    duplicates, batch contiguity, finiteness.  Returns None or the reference's
-    error message."""
+    """SparseTensorF32::valid (src/sparse.cpp:241-335): shape, then the
+    sequential per-row scan of validate_first.  Returns None or the
+    reference's error message."""
     if batch <= 0 or feats.shape[1] <= 0 or min(shape) <= 0:
         return "invalid sparse tensor shape"
-    c = coords
-    if c.shape[0]:
-        if (c[:, 0] < 0).any() or (c[:, 0] >= batch).any() or (c[:, 1:] < 0).any() or \
-                (c[:, 1] >= shape[0]).any() or (c[:, 2] >= shape[1]).any() or (c[:, 3] >= shape[2]).any():
-            return "sparse coordinate is outside its shape"
-        keys = pack_keys(c)
-        if np.unique(keys).size != keys.size:
-            return "sparse coordinates contain a duplicate point"
-        if (np.diff(c[:, 0]) < 0).any():
-            return "sparse coordinates must be contiguous by batch"
-    if not np.isfinite(feats).all():
-        return "sparse features contain a non-finite value"
-    return None
+    r = validate_first(coords, feats, batch, shape)
+    return None if r is None else VALID_ERRORS[r[1]]
 
 
 # --------------------------------------------------------------------------

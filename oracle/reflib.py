@@ -65,6 +65,15 @@ def _shape(coords, batch, shape):
     return batch, shape
 
 
+def valid(coords, x, batch, shape) -> str | None:
+    """SparseTensorF32::valid: None or the reference's error message."""
+    coords, x = _c(coords, np.int32), _c(x, np.float32)
+    err = _err()
+    rc = lib().p3dref_valid(coords.ctypes, C.c_int64(coords.shape[0]), x.ctypes, x.shape[1], batch, *shape, err,
+                            len(err))
+    return None if rc == 0 else err.value.decode()
+
+
 def sparse_linear(coords, x, w, b, batch=None, shape=None):
     coords, x = _c(coords, np.int32), _c(x, np.float32)
     batch, shape = _shape(coords, batch, shape)

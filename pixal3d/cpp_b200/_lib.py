@@ -106,6 +106,13 @@ _sig("p3d_neighbor_map27", i32, vp, vp, i64, vp, vp, i64, vp)
 _sig("p3d_neighbor_map27_workspace", sz, i64)
 _sig("p3d_neighbor_map27_ws", i32, vp, vp, i64, vp, sz, vp)
 _sig("p3d_neighbor_map27_static", i32, vp, vp, i64, vp)
+_sig("p3d_sparse_validate_workspace", sz, i64)
+_sig("p3d_sparse_validate", i32, vp, vp, i64, vp, i32, i32, i32, i32, i32, vp, sz, vp)
+_sig("p3d_device_alloc", i32, vp, sz, vp)
+_sig("p3d_device_free", i32, vp, vp)
+_sig("p3d_copy_to_device", i32, vp, vp, vp, sz)
+_sig("p3d_copy_to_host", i32, vp, vp, vp, sz)
+_sig("p3d_ctx_synchronize", i32, vp)
 _sig("p3d_downsample_grid_ints", i64, i32, i32, i32, i32, i32)
 _sig("p3d_downsample_topology", i32, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp)
 _sig("p3d_downsample_mean", i32, vp, vp, i64, i32, i32, vp, i32, vp)
@@ -121,8 +128,10 @@ _sig("p3d_qk_rmsnorm_rope", i32, vp, vp, i64, i64, i32, i32, vp, vp, f32, f32, i
 _sig("p3d_linear_headnorm", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i64, vp, i64, vp)
 _sig("p3d_rope_table", i32, vp, vp, i64, i32, f32, f32, vp)
 _sig("p3d_activation", i32, vp, vp, i64, i32, i32, vp)
+_sig("p3d_repack_heads", i32, vp, vp, i64, i64, i32, i32, i32, vp, i64, i32)
+_sig("p3d_timestep_mlp", i32, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp)
 _sig("p3d_group_norm_silu", i32, vp, vp, i64, i32, i32, f32, vp, vp, vp, i32, i32, vp, vp, i32)
-_sig("p3d_euler_cfg_step", i32, vp, vp, vp, vp, i64, i32, vp, i32, f32, f32, f32, f32, f32, vp)
+_sig("p3d_euler_cfg_step", i32, vp, vp, vp, vp, i64, i32, vp, i32, f32, f32, f32, f32, f32, vp, vp)
 _sig("p3d_convert", i32, vp, vp, i32, i64, vp, i32)
 
 OPTIONAL = {}

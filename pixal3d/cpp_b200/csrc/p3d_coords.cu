@@ -63,6 +63,27 @@ __global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, u
     latch_fault(fault, P3D_ERR_HASH_FULL);
 }
 
+// Validation insert: every row inserts its key; the slot's value ends as the
+// smallest row index holding that key (vals pre-filled with INT32_MAX).
+__global__ void validate_insert_kernel(const int4 *__restrict__ coords, int64_t n, uint64_t *keys, int32_t *vals,
+                                       uint64_t mask, int *fault) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int4 c = coords[i];
+    const uint64_t key = pack_key(c.x, c.y, c.z, c.w);
+    uint64_t slot = mix64(key) & mask;
+    for (int probe = 0; probe < kMaxProbes; ++probe) {
+        const unsigned long long prev =
+            atomicCAS(reinterpret_cast<unsigned long long *>(keys + slot), kEmpty, static_cast<unsigned long long>(key));
+        if (prev == kEmpty || prev == key) {
+            atomicMin(vals + slot, static_cast<int32_t>(i));
+            return;
+        }
+        slot = (slot + 1) & mask;
+    }
+    latch_fault(fault, P3D_ERR_HASH_FULL);
+}
+
 __device__ __forceinline__ int32_t hash_find(const uint64_t *__restrict__ keys, const int32_t *__restrict__ vals,
                                              uint64_t mask, uint64_t key, int32_t miss) {
     uint64_t slot = mix64(key) & mask;
@@ -324,6 +345,78 @@ extern "C" int p3d_neighbor_map27(p3d_ctx *ctx, const int32_t *coords, int64_t n
 extern "C" size_t p3d_neighbor_map27_workspace(int64_t n) {
     const int64_t cap = p3d_coord_hash_capacity(n);
     return static_cast<size_t>(cap) * 8 + static_cast<size_t>(cap) * 4 + 256;
+}
+
+namespace p3d {
+namespace {
+// Per row, the first failing check in the order SparseTensorF32::valid
+// applies them (src/sparse.cpp:286-308): 0 outside the shape, 1 duplicate of
+// an earlier row, 2 batch index decreasing; folded into *first as
+// (row << 2 | code) by atomicMin, so *first ends as the reference's first
+// error.  Finiteness (code 3) is folded in by validate_finite_kernel.
+__global__ void validate_points_kernel(const int4 *__restrict__ coords, int64_t n, int batch, int sx, int sy, int sz,
+                                       const uint64_t *__restrict__ keys, const int32_t *__restrict__ vals,
+                                       uint64_t mask, unsigned long long *first) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int4 c = coords[i];
+    int code = -1;
+    if (c.x < 0 || c.x >= batch || c.y < 0 || c.y >= sx || c.z < 0 || c.z >= sy || c.w < 0 || c.w >= sz) {
+        code = 0;
+    } else if (hash_find(keys, vals, mask, pack_key(c.x, c.y, c.z, c.w), -1) != static_cast<int32_t>(i)) {
+        code = 1;
+    } else if (i > 0 && coords[i - 1].x > c.x) {
+        code = 2;
+    }
+    if (code >= 0) atomicMin(first, (static_cast<unsigned long long>(i) << 2) | static_cast<unsigned long long>(code));
+}
+
+__global__ void validate_finite_kernel(const float *__restrict__ x, int64_t count, int channels,
+                                       unsigned long long *first) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= count) return;
+    if (!isfinite(x[e])) atomicMin(first, (static_cast<unsigned long long>(e / channels) << 2) | 3ull);
+}
+}  // namespace
+}  // namespace p3d
+
+extern "C" size_t p3d_sparse_validate_workspace(int64_t n) { return p3d_neighbor_map27_workspace(n); }
+
+extern "C" int p3d_sparse_validate(p3d_ctx *ctx, const int32_t *coords, int64_t n, const float *feats, int channels,
+                                   int batch, int sx, int sy, int sz, void *ws, size_t ws_bytes, int64_t *first_bad) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, first_bad && n >= 0 && channels > 0, "p3d_sparse_validate: bad argument");
+    P3D_REQUIRE(ctx, !feats || n < (int64_t(1) << 60) / channels, "p3d_sparse_validate: too many values");
+    unsigned long long *first = reinterpret_cast<unsigned long long *>(first_bad);
+    P3D_CUDA(ctx, cudaMemsetAsync(first, 0x7F, sizeof(int64_t), ctx->stream));  // 0x7F7F... = no error
+    if (n == 0) return P3D_OK;
+    if (coords) {
+        P3D_REQUIRE(ctx, ws && (reinterpret_cast<uintptr_t>(ws) & 255) == 0 &&
+                             ws_bytes >= p3d_sparse_validate_workspace(n),
+                    "p3d_sparse_validate: workspace too small or not 256-byte aligned");
+        P3D_REQUIRE(ctx, n < (int64_t(1) << 31), "p3d_sparse_validate: too many points");
+        const int64_t cap = p3d_coord_hash_capacity(n);
+        uint64_t *keys = static_cast<uint64_t *>(ws);
+        int32_t *vals = reinterpret_cast<int32_t *>(keys + cap);
+        fill_u64_kernel<<<blocks_for(cap, 256), 256, 0, ctx->stream>>>(keys, cap, kEmpty);
+        int rc = check_launch(ctx, "fill_u64");
+        if (rc) return rc;
+        fill_i32_kernel<<<blocks_for(cap, 256), 256, 0, ctx->stream>>>(vals, cap, 0x7FFFFFFF);
+        if ((rc = check_launch(ctx, "fill_i32"))) return rc;
+        const int4 *c4 = reinterpret_cast<const int4 *>(coords);
+        validate_insert_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(c4, n, keys, vals,
+                                                                            static_cast<uint64_t>(cap - 1), ctx->fault);
+        if ((rc = check_launch(ctx, "validate_insert"))) return rc;
+        validate_points_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(
+            c4, n, batch, sx, sy, sz, keys, vals, static_cast<uint64_t>(cap - 1), first);
+        if ((rc = check_launch(ctx, "validate_points"))) return rc;
+    }
+    if (feats) {
+        const int64_t count = n * channels;
+        validate_finite_kernel<<<blocks_for(count, 256), 256, 0, ctx->stream>>>(feats, count, channels, first);
+        return check_launch(ctx, "validate_finite");
+    }
+    return P3D_OK;
 }
 
 extern "C" int p3d_neighbor_map27_ws(p3d_ctx *ctx, const int32_t *coords, int64_t n, void *ws, size_t ws_bytes,

@@ -107,3 +107,46 @@ extern "C" int p3d_convert(p3d_ctx *ctx, const void *x, int x_dtype, int64_t cou
                                                               static_cast<const TI *>(x), count, static_cast<TO *>(out))));
     return check_launch(ctx, "convert");
 }
+
+extern "C" int p3d_device_alloc(p3d_ctx *ctx, size_t bytes, void **out) {
+    if (!ctx || !out) return P3D_ERR_INVALID;
+    *out = nullptr;
+    if (bytes == 0) bytes = 1;
+    DeviceGuard dg(ctx->device);
+    P3D_CUDA(ctx, cudaMalloc(out, bytes));
+    return P3D_OK;
+}
+
+extern "C" int p3d_device_free(p3d_ctx *ctx, void *ptr) {
+    if (!ctx) return P3D_ERR_INVALID;
+    if (!ptr) return P3D_OK;
+    DeviceGuard dg(ctx->device);
+    P3D_CUDA(ctx, cudaFree(ptr));
+    return P3D_OK;
+}
+
+extern "C" int p3d_copy_to_device(p3d_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    if (!ctx) return P3D_ERR_INVALID;
+    if (bytes == 0) return P3D_OK;
+    P3D_REQUIRE(ctx, dst && src, "p3d_copy_to_device: null pointer");
+    DeviceGuard dg(ctx->device);
+    P3D_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return P3D_OK;
+}
+
+extern "C" int p3d_copy_to_host(p3d_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    if (!ctx) return P3D_ERR_INVALID;
+    if (bytes == 0) return P3D_OK;
+    P3D_REQUIRE(ctx, dst && src, "p3d_copy_to_host: null pointer");
+    DeviceGuard dg(ctx->device);
+    P3D_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return P3D_OK;
+}
+
+extern "C" int p3d_ctx_synchronize(p3d_ctx *ctx) {
+    if (!ctx) return P3D_ERR_INVALID;
+    DeviceGuard dg(ctx->device);
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return p3d_ctx_check(ctx);
+}

@@ -202,6 +202,24 @@ __global__ void rope_table_kernel(const int4 *__restrict__ coords, int64_t n, in
     table[i] = make_float2(cs, sn);
 }
 
+// out[row][h][c] = c < hd_in ? x[row][h][c] : 0 for c < hd_out, and the
+// row's pitch padding [heads*hd_out, ldo) = 0: moves heads between head
+// widths (e.g. head_dim 6 <-> the attention kernel's 64).
+template <typename T>
+__global__ void repack_heads_kernel(const T *__restrict__ x, int64_t ldx, int64_t n, int heads, int hd_in,
+                                    int hd_out, T *__restrict__ out, int64_t ldo) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * ldo) return;
+    const int64_t row = i / ldo;
+    const int64_t r = i - row * ldo;
+    T v = from_f32<T>(0.0f);
+    if (r < static_cast<int64_t>(heads) * hd_out) {
+        const int h = static_cast<int>(r / hd_out), c = static_cast<int>(r - static_cast<int64_t>(h) * hd_out);
+        if (c < hd_in) v = x[row * ldx + static_cast<int64_t>(h) * hd_in + c];
+    }
+    out[i] = v;
+}
+
 // ------------------------------------------------------------ activations
 template <typename T>
 __global__ void activation_kernel(const T *__restrict__ x, int64_t n, int act, T *__restrict__ out) {
@@ -343,7 +361,8 @@ __global__ void cfg_rescale_stats_kernel(const float *__restrict__ x, const floa
 
 __global__ void euler_cfg_kernel(float *__restrict__ x, const float *__restrict__ vp, const float *__restrict__ vn,
                                  int64_t n, int C, const int32_t *__restrict__ offsets, int nbatch, float t, float dt,
-                                 float g, float gr, float sigma_min, const double *__restrict__ stats) {
+                                 float g, float gr, float sigma_min, const double *__restrict__ stats,
+                                 float *__restrict__ x0_out) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n * C) return;
     const float p = vp[i];
@@ -361,6 +380,11 @@ __global__ void euler_cfg_kernel(float *__restrict__ x, const float *__restrict_
         float x0 = a * x[i] - bb * pred;
         x0 = gr * (x0 * ratio) + (1.0f - gr) * x0;
         pred = (a * x[i] - x0) / bb;
+    }
+    if (x0_out) {
+        // pred_to_xstart (src/flow_sampler.cpp:139-147) of the final prediction
+        const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+        x0_out[i] = a * x[i] - bb * pred;
     }
     x[i] -= dt * pred;
 }
@@ -445,6 +469,21 @@ extern "C" int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, in
     return check_launch(ctx, "rope_table");
 }
 
+extern "C" int p3d_repack_heads(p3d_ctx *ctx, const void *x, int64_t ldx, int64_t n, int heads, int hd_in,
+                                int hd_out, void *out, int64_t ldo, int dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && x != out && heads > 0 && hd_in > 0 && hd_out > 0 && n >= 0,
+                "p3d_repack_heads: bad argument");
+    P3D_REQUIRE(ctx, ldx >= static_cast<int64_t>(heads) * hd_in && ldo >= static_cast<int64_t>(heads) * hd_out,
+                "p3d_repack_heads: row pitch too small");
+    const int64_t count = n * ldo;
+    if (count == 0) return P3D_OK;
+    P3D_DISPATCH(dtype, T,
+                 repack_heads_kernel<T><<<blocks_for(count, 256), 256, 0, ctx->stream>>>(
+                     static_cast<const T *>(x), ldx, n, heads, hd_in, hd_out, static_cast<T *>(out), ldo));
+    return check_launch(ctx, "repack_heads");
+}
+
 extern "C" int p3d_activation(p3d_ctx *ctx, const void *x, int64_t count, int act, int dtype, void *out) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && out && (act == P3D_EPI_GELU_TANH || act == P3D_EPI_SILU), "p3d_activation: bad argument");
@@ -485,7 +524,7 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
 
 extern "C" int p3d_euler_cfg_step(p3d_ctx *ctx, float *x, const float *v_pos, const float *v_neg, int64_t n,
                                   int channels, const int32_t *batch_offsets, int nbatch, float t, float t_next,
-                                  float guidance, float guidance_rescale, float sigma_min, double *stats) {
+                                  float guidance, float guidance_rescale, float sigma_min, double *stats, float *x0_out) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && v_pos && channels > 0, "p3d_euler_cfg_step: bad argument");
     const bool rescale = v_neg && guidance_rescale > 0.0f;
@@ -502,6 +541,6 @@ extern "C" int p3d_euler_cfg_step(p3d_ctx *ctx, float *x, const float *v_pos, co
     }
     euler_cfg_kernel<<<blocks_for(n * channels, 256), 256, 0, ctx->stream>>>(
         x, v_pos, v_neg, n, channels, batch_offsets, nbatch, t, t - t_next, guidance, guidance_rescale, sigma_min,
-        rescale ? stats : nullptr);
+        rescale ? stats : nullptr, x0_out);
     return check_launch(ctx, "euler_cfg");
 }

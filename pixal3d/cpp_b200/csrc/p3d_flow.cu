@@ -219,11 +219,6 @@ __global__ void euler_sched_kernel(float *__restrict__ x, const float *__restric
 
 __global__ void advance_kernel(int *counter) { *counter += 1; }
 
-__global__ void zero_f32_rows_kernel(float *p, int64_t count) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < count) p[i] = 0.0f;
-}
-
 }  // namespace
 }  // namespace p3d
 
@@ -519,6 +514,22 @@ void p3d_flow::reset_topology() {
     hash_ws = down_grid = nullptr;
     down_m = nullptr;
     h_trunk_off.clear();
+}
+
+extern "C" int p3d_timestep_mlp(p3d_ctx *ctx, const float *timesteps, int batch, int channels, const float *w0,
+                                const float *b0, const float *w2, const float *b2, const float *mod_w,
+                                const float *mod_b, float *scratch, float *tmod) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, timesteps && w0 && b0 && w2 && b2 && mod_w && mod_b && scratch && tmod && batch > 0 &&
+                         channels > 0,
+                "p3d_timestep_mlp: bad argument");
+    DeviceGuard dg(ctx->device);
+    float *freq = scratch, *t1 = scratch + static_cast<int64_t>(batch) * 256, *t2 = t1 + static_cast<int64_t>(batch) * channels;
+    temb_freq_kernel<<<batch, 128, 0, ctx->stream>>>(timesteps, 1, nullptr, 1.0f, batch, 256, freq);
+    P3D_TRY(check_launch(ctx, "temb_freq"));
+    P3D_TRY(small_linear(ctx, freq, batch, 256, w0, b0, channels, t1, 0, 1));
+    P3D_TRY(small_linear(ctx, t1, batch, channels, w2, b2, channels, t2, 0, 0));
+    return small_linear(ctx, t2, batch, channels, mod_w, mod_b, 6 * channels, tmod, 2, 0);
 }
 
 extern "C" int p3d_flow_create(p3d_ctx *ctx, const p3d_flow_hparams *hp, const p3d_flow_weights *w, p3d_flow **out) {

@@ -95,6 +95,24 @@ def neighbor_map27(coords: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def sparse_validate(coords: torch.Tensor, feats: torch.Tensor | None, batch: int, spatial) -> tuple[int, int] | None:
+    """Device validity probe (SparseTensorF32::valid): None, or the first
+    failing (row, check) with check 0 outside the shape, 1 duplicate, 2 batch
+    order, 3 non-finite feature."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    ws_bytes = int(L.lib.p3d_sparse_validate_workspace(n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=coords.device)
+    first = torch.empty(1, dtype=torch.int64, device=coords.device)
+    ch = feats.shape[1] if feats is not None else 1
+    c.check(L.lib.p3d_sparse_validate(c.h, _p(coords), n, _p(feats), ch, batch, *spatial, _p(ws), ws_bytes,
+                                      _p(first)))
+    v = int(first.item())
+    if v >= 0x7F7F7F7F7F7F7F7F:
+        return None
+    return v >> 2, v & 3
+
+
 def downsample_topology(coords: torch.Tensor, batch: int, shape, factor: int = 2):
     """Parents of sparse_downsample_mean (src/sparse.cpp:536-602).
     Returns (out_coords [m,4], parent [n], child [m, f^3], m)."""
@@ -284,13 +302,14 @@ def group_norm_silu(x: torch.Tensor, groups: int, eps: float, gamma, beta, batch
 
 
 def euler_cfg_step(x: torch.Tensor, v_pos: torch.Tensor, v_neg: torch.Tensor | None, batch_offsets: torch.Tensor,
-                   t: float, t_next: float, guidance: float, guidance_rescale: float, sigma_min: float) -> None:
+                   t: float, t_next: float, guidance: float, guidance_rescale: float, sigma_min: float,
+                   x0_out: torch.Tensor | None = None) -> None:
     c = ctx(x.device)
     n, ch = x.shape
     nb = batch_offsets.shape[0] - 1
     stats = torch.empty(4 * nb, dtype=torch.float64, device=x.device)
     c.check(L.lib.p3d_euler_cfg_step(c.h, _p(x), _p(v_pos), _p(v_neg), n, ch, _p(batch_offsets), nb, t, t_next,
-                                     guidance, guidance_rescale, sigma_min, _p(stats)))
+                                     guidance, guidance_rescale, sigma_min, _p(stats), _p(x0_out)))
 
 
 def convert(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:

@@ -1,0 +1,175 @@
+"""The B200 build of the reference's C++ API (include/pixal3d/sparse.h,
+sparse_transformer.h, flow_sampler.h, slat_flow.h) on the reference's own
+numeric fixtures: tests/cpp/host_api_check.cpp makes the same calls as the
+reference's tests/*_numeric_fixture.cpp, linked against libpixal3d_b200.so,
+and its outputs are compared with the fixture outputs the reference printed
+(tests/golden/).  Tolerance: the north-star bound (max-abs 2e-2, relative-L2
+5e-3) for 16-bit-operand kernels; 1e-5 relative for the f32 sampler math.
+"""
+import struct
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from tests import _fixtures as FX
+
+pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parent.parent
+PKG = REPO / "pixal3d" / "cpp_b200"
+
+
+def _write(path, arrays):
+    with open(path, "wb") as f:
+        for name, a in arrays.items():
+            a = np.ascontiguousarray(a)
+            t = {np.dtype(np.float32): 0, np.dtype(np.int32): 1, np.dtype(np.int64): 2}[a.dtype]
+            nb = name.encode()
+            f.write(struct.pack("<I", len(nb)) + nb + struct.pack("<BQ", t, a.size))
+            f.write(a.tobytes())
+
+
+def _read(path):
+    out = {}
+    data = Path(path).read_bytes()
+    i = 0
+    while i < len(data):
+        (ln,) = struct.unpack_from("<I", data, i)
+        i += 4
+        name = data[i:i + ln].decode()
+        i += ln
+        t, count = struct.unpack_from("<BQ", data, i)
+        i += 9
+        assert t == 0
+        out[name] = np.frombuffer(data, np.float32, count, i).copy()
+        i += 4 * count
+    return out
+
+
+def _inputs():
+    a = {}
+    d = FX.sparse_fixture()
+    for k in ("coords", "x", "lin_w", "lin_b", "conv_w", "conv_b", "gamma", "beta", "q", "k", "v", "rms_gamma",
+              "ctx_k", "ctx_v", "packed_coords", "packed", "subdiv"):
+        a["sp." + k] = d[k].astype(np.int32 if k.endswith("coords") else np.float32)
+    C = 12
+    for k, v in FX.block_params("", C, 5, 7, 18).items():
+        a["blk.w." + k] = v.astype(np.float32)
+    a["blk.x"] = FX.seq(120, -0.27, 0.013)
+    a["blk.proj"] = FX.seq(70, 0.19, -0.017)
+    a["blk.ctx"] = FX.seq(25, -0.11, 0.021)
+    a["blk.tmod"] = FX.seq(2 * 6 * C, 0.07, -0.009)
+    w, inp = FX.flow_fixture()
+    for k, v in w.items():
+        if k != "blocks":
+            a["fl." + k] = v.astype(np.float32)
+    for k, v in w["blocks"][0].items():
+        a["fl.b0." + k] = v.astype(np.float32)
+    for k in ("x", "proj", "ctx", "timesteps"):
+        a["fl." + k] = inp[k].astype(np.float32)
+    # a model shape served by the device-resident flow (64-wide heads)
+    from tests._models import random_flow_weights
+    from oracle import oracle as O
+    from pixal3d.cpp_b200.workloads import shell_coords
+    hp = _device_hp()
+    bw = random_flow_weights(np.random.default_rng(5), hp)
+    for k, v in bw.items():
+        if k != "blocks":
+            a["bf." + k] = np.asarray(v, np.float32)
+    for i, b in enumerate(bw["blocks"]):
+        for k, v in b.items():
+            a[f"bf.b{i}." + k] = np.asarray(v, np.float32)
+    rng = np.random.default_rng(6)
+    a["bf.hparams"] = np.array([8, 8, 128, 64, 2, 4.0, 16], np.float32)
+    a["bf.coords"] = shell_coords(16, 5.5, 1.0)
+    a["bf.noise"] = rng.standard_normal((a["bf.coords"].shape[0], 8)).astype(np.float32)
+    a["bf.ctx"] = rng.standard_normal((33, 64)).astype(np.float32)
+    a["bf.timestep"] = np.array([640.0], np.float32)
+    a["fs.coords"] = np.array([[0, 0, 0, 0], [0, 0, 1, 0], [0, 2, 1, 1], [1, 0, 0, 1], [1, 1, 2, 0]], np.int32)
+    a["fs.noise"] = FX.seq(15, -0.73, 0.091)
+    return a
+
+
+def _device_hp():
+    from oracle import oracle as O
+    return O.FlowHParams(in_channels=8, out_channels=8, model_channels=128, cond_channels=64, num_blocks=2,
+                         num_heads=2)
+
+
+@pytest.fixture(scope="module")
+def harness(tmp_path_factory):
+    d = tmp_path_factory.mktemp("host_api")
+    exe = d / "host_api_check"
+    cmd = ["g++", "-O2", "-std=c++17", f"-I{PKG / 'host' / 'include'}", str(REPO / "tests" / "cpp" / "host_api_check.cpp"),
+           f"-L{PKG}", "-lpixal3d_b200", "-lp3dcuda", f"-Wl,-rpath,{PKG}", "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    _write(d / "in.bin", _inputs())
+    r = subprocess.run([str(exe), str(d / "in.bin"), str(d / "out.bin")], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return _read(d / "out.bin")
+
+
+def _close(got, exp, what, max_abs=2e-2, rel_l2=5e-3):
+    got = np.asarray(got, np.float64)
+    exp = np.asarray(exp, np.float64)
+    assert got.shape == exp.shape, (what, got.shape, exp.shape)
+    mx = float(np.abs(got - exp).max())
+    rl = float(np.linalg.norm(got - exp) / max(np.linalg.norm(exp), 1e-30))
+    assert mx <= max_abs and rl <= rel_l2, f"{what}: max_abs {mx:.3e} rel_l2 {rl:.3e}"
+
+
+def test_sparse_operators_match_reference_fixture(harness):
+    g = FX.parse_golden("sparse_numeric_fixture")
+    for k in ("sparse_linear_output", "sparse_conv_output", "sparse_norm_output", "sparse_downsample_output",
+              "sparse_attention_output", "sparse_rope_output", "sparse_rms_output", "sparse_cross_output",
+              "sparse_channel_to_spatial_output"):
+        _close(harness[k], g[k], k)
+    for k in ("sparse_downsample_coords", "sparse_channel_to_spatial_coords"):
+        np.testing.assert_array_equal(harness[k], g[k])
+
+
+def test_transformer_block_matches_reference_fixture(harness):
+    g = FX.parse_golden("sparse_transformer_numeric_fixture")
+    _close(harness["sparse_transformer_output"], g["sparse_transformer_output"], "block")
+
+
+def test_slat_flow_matches_reference_fixture(harness):
+    g = FX.parse_golden("slat_flow_numeric_fixture")
+    np.testing.assert_array_equal(harness["slat_flow_coords"], g["slat_flow_coords"])
+    _close(harness["slat_flow_output"], g["slat_flow_output"], "flow forward")
+    _close(harness["slat_flow_model_forward"], g["slat_flow_output"], "SLatFlowModel::forward")
+    _close(harness["slat_flow_sample_direct"], g["slat_flow_sample_direct"], "sample (trajectory loop)")
+    _close(harness["slat_flow_sample_direct_x0_last"], g["slat_flow_sample_direct_x0_last"], "sample x0")
+    _close(harness["slat_flow_sample_device"], g["slat_flow_sample_direct"], "sample (device loop)")
+
+
+def test_flow_sampler_matches_reference_fixture(harness):
+    g = FX.parse_golden("flow_sampler_numeric_fixture")
+    scale = max(1.0, float(np.abs(g["flow_sampler_samples"]).max()))
+    for k in ("flow_sampler_samples", "flow_sampler_pred_x_t_last", "flow_sampler_pred_x_0_last"):
+        _close(harness[k], g[k], k, max_abs=1e-5 * scale, rel_l2=1e-5)
+
+
+def test_device_resident_flow_through_host_api(harness):
+    """SLatFlowModel::forward / ::sample on a model the device-resident flow
+    serves (C = 128, 64-wide heads): batched-CFG device sampler == the
+    oracle's flow_euler_sample with the zero condition."""
+    from oracle import oracle as O
+    from tests._models import random_flow_weights
+    a = _inputs()
+    hp = _device_hp()
+    w = random_flow_weights(np.random.default_rng(5), hp)
+    c, x, ctx = a["bf.coords"], a["bf.noise"], a["bf.ctx"]
+    one = np.array([0, ctx.shape[0]], np.int64)
+    exp = O.slat_flow_forward(c, x, a["bf.timestep"], one, ctx, None, hp, w)
+    _close(harness["device_flow_forward"], exp.ravel(), "device forward")
+    sc = O.SamplerConfig(steps=4, guidance_strength=3.0, rescale_t=3.0)
+    zctx = np.zeros_like(ctx)
+
+    def model(state, t, cond):
+        return O.slat_flow_forward(c, state, np.array([t], np.float32), one, ctx if cond else zctx, None, hp, w)
+
+    exp_s = O.flow_euler_sample(x, sc, model, c[:, 0].astype(np.int64), 1)
+    _close(harness["device_flow_sample"], exp_s.ravel(), "device sample")

@@ -105,6 +105,34 @@ def test_neighbor_map_edge_cases():
     assert e.value.status == L().P3D_ERR_DUPLICATE
 
 
+def test_sparse_validate_matches_reference_order():
+    """Device validity probe == the reference's sequential scan (first failing
+    row and check) on crafted cases and on the config-0 shell with failures
+    planted at random rows."""
+    from tests.test_oracle_pin import validity_cases
+    o = ops()
+    for name, c, x in validity_cases():
+        got = o.sparse_validate(dev(c), dev(x), 2, (4, 4, 4))
+        assert got == O.validate_first(c, x, 2, (4, 4, 4)), name
+    rng = np.random.default_rng(3)
+    shell = batched(shell_coords(), 2)
+    n = shell.shape[0]
+    x = rng.standard_normal((n, 5)).astype(np.float32)
+    assert o.sparse_validate(dev(shell), dev(x), 2, (64, 64, 64)) is None
+    for trial in range(6):
+        c = shell.copy()
+        xx = x.copy()
+        rows = rng.choice(n, 3, replace=False)
+        c[rows[0], 1 + trial % 3] = 64 + trial            # outside the shape
+        c[rows[1]] = c[rng.integers(0, n)]                # duplicate (or itself: no-op)
+        xx[rows[2], trial % 5] = np.nan                   # non-finite
+        got = o.sparse_validate(dev(c), dev(xx), 2, (64, 64, 64))
+        assert got == O.validate_first(c, xx, 2, (64, 64, 64)), (trial, got)
+    # coordinates only / features only
+    assert o.sparse_validate(dev(shell), None, 2, (64, 64, 64)) is None
+    assert o.sparse_validate(dev(shell), None, 1, (64, 64, 64)) == O.validate_first(shell, None, 1, (64, 64, 64))
+
+
 def test_downsample_bitexact():
     o = ops()
     v = np.load(FX.GOLDEN / "ref_vectors.npz")
@@ -432,9 +460,12 @@ def test_euler_cfg_step(g, gr):
     exp = x - (t - tn) * pred
     o = ops()
     xt = dev(x.copy())
+    x0 = torch.empty_like(xt)
     o.euler_cfg_step(xt, dev(vp), dev(vn) if g != 1.0 else None, o.batch_offsets_of(dev(c), 2), float(t), float(tn),
-                     g, gr, 0.031)
+                     g, gr, 0.031, x0_out=x0)
     check(xt.cpu().numpy(), exp, max_abs=1e-5, rel_l2=1e-6, what="euler/cfg")
+    a = np.float32(1 - 0.031)
+    check(x0.cpu().numpy(), a * x - (np.float32(0.031) + a * t) * pred, max_abs=1e-5, rel_l2=1e-6, what="x0 out")
 
 
 # ------------------------------------------------------ f16 operand variants

@@ -229,3 +229,31 @@ def test_live_reference_ops():
     rc, rf, _ = reflib.downsample_mean(c, x, 2)
     np.testing.assert_array_equal(oc, rc)
     close(of, rf, SPARSE_TOL)
+
+
+def validity_cases():
+    """Valid and invalid sparse tensors, including rows that fail different
+    checks in different orders (the first failing row decides the error)."""
+    rng = np.random.default_rng(21)
+    base = FX.TEN_COORDS.copy()
+    x = rng.standard_normal((10, 3)).astype(np.float32)
+    cases = [("valid", base, x)]
+    c = base.copy(); c[6] = c[2]
+    cases.append(("duplicate", c, x))
+    c = base.copy(); c[4, 2] = 9
+    cases.append(("outside", c, x))
+    c = base.copy(); c[3] = [1, 3, 3, 3]; c[4] = [0, 3, 2, 1]
+    cases.append(("batch order", c, x))
+    xx = x.copy(); xx[5, 1] = np.nan
+    cases.append(("nan", base, xx))
+    c = base.copy(); c[7, 3] = -1; c[5] = c[1]; xx = x.copy(); xx[2, 0] = np.inf
+    cases.append(("inf before duplicate before outside", c, xx))
+    c = base.copy(); c[2, 1] = 99; c[8] = c[0]
+    cases.append(("outside before duplicate", c, x))
+    return cases
+
+
+@needs_ref
+def test_validate_matches_reference():
+    for name, c, x in validity_cases():
+        assert O.validate(c, x, 2, (4, 4, 4)) == reflib.valid(c, x, 2, (4, 4, 4)), name
