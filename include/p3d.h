@@ -266,6 +266,16 @@ int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads,
 int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, int head_dim, float freq_min,
                    float freq_base, float *table);
 
+/* LayerNorm (+affine when gamma/beta) (+SiLU when silu != 0) written to an
+ * operand of row pitch ld_out >= channels, padding columns zeroed
+ * (sparse_layer_norm + silu_in_place, src/sparse.cpp:490-534,
+ * src/slat_decoder.cpp:68-78).  x f32 [n][channels]. */
+int p3d_layernorm_act(p3d_ctx *ctx, const float *x, int64_t n, int channels, float eps, const float *gamma,
+                      const float *beta, int silu, void *out, int64_t ld_out, int out_dtype);
+/* f32 [rows][cols] -> out_dtype [rows][ld] (ld >= cols, padding zeroed): the
+ * 16-bit GEMM operand layout.  No reference counterpart (layout plumbing). */
+int p3d_pack_operand(p3d_ctx *ctx, const float *x, int64_t rows, int cols, void *out, int64_t ld, int out_dtype);
+
 /* Head-width repack (no reference counterpart; layout plumbing for head_dim
  * below the attention kernel's 64): out[r][h][c] = x[r][h][c] for
  * c < min(hd_in, hd_out), 0 for the rest of the hd_out columns, and the
@@ -390,6 +400,65 @@ int p3d_flow_sample(p3d_flow *flow, float *x, const void *ctx_feats, int ctx_dty
                     const p3d_sampler_config *cfg);
 /* Kernel launches one sampler step issued (forward + update), for reporting. */
 int64_t p3d_flow_launches_per_step(const p3d_flow *flow);
+
+/* ------------------------------------------------------- SLat decoder */
+
+#define P3D_DECODER_MAX_LEVELS 8
+
+/* SLatDecoderConfig (include/pixal3d/slat_decoder.h): levels of
+ * model_channels / num_blocks ConvNeXt blocks, a channel-to-spatial
+ * res block between consecutive levels. */
+typedef struct p3d_decoder_config {
+    int latent_channels, out_channels, levels;
+    int model_channels[P3D_DECODER_MAX_LEVELS];
+    int num_blocks[P3D_DECODER_MAX_LEVELS];
+    int pred_subdiv;
+    float norm_eps;
+    int operand_dtype; /* P3D_F16 or P3D_BF16 */
+} p3d_decoder_config;
+
+/* SLatDecoderBlockWeightsF32 (include/pixal3d/slat_decoder.h), f32 DEVICE
+ * pointers.  kind 0 = ConvNeXt (norm, conv1, mlp0, mlp2), 1 =
+ * channel-to-spatial res block (norm1, conv1, conv2, to_subdiv).  Conv
+ * weights [27][cout][cin]. */
+typedef struct p3d_decoder_block {
+    int kind, channels, out_channels, mlp_hidden;
+    const float *norm_w, *norm_b, *norm1_w, *norm1_b, *conv1_w, *conv1_b, *conv2_w, *conv2_b;
+    const float *mlp0_w, *mlp0_b, *mlp2_w, *mlp2_b, *subdiv_w, *subdiv_b;
+} p3d_decoder_block;
+
+typedef struct p3d_decoder_weights {
+    const float *from_latent_w, *from_latent_b, *output_w, *output_b;
+    const p3d_decoder_block *blocks;
+    int num_blocks;
+} p3d_decoder_weights;
+
+typedef struct p3d_decoder p3d_decoder;
+
+/* Upload/convert the decoder weights into the device layout (16-bit,
+ * padded operands).  Replaces SLatDecoderModel::load's tensor upload. */
+int p3d_decoder_create(p3d_ctx *ctx, const p3d_decoder_config *cfg, const p3d_decoder_weights *w, p3d_decoder **out);
+int p3d_decoder_destroy(p3d_decoder *dec);
+
+/* slat_decoder_forward_f32 (src/slat_decoder.cpp:290-376) on the device, or
+ * with stop_level in [0, levels) slat_decoder_upsample_coords_f32
+ * (:378-455): stop at that level's input.  coords int32 [n][4] and latent
+ * f32 [n][latent_channels] on the device.  guides: NULL or levels-1 device
+ * pointers to f32 [rows(level)][8] subdivision logits (child c kept where
+ * > 0) used when pred_subdiv is 0, with their row counts in guide_rows.
+ * Synchronises once per level (the next level's size).  Results stay in the
+ * decoder until the next run; read them with the calls below. */
+int p3d_decoder_run(p3d_decoder *dec, const int32_t *coords, int64_t n, int batch, int sx, int sy, int sz,
+                    const float *latent, const float *const *guides, const int64_t *guide_rows, int stop_level);
+/* Rows of level l (l < levels; the output has the last level's rows). */
+int64_t p3d_decoder_rows(const p3d_decoder *dec, int level);
+/* Coordinates of level l -> out int32 [rows(l)][4] (device). */
+int p3d_decoder_coords(p3d_decoder *dec, int level, int32_t *out);
+/* Output features f32 [rows][out_channels] (device); after a stopped run,
+ * the hidden features f32 [rows(stop)][model_channels[stop]]. */
+int p3d_decoder_output(p3d_decoder *dec, float *out);
+/* Predicted subdivision logits of level l (pred_subdiv), f32 [rows(l)][8]. */
+int p3d_decoder_subdivision(p3d_decoder *dec, int level, float *out);
 
 #ifdef __cplusplus
 }

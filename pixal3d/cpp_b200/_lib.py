@@ -130,6 +130,8 @@ _sig("p3d_rope_table", i32, vp, vp, i64, i32, f32, f32, vp)
 _sig("p3d_activation", i32, vp, vp, i64, i32, i32, vp)
 _sig("p3d_repack_heads", i32, vp, vp, i64, i64, i32, i32, i32, vp, i64, i32)
 _sig("p3d_timestep_mlp", i32, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp)
+_sig("p3d_layernorm_act", i32, vp, vp, i64, i32, f32, vp, vp, i32, vp, i64, i32)
+_sig("p3d_pack_operand", i32, vp, vp, i64, i32, vp, i64, i32)
 _sig("p3d_group_norm_silu", i32, vp, vp, i64, i32, i32, f32, vp, vp, vp, i32, i32, vp, vp, i32)
 _sig("p3d_euler_cfg_step", i32, vp, vp, vp, vp, i64, i32, vp, i32, f32, f32, f32, f32, f32, vp, vp)
 _sig("p3d_convert", i32, vp, vp, i32, i64, vp, i32)
@@ -151,6 +153,37 @@ _optional("p3d_flow_forward", i32, vp, vp, vp, vp, i32, vp, vp)
 _optional("p3d_flow_sample", i32, vp, vp, vp, i32, vp, C.POINTER(SamplerConfig))
 _optional("p3d_flow_last_error", C.c_char_p, vp)
 _optional("p3d_flow_launches_per_step", i64, vp)
+
+DECODER_MAX_LEVELS = 8
+
+
+class DecoderConfig(C.Structure):
+    _fields_ = [("latent_channels", i32), ("out_channels", i32), ("levels", i32),
+                ("model_channels", i32 * DECODER_MAX_LEVELS), ("num_blocks", i32 * DECODER_MAX_LEVELS),
+                ("pred_subdiv", i32), ("norm_eps", f32), ("operand_dtype", i32)]
+
+
+DECODER_BLOCK_FIELDS = ("norm_w", "norm_b", "norm1_w", "norm1_b", "conv1_w", "conv1_b", "conv2_w", "conv2_b",
+                        "mlp0_w", "mlp0_b", "mlp2_w", "mlp2_b", "subdiv_w", "subdiv_b")
+
+
+class DecoderBlock(C.Structure):
+    _fields_ = [("kind", i32), ("channels", i32), ("out_channels", i32), ("mlp_hidden", i32)] + \
+        [(n, vp) for n in DECODER_BLOCK_FIELDS]
+
+
+class DecoderWeights(C.Structure):
+    _fields_ = [("from_latent_w", vp), ("from_latent_b", vp), ("output_w", vp), ("output_b", vp),
+                ("blocks", C.POINTER(DecoderBlock)), ("num_blocks", i32)]
+
+
+_sig("p3d_decoder_create", i32, vp, C.POINTER(DecoderConfig), C.POINTER(DecoderWeights), C.POINTER(vp))
+_sig("p3d_decoder_destroy", i32, vp)
+_sig("p3d_decoder_run", i32, vp, vp, i64, i32, i32, i32, i32, vp, C.POINTER(vp), C.POINTER(i64), i32)
+_sig("p3d_decoder_rows", i64, vp, i32)
+_sig("p3d_decoder_coords", i32, vp, i32, vp)
+_sig("p3d_decoder_output", i32, vp, vp)
+_sig("p3d_decoder_subdivision", i32, vp, i32, vp)
 
 
 def exported_symbols() -> list[str]:

@@ -132,6 +132,49 @@ __global__ void __launch_bounds__(256) layernorm_reg_kernel(const float *__restr
     }
 }
 
+// LayerNorm (+affine) (+SiLU) into an operand of row pitch ld_out >= C whose
+// pitch padding is written as zeros.  One warp per row, two-pass statistics
+// (sparse_layer_norm, src/sparse.cpp:514-531).
+template <typename TO>
+__global__ void layernorm_act_kernel(const float *__restrict__ x, int64_t n, int C, float eps,
+                                     const float *__restrict__ gamma, const float *__restrict__ beta, int silu,
+                                     TO *__restrict__ out, int64_t ld_out) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int lane = threadIdx.x & 31;
+    const float *xr = x + row * C;
+    float s = 0.0f;
+    for (int c = lane; c < C; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / static_cast<float>(C);
+    float ss = 0.0f;
+    for (int c = lane; c < C; c += 32) {
+        const float d = xr[c] - mean;
+        ss += d * d;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(C) + eps);
+    TO *o = out + row * ld_out;
+    for (int c = lane; c < ld_out; c += 32) {
+        float v = 0.0f;
+        if (c < C) {
+            v = (xr[c] - mean) * inv;
+            if (gamma) v = v * gamma[c] + beta[c];
+            if (silu) v = silu_f(v);
+        }
+        store_val(o + c, v);
+    }
+}
+
+// f32 [rows][cols] -> TO [rows][ld] with zero pitch padding.
+template <typename TO>
+__global__ void pack_operand_kernel(const float *__restrict__ x, int64_t rows, int cols, TO *__restrict__ out,
+                                    int64_t ld) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * ld) return;
+    const int64_t r = i / ld;
+    const int64_t c = i - r * ld;
+    store_val(out + i, c < cols ? x[r * cols + c] : 0.0f);
+}
+
 // ------------------------------------------------ per-head RMS + 3D RoPE
 // One warp per row; lane p owns rotation pair p (elements 2p, 2p+1) of
 // every head.  head_dim <= 64.
@@ -434,6 +477,32 @@ extern "C" int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, i
                 x, n, channels, eps, gamma, beta, mod, mod_ld, batch_offsets, nbatch, static_cast<TO *>(out));
     });
     return check_launch(ctx, "layernorm_mod");
+}
+
+extern "C" int p3d_layernorm_act(p3d_ctx *ctx, const float *x, int64_t n, int channels, float eps,
+                                 const float *gamma, const float *beta, int silu, void *out, int64_t ld_out,
+                                 int out_dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && channels > 0 && ld_out >= channels && n >= 0, "p3d_layernorm_act: bad argument");
+    P3D_REQUIRE(ctx, (gamma == nullptr) == (beta == nullptr),
+                "sparse layer norm affine parameters must be both null or non-null");
+    P3D_REQUIRE(ctx, eps > 0.0f, "sparse layer norm epsilon must be finite and positive");
+    if (n == 0) return P3D_OK;
+    P3D_DISPATCH(out_dtype, TO,
+                 layernorm_act_kernel<TO><<<blocks_for(n, 8), 256, 0, ctx->stream>>>(
+                     x, n, channels, eps, gamma, beta, silu, static_cast<TO *>(out), ld_out));
+    return check_launch(ctx, "layernorm_act");
+}
+
+extern "C" int p3d_pack_operand(p3d_ctx *ctx, const float *x, int64_t rows, int cols, void *out, int64_t ld,
+                                int out_dtype) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, x && out && cols > 0 && ld >= cols && rows >= 0, "p3d_pack_operand: bad argument");
+    if (rows == 0) return P3D_OK;
+    P3D_DISPATCH(out_dtype, TO,
+                 pack_operand_kernel<TO><<<blocks_for(rows * ld, 256), 256, 0, ctx->stream>>>(
+                     x, rows, cols, static_cast<TO *>(out), ld));
+    return check_launch(ctx, "pack_operand");
 }
 
 extern "C" int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads, int head_dim,
