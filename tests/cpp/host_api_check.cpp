@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "pixal3d/flow_sampler.h"
+#include "pixal3d/slat_decoder.h"
 #include "pixal3d/slat_flow.h"
 #include "pixal3d/sparse.h"
 #include "pixal3d/sparse_transformer.h"
@@ -315,6 +316,90 @@ void flow_device() {
     else put_error("device_flow_sample", e);
 }
 
+SLatDecoderBlockWeightsF32 dec_block(int i, bool c2s, int C, int O, int mlp) {
+    SLatDecoderBlockWeightsF32 b;
+    const std::string p = "dec.b" + std::to_string(i) + ".";
+    auto g = [&](const char *n) { return in.count(p + n) ? F(p + n).data() : nullptr; };
+    b.kind = c2s ? SLatDecoderBlockKind::channel_to_spatial : SLatDecoderBlockKind::convnext;
+    b.channels = C;
+    b.out_channels = O;
+    b.mlp_hidden = mlp;
+    if (!c2s) {
+        b.norm_weight = g("norm_w");
+        b.norm_bias = g("norm_b");
+        b.conv1_weight = g("conv_w");
+        b.conv1_bias = g("conv_b");
+        b.mlp0_weight = g("mlp0_w");
+        b.mlp0_bias = g("mlp0_b");
+        b.mlp2_weight = g("mlp2_w");
+        b.mlp2_bias = g("mlp2_b");
+    } else {
+        b.norm1_weight = g("norm1_w");
+        b.norm1_bias = g("norm1_b");
+        b.conv1_weight = g("conv1_w");
+        b.conv1_bias = g("conv1_b");
+        b.conv2_weight = g("conv2_w");
+        b.conv2_bias = g("conv2_b");
+        b.to_subdiv_weight = g("subdiv_w");
+        b.to_subdiv_bias = g("subdiv_b");
+    }
+    return b;
+}
+
+// The reference decoder fixture (3 levels 8 -> 8 -> 4, predicted subdivision).
+void decoder() {
+    SLatDecoderWeightsF32 w;
+    w.from_latent_weight = F("dec.from_latent_w").data();
+    w.from_latent_bias = F("dec.from_latent_b").data();
+    w.output_weight = F("dec.output_w").data();
+    w.output_bias = F("dec.output_b").data();
+    w.blocks = {dec_block(0, false, 8, 8, 32), dec_block(1, true, 8, 8, 0), dec_block(2, false, 8, 8, 32),
+                dec_block(3, true, 8, 4, 0), dec_block(4, false, 4, 4, 16)};
+    SLatDecoderConfig cfg;
+    cfg.latent_channels = 3;
+    cfg.out_channels = 3;
+    cfg.pred_subdiv = true;
+    cfg.model_channels = {8, 8, 4};
+    cfg.num_blocks = {1, 1, 1};
+    const SparseTensorF32 x = sparse(I("dec.coords"), F("dec.x"), 3, 1, 2, 2, 2);
+    SparseTensorF32 o;
+    std::vector<SparseTensorF32> preds;
+    std::string e;
+    if (slat_decoder_forward_f32(x, cfg, w, nullptr, o, &preds, &e)) {
+        put("slat_decoder_coords", o.coords);
+        put("slat_decoder_output", o.feats);
+        put("slat_decoder_subdiv_0_output", preds.at(0).feats);
+        put("slat_decoder_subdiv_1_output", preds.at(1).feats);
+    } else put_error("slat_decoder_forward", e);
+    SLatDecoderModel model;
+    SLatDecoderHParams hp;
+    hp.latent_channels = 3;
+    hp.out_channels = 3;
+    hp.pred_subdiv = true;
+    hp.model_channels = cfg.model_channels;
+    hp.num_blocks = cfg.num_blocks;
+    if (!model.bind(hp, w, &e)) {
+        put_error("slat_decoder_bind", e);
+        return;
+    }
+    for (int level = 0; level < 3; ++level) {
+        if (model.upsample_coords(x, level, o, &e)) put("slat_decoder_upsample_coords_" + std::to_string(level), o.coords);
+        else put_error("slat_decoder_upsample_coords", e);
+    }
+    if (model.decode(x, nullptr, o, &preds, &e)) put("slat_decoder_model_output", o.feats);
+    else put_error("slat_decoder_decode", e);
+    // single blocks on the level-0 hidden state
+    const SparseTensorF32 h0 = sparse(I("dec.coords"), F("dec.h0"), 8, 1, 2, 2, 2);
+    if (sparse_convnext_block_f32(h0, w.blocks[0], 1e-6f, o, &e)) put("dec_convnext_output", o.feats);
+    else put_error("dec_convnext", e);
+    SparseTensorF32 pred;
+    if (sparse_resblock_c2s_f32(h0, w.blocks[1], 1e-6f, true, nullptr, o, &pred, &e)) {
+        put("dec_c2s_coords", o.coords);
+        put("dec_c2s_output", o.feats);
+        put("dec_c2s_subdiv", pred.feats);
+    } else put_error("dec_c2s", e);
+}
+
 void sampler() {
     const SparseTensorF32 noise = sparse(I("fs.coords"), F("fs.noise"), 3, 2, 3, 3, 3);
     FlowEulerSamplerConfig sc;
@@ -358,6 +443,7 @@ int main(int argc, char **argv) {
         block();
         flow();
         flow_device();
+        decoder();
         sampler();
     } catch (const std::exception &ex) {
         std::cerr << "exception: " << ex.what() << "\n";

@@ -53,6 +53,9 @@ REFERENCE_API = [
     "pixal3d::sparse_submanifold_conv3d", "pixal3d::sparse_transformer_cross_block_f32",
     "pixal3d::flow_euler_sample_f32", "pixal3d::slat_flow_forward_f32", "pixal3d::SLatFlowModel::forward",
     "pixal3d::SLatFlowModel::sample", "pixal3d::SLatFlowModel::load", "pixal3d::SLatFlowModel::bind",
+    "pixal3d::sparse_convnext_block_f32", "pixal3d::sparse_resblock_c2s_f32", "pixal3d::slat_decoder_forward_f32",
+    "pixal3d::slat_decoder_upsample_coords_f32", "pixal3d::SLatDecoderModel::decode",
+    "pixal3d::SLatDecoderModel::upsample_coords", "pixal3d::SLatDecoderModel::bind",
 ]
 
 

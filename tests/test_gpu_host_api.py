@@ -87,6 +87,15 @@ def _inputs():
     a["bf.noise"] = rng.standard_normal((a["bf.coords"].shape[0], 8)).astype(np.float32)
     a["bf.ctx"] = rng.standard_normal((33, 64)).astype(np.float32)
     a["bf.timestep"] = np.array([640.0], np.float32)
+    wd, cfgd, dcoords, dx = FX.decoder_fixture()
+    for k in ("from_latent_w", "from_latent_b", "output_w", "output_b"):
+        a["dec." + k] = wd[k].astype(np.float32)
+    for i, b in enumerate(wd["blocks"]):
+        for k, v in b.items():
+            a[f"dec.b{i}.{k}"] = np.asarray(v, np.float32)
+    a["dec.coords"] = dcoords.astype(np.int32)
+    a["dec.x"] = dx.astype(np.float32)
+    a["dec.h0"] = O.linear(dx, wd["from_latent_w"], wd["from_latent_b"])
     a["fs.coords"] = np.array([[0, 0, 0, 0], [0, 0, 1, 0], [0, 2, 1, 1], [1, 0, 0, 1], [1, 1, 2, 0]], np.int32)
     a["fs.noise"] = FX.seq(15, -0.73, 0.091)
     return a
@@ -173,3 +182,25 @@ def test_device_resident_flow_through_host_api(harness):
 
     exp_s = O.flow_euler_sample(x, sc, model, c[:, 0].astype(np.int64), 1)
     _close(harness["device_flow_sample"], exp_s.ravel(), "device sample")
+
+
+def test_slat_decoder_matches_reference_fixture(harness):
+    """slat_decoder_forward_f32, SLatDecoderModel::decode / ::upsample_coords
+    and the single-block functions through the host API."""
+    from oracle import oracle as O
+    g = FX.parse_golden("slat_decoder_numeric_fixture")
+    np.testing.assert_array_equal(harness["slat_decoder_coords"], g["slat_decoder_coords"])
+    _close(harness["slat_decoder_output"], g["slat_decoder_output"], "decoder output")
+    _close(harness["slat_decoder_model_output"], g["slat_decoder_output"], "SLatDecoderModel::decode")
+    _close(harness["slat_decoder_subdiv_0_output"], g["slat_decoder_subdiv_0_output"], "subdiv 0")
+    _close(harness["slat_decoder_subdiv_1_output"], g["slat_decoder_subdiv_1_output"], "subdiv 1")
+    for level in range(3):
+        k = f"slat_decoder_upsample_coords_{level}"
+        np.testing.assert_array_equal(harness[k], g[k])
+    w, cfg, coords, x = FX.decoder_fixture()
+    h0 = O.linear(x, w["from_latent_w"], w["from_latent_b"])
+    _close(harness["dec_convnext_output"], O.convnext_block(coords, h0, w["blocks"][0], 1e-6).ravel(), "convnext")
+    cc, hh, pp = O.resblock_c2s(coords, h0, w["blocks"][1], 1e-6, 8, True)
+    np.testing.assert_array_equal(harness["dec_c2s_coords"], cc.ravel())
+    _close(harness["dec_c2s_output"], hh.ravel(), "c2s block")
+    _close(harness["dec_c2s_subdiv"], pp.ravel(), "c2s predicted subdivision")
