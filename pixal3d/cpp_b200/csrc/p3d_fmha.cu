@@ -15,15 +15,19 @@
 //              quarter w % 4)
 // Per key block j (S/P buffer b = j & 1 in TMEM):
 //   S_b = Q K_j^T              tcgen05.mma, A = Q (smem), B = K (smem), K-major
-//   P_b = exp2(S_b*c - m)      softmax threads: tcgen05.ld S row, write P as
-//                              packed 16-bit pairs back into S_b's columns
+//   P_b = exp2(S_b*c - m)      softmax threads: tcgen05.ld S row, exponents in
+//                              packed 16-bit pairs (ex2.approx.f16x2 /
+//                              .bf16x2: two per MUFU op), written as P back
+//                              into S_b's columns
 //   O  += P_b V_j              tcgen05.mma with A read from TMEM (P_b),
 //                              B = V (smem, MN-major); O stays in TMEM
+//   l  += P_b 1                the row sums, by the tensor core from the same
+//                              16-bit P (N = 16 against a ones tile)
 // The running max m is raised lazily: only when a block's max exceeds it by
 // more than 8 (a factor 2^8 in P) does the row's owner wait for the pending
-// P V, rescale O in TMEM (ld, scale, st) and the running sum; otherwise P
-// is computed against the stale max, which is exact because the final
-// normalisation divides by a sum taken against the same max.
+// P V, rescale O and l in TMEM (ld, scale, st); otherwise P is computed
+// against the stale max, which is exact because the final normalisation
+// divides by a sum taken against the same max.
 // Every mbarrier wait is bounded; a stuck pipeline latches P3D_ERR_TIMEOUT,
 // the CTA still frees its TMEM and exits.
 #include <type_traits>
@@ -42,13 +46,15 @@ constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int Q_BYTES = kM * kD * 2;   // 16 KB
 constexpr int KV_BYTES = kN * kD * 2;  // 8 KB each
-constexpr int USED_BYTES = Q_BYTES + kStages * 2 * KV_BYTES + 1024 + 512;
+constexpr int ONES_BYTES = 16 * kN * 2;  // B operand of the row-sum MMA: 16 x 64 ones
+constexpr int USED_BYTES = Q_BYTES + kStages * 2 * KV_BYTES + ONES_BYTES + 1024 + 512;
 // Request enough dynamic shared memory that at most two CTAs fit on an SM:
 // two CTAs use 2 x 256 = 512 TMEM columns, a third would wait in tcgen05.alloc.
 constexpr int SMEM_BYTES = 100 * 1024;
 static_assert(USED_BYTES <= SMEM_BYTES, "smem layout exceeds the request");
-constexpr uint32_t TMEM_COLS = 256;  // S/P 0 (64) | S/P 1 (64) | O (64) | unused
+constexpr uint32_t TMEM_COLS = 256;  // S/P 0 (64) | S/P 1 (64) | O (64) | l (16) | unused
 constexpr uint32_t O_COL = 128;
+constexpr uint32_t L_COL = 192;
 
 __device__ __forceinline__ uint32_t sp_col(int b) { return b ? 64u : 0u; }
 
@@ -76,6 +82,37 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One TMEM column for the warp's 32 lanes.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v))
+                 : "memory");
+}
+
+// 2^x0, 2^x1 as a packed 16-bit pair (x0 in the low half): one MUFU op.
+template <typename T>
+__device__ __forceinline__ uint32_t ex2_pair(float x0, float x1);
+template <>
+__device__ __forceinline__ uint32_t ex2_pair<__half>(float x0, float x1) {
+    uint32_t r;
+    asm("{\n\t.reg .b32 t;\n\tcvt.rn.f16x2.f32 t, %2, %1;\n\tex2.approx.f16x2 %0, t;\n\t}"
+        : "=r"(r)
+        : "f"(x0), "f"(x1));
+    return r;
+}
+template <>
+__device__ __forceinline__ uint32_t ex2_pair<__nv_bfloat16>(float x0, float x1) {
+    uint32_t r;
+    asm("{\n\t.reg .b32 t;\n\tcvt.rn.bf16x2.f32 t, %2, %1;\n\tex2.approx.ftz.bf16x2 %0, t;\n\t}"
+        : "=r"(r)
+        : "f"(x0), "f"(x1));
+    return r;
+}
+
 struct FmhaParams {
     const int32_t *cu_q, *cu_k;
     void *out;
@@ -101,7 +138,8 @@ __global__ void __launch_bounds__(kThreadsF, 2)
     uint8_t *sQ = smem;
     uint8_t *sK = sQ + Q_BYTES;             // [kStages][KV_BYTES]
     uint8_t *sV = sK + kStages * KV_BYTES;  // [kStages][KV_BYTES]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kStages * KV_BYTES);
+    uint8_t *sOnes = sV + kStages * KV_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sOnes + ONES_BYTES);
     uint64_t *q_full = bars;                 // 1
     uint64_t *kv_full = bars + 1;            // kStages
     uint64_t *kv_empty = kv_full + kStages;  // kStages
@@ -133,6 +171,13 @@ __global__ void __launch_bounds__(kThreadsF, 2)
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
+    {
+        // ones tile (16-bit 1.0) for the row-sum MMA; read by the async proxy
+        const uint32_t one2 = std::is_same<T, __nv_bfloat16>::value ? 0x3F803F80u : 0x3C003C00u;
+        uint32_t *o32 = reinterpret_cast<uint32_t *>(sOnes);
+        for (int i = threadIdx.x; i < ONES_BYTES / 4; i += kThreadsF) o32[i] = one2;
+        fence_proxy_async_smem();
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -163,7 +208,9 @@ __global__ void __launch_bounds__(kThreadsF, 2)
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f32acc(kM, kN, kBf16);
             const uint32_t idesc_o = idesc_f32acc(kM, kD, kBf16, true);
+            const uint32_t idesc_l = idesc_f32acc(kM, 16, kBf16);
             const uint32_t q_addr = smem_u32(sQ);
+            const uint32_t ones_addr = smem_u32(sOnes);
             bool ok = mbar_wait(q_full, 0, p.fault);
             auto issue_pv = [&](int i) -> bool {
                 const int b = i & 1, st = i % kStages;
@@ -171,9 +218,12 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV + st * KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < kN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
+                for (int kk = 0; kk < kN / 16; ++kk) {  // 16 keys = 8 packed TMEM columns of P
                     umma_f16_ts(tmem + O_COL, tmem + sp_col(b) + kk * 8, sw128_desc_mn(v_addr + kk * 2048, kN * 128),
                                 idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_ts(tmem + L_COL, tmem + sp_col(b) + kk * 8, sw128_desc(ones_addr + kk * 32), idesc_l,
+                                (i > 0 || kk > 0) ? 1u : 0u);
+                }
                 umma_commit(&pv_done[b]);
                 umma_commit(&kv_empty[st]);
                 return true;
@@ -202,7 +252,7 @@ __global__ void __launch_bounds__(kThreadsF, 2)
         const int q = warp & 3;  // TMEM lane quarter
         const int row = q * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        float m_run = -INFINITY, l_run = 0.0f;
+        float m_run = -INFINITY;
         bool ok = true;
         // Waits are warp-uniform (lane 0 polls) because the tcgen05.ld/st
         // that follow are warp-collective.
@@ -228,12 +278,21 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                 }
             }
             const int valid = min(kN, k1 - (k0 + j * kN));
-            float mx = -INFINITY;
+            if (valid < kN) {
 #pragma unroll
-            for (int i = 0; i < kN; ++i) {
-                s[i] = i < valid ? s[i] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, s[i]);
+                for (int i = 0; i < kN; ++i) s[i] = i < valid ? s[i] : -INFINITY;
             }
+            // row max as a tree (8 independent chains), not one 64-long chain
+            float m8[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) m8[c] = s[c];
+#pragma unroll
+            for (int i = 8; i < kN; i += 8)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) m8[c] = fmaxf(m8[c], s[i + c]);
+            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            mx *= p.scale_log2;  // the scale is positive
             const bool need = j > 0 && mx > m_run + kRescaleLog2;
             if (j == 0) m_run = mx;
             if (__any_sync(0xffffffffu, need)) {
@@ -243,10 +302,7 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                 if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const float alpha = need ? exp2f(m_run - mx) : 1.0f;
-                if (need) {
-                    l_run *= alpha;
-                    m_run = mx;
-                }
+                if (need) m_run = mx;
 #pragma unroll
                 for (int c = 0; c < kD; c += 32) {
                     float o[32];
@@ -257,17 +313,16 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                     for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
                     tmem_st32(tmem + lane_base + O_COL + c, r);
                 }
+                const float l = tmem_ld1(tmem + lane_base + L_COL);
+                tmem_ld_wait();
+                tmem_st1(tmem + lane_base + L_COL, l * alpha);
                 tmem_st_wait();
             }
-            float rs = 0.0f;
+            const float nm = -m_run;
             uint32_t pk[32];
 #pragma unroll
-            for (int i = 0; i < kN; i += 2) {
-                const float a = exp2f(s[i] - m_run), c = exp2f(s[i + 1] - m_run);
-                rs += a + c;
-                pk[i / 2] = pack2<T>(a, c);
-            }
-            l_run += rs;
+            for (int i = 0; i < kN; i += 2)
+                pk[i / 2] = ex2_pair<T>(fmaf(s[i], p.scale_log2, nm), fmaf(s[i + 1], p.scale_log2, nm));
             tmem_st32(tmem + lane_base + sp_col(b), pk);
             tmem_st_wait();
             tc_fence_before();
@@ -287,6 +342,8 @@ __global__ void __launch_bounds__(kThreadsF, 2)
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[c + i] = v[i];
         }
+        const float l_run = tmem_ld1(tmem + lane_base + L_COL);
+        tmem_ld_wait();
         if (ok && grow < q1) {
             const float inv = 1.0f / l_run;
             T *dst = reinterpret_cast<T *>(p.out) + grow * p.ldo + head * kD;

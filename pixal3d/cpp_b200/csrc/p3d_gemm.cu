@@ -487,7 +487,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 // even CTA's `tempty` barrier (count 8).  No TMA multicast.  All waits are
 // bounded; the pair meets at cluster barriers before the first remote
 // arrival and before freeing TMEM.
-template <int NSUB, bool GATHER>
+// Source rows m0 + 4*lane .. +3 of tap `tap` for the TMA row gather (sentinel
+// or out of range -> row M, read as zeros).
+__device__ __forceinline__ int4 gather_src4(const GemmParams &p, int lane, int64_t m0, int tap) {
+    int r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int64_t row = m0 + 4 * lane + j;
+        int32_t s = static_cast<int32_t>(p.M);
+        if (tap < 27 && row < p.M) {
+            s = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
+            if (s >= p.M || s < 0) s = static_cast<int32_t>(p.M);
+        }
+        r[j] = s;
+    }
+    return make_int4(r[0], r[1], r[2], r[3]);
+}
+
+template <int NSUB, bool GATHER, bool TMAG = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const GemmParams p) {
@@ -523,7 +540,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
         // the odd CTA's forwarded gather completion); odd CTA (gather): its
         // 128 row-gather threads, forwarded by its warp 8.
-        const uint32_t full_count = GATHER ? (rank == 0 ? kProducerThreads + 2 : kProducerThreads) : 1;
+        const uint32_t full_count = (GATHER && !TMAG) ? (rank == 0 ? kProducerThreads + 2 : kProducerThreads) : 1;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full_bar[s], full_count);
             mbar_init(&empty_bar[s], 1);
@@ -534,7 +551,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
-        if (!GATHER) prefetch_tmap(&tmap_a);
+        if (!GATHER || TMAG) prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
     if (warp == kMmaWarp) {
@@ -546,7 +563,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp < 4) {
+    if (GATHER && TMAG && warp < 4) {
+        // ---------------------------------------- producer, TMA row gather
+        // Warp 0 only: lane l gathers rows 4l..4l+3 of the A stage with one
+        // tile::gather4 (box 64 columns x 1 row); both CTAs' A and B bytes
+        // complete on the even CTA's `full` barrier.
+        if (warp == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
+                const int64_t n0 = (tile % n_tiles) * PAIR_N;
+                int4 cur = gather_src4(p, lane, m0, 0), next = gather_src4(p, lane, m0, 1);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!warp_wait<true>(&empty_bar[stage], phase ^ 1, p.fault)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tap = kb / kblocks_per_tap;
+                    const int kc = (kb % kblocks_per_tap) * BK;
+                    if (kc == 0 && tap > 0) {
+                        cur = next;
+                        next = gather_src4(p, lane, m0, tap + 1);
+                    }
+                    uint8_t *sa = smem_a + stage * C::A_BYTES;
+                    uint8_t *sb = smem_b + stage * C::B_BYTES;
+                    const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+                    if (lane == 0 && rank == 0)
+                        mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
+                    tma_gather4_pair(sa + lane * 4 * 128, &tmap_a, fb, kc, cur.x, cur.y, cur.z, cur.w);
+                    if (lane == 0) {
+#pragma unroll
+                        for (int j = 0; j < NSUB; ++j)
+                            tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
+                                             static_cast<int>(tap * p.N + n0 + j * 256 + rank * 128));
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp < 4) {
         // ------------------------------------------------------------ producer
         const int t = threadIdx.x;
         int stage = 0;
@@ -623,7 +683,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    if (GATHER) fence_proxy_async_smem();
+                    if (GATHER && !TMAG) fence_proxy_async_smem();
                     const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
@@ -655,7 +715,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 umma_commit2(smem_u32(done_bar));
                 mbar_wait(done_bar, 0, p.fault);
             }
-        } else if (GATHER && lane == 0) {
+        } else if (GATHER && !TMAG && lane == 0) {
             // ------------ odd CTA: forward its row-gather completion to rank 0
             int stage = 0;
             uint32_t phase = 0;
@@ -744,12 +804,12 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
-template <int NSUB, bool GATHER>
+template <int NSUB, bool GATHER, bool TMAG = false>
 int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
     using C = Cfg2<NSUB>;
     static bool attr_set = false;
     if (!attr_set) {
-        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm2_tc_kernel<NSUB, GATHER>,
+        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm2_tc_kernel<NSUB, GATHER, TMAG>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set = true;
     }
@@ -763,12 +823,12 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
         cfg.dynamicSmemBytes = C::SMEM;
         cfg.stream = ctx->stream;
         int n = 0;
-        P3D_CUDA(ctx, cudaOccupancyMaxActiveClusters(&n, gemm2_tc_kernel<NSUB, GATHER>, &cfg));
+        P3D_CUDA(ctx, cudaOccupancyMaxActiveClusters(&n, gemm2_tc_kernel<NSUB, GATHER, TMAG>, &cfg));
         max_pairs = std::max(1, std::min(n, ctx->num_sms / 2));
     }
     const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
-    gemm2_tc_kernel<NSUB, GATHER><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
     return check_launch(ctx, "gemm2_tc_kernel");
 }
 
@@ -796,6 +856,16 @@ bool pair_dense() {
     return on;
 }
 
+// P3D_CONV_GATHER=tma gathers the conv's A rows with TMA tile::gather4
+// (counted on the even CTA's barrier, no forwarding) instead of cp.async.
+bool conv_tma_gather() {
+    static const bool on = [] {
+        const char *e = std::getenv("P3D_CONV_GATHER");
+        return e && std::string(e) == "tma";
+    }();
+    return on;
+}
+
 // x == nullptr selects the gather (sparse conv) variant, whose B operand is
 // the [27 * N, K] tap stack.  Builds the tensor maps and instruction
 // descriptor for the chosen kernel and launches it.
@@ -815,8 +885,13 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
         int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, 128);
         if (rc) return rc;
         if (!gather && (rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM))) return rc;
-        if (gather) ta = tb;
         p.idesc = idesc_f32acc(2 * BM, 256, bf16);
+        if (gather && conv_tma_gather()) {
+            // A rows by TMA tile::gather4 from x [M][K] (box 64 x 1 row)
+            if ((rc = make_tmap_16bit_2d(ctx, &ta, p.x, ab_dtype, p.M, p.K, p.ldx, 1))) return rc;
+            return nsub == 2 ? launch_gemm2<2, true, true>(ctx, ta, tb, p) : launch_gemm2<1, true, true>(ctx, ta, tb, p);
+        }
+        if (gather) ta = tb;
         if (gather) return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, p) : launch_gemm2<1, true>(ctx, ta, tb, p);
         return launch_gemm2<1, false>(ctx, ta, tb, p);
     }
