@@ -409,7 +409,8 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
     if (hp.proj_mode && proj) {
         P3D_TRY(pad16(ctx, proj, nt, hp.proj_in_channels, f->proj_pad, f->proj_bf, dt));
     }
-    for (const DevBlock &bw : f->blocks) {
+    for (std::size_t bi = 0; bi < f->blocks.size(); ++bi) {
+        const DevBlock &bw = f->blocks[bi];
         add_mod_kernel<<<blocks_for(static_cast<int64_t>(B) * 6 * C, 256), 256, 0, ctx->stream>>>(
             bw.modulation, f->tmod, B, 6 * C, f->mods);
         P3D_TRY(check_launch(ctx, "add_mod"));
@@ -442,20 +443,15 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         if (fuse_heads && hp.qk_rms_norm_cross) {
             P3D_TRY(p3d_linear_headnorm(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, C, bw.cq_gamma, 0,
                                         nullptr));
-            P3D_TRY(p3d_linear_headnorm(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad,
-                                        f->kv, 2 * C, dt, C, bw.ck_gamma, 0, nullptr));
         } else {
             P3D_TRY(p3d_linear(ctx, f->xn, C, bw.cq_w, dt, bw.cq_b, nt, C, C, f->cq, C, dt, P3D_EPI_NONE, nullptr, 0,
                                nullptr, 0));
             if (hp.qk_rms_norm_cross)
                 P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->cq, nt, C, H, C / H, bw.cq_gamma, nullptr, 1.0f, 10000.0f, dt));
-            P3D_TRY(p3d_linear(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad, f->kv,
-                               2 * C, dt, P3D_EPI_NONE, nullptr, 0, nullptr, 0));
-            if (hp.qk_rms_norm_cross)
-                P3D_TRY(p3d_qk_rmsnorm_rope(ctx, f->kv, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f,
-                                            dt));
         }
-        P3D_TRY(p3d_varlen_attention(ctx, f->cq, C, f->kv, 2 * C, f->kv + C, 2 * C, f->attn, C, f->trunk_off,
+        // this block's condition keys/values: computed once per condition (compute_kv)
+        const uint16_t *kvb = f->kv + static_cast<int64_t>(bi) * f->T * 2 * C;
+        P3D_TRY(p3d_varlen_attention(ctx, f->cq, C, kvb, 2 * C, kvb + C, 2 * C, f->attn, C, f->trunk_off,
                                      f->ctx_off, B, f->max_trunk, nt, f->T, H, C / H, attn_scale, dt));
         P3D_TRY(p3d_linear(ctx, f->attn, C, bw.co_w, dt, bw.co_b, nt, C, C, f->h, C, P3D_F32, P3D_EPI_RESIDUAL, nullptr, 0,
                            nullptr, 0));
@@ -753,7 +749,7 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     P3D_TRY(f->alloc(&f->attn, nt * C));
     P3D_TRY(f->alloc(&f->cq, nt * C));
     P3D_TRY(f->alloc(&f->mlp, nt * hp.mlp_hidden));
-    P3D_TRY(f->alloc(&f->kv, f->T * 2 * C));
+    P3D_TRY(f->alloc(&f->kv, static_cast<int64_t>(hp.num_blocks) * f->T * 2 * C));  // all blocks' K/V
     P3D_TRY(f->alloc(&f->ctx_bf, f->T * f->cond_pad));
     P3D_TRY(f->alloc(&f->proj_bf, nt * f->proj_pad));
     P3D_TRY(f->alloc(&f->x_in, n * f->in_pad));
@@ -799,6 +795,31 @@ int load_ctx(p3d_flow *f, const void *ctx_feats, int ctx_dtype) {
 }
 }  // namespace
 
+namespace {
+// Cross-attention keys/values of every block from the loaded condition
+// tokens (ctx_bf): they depend on neither the timestep nor the latents, so
+// a sampling run computes them once, outside the per-step graph.
+int compute_kv(p3d_flow *f) {
+    p3d_ctx *ctx = f->ctx;
+    const p3d_flow_hparams &hp = f->hp;
+    const int C = f->C, H = hp.num_heads, dt = f->dt;
+    for (std::size_t bi = 0; bi < f->blocks.size(); ++bi) {
+        const DevBlock &bw = f->blocks[bi];
+        uint16_t *kvb = f->kv + static_cast<int64_t>(bi) * f->T * 2 * C;
+        if (C / H == 64 && hp.qk_rms_norm_cross) {
+            P3D_TRY(p3d_linear_headnorm(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad,
+                                        kvb, 2 * C, dt, C, bw.ck_gamma, 0, nullptr));
+        } else {
+            P3D_TRY(p3d_linear(ctx, f->ctx_bf, f->cond_pad, bw.ckv_w, dt, bw.ckv_b, f->T, 2 * C, f->cond_pad, kvb,
+                               2 * C, dt, P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            if (hp.qk_rms_norm_cross)
+                P3D_TRY(p3d_qk_rmsnorm_rope(ctx, kvb, f->T, 2 * C, H, C / H, bw.ck_gamma, nullptr, 1.0f, 10000.0f, dt));
+        }
+    }
+    return P3D_OK;
+}
+}  // namespace
+
 extern "C" int p3d_flow_forward(p3d_flow *f, const float *x, const float *timesteps, const void *ctx_feats,
                                 int ctx_dtype, const float *proj, float *out) {
     if (!f) return P3D_ERR_INVALID;
@@ -808,6 +829,7 @@ extern "C" int p3d_flow_forward(p3d_flow *f, const float *x, const float *timest
     P3D_REQUIRE(ctx, x && timesteps && ctx_feats && out, "SLat flow input, timestep, or context shape mismatch");
     P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
     P3D_TRY(load_ctx(f, ctx_feats, ctx_dtype));
+    P3D_TRY(compute_kv(f));
     return forward_impl(f, x, timesteps, 1, nullptr, 1.0f, proj, out);
 }
 
@@ -861,6 +883,7 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
         const int64_t z0 = f->h_ctx_off[I], z1 = f->h_ctx_off[f->batch];
         P3D_CUDA(ctx, cudaMemsetAsync(f->ctx_bf + z0 * f->cond_pad, 0, sizeof(uint16_t) * (z1 - z0) * f->cond_pad,
                                       f->stream));
+        P3D_TRY(compute_kv(f));
         if (f->hp.proj_mode) {
             const int64_t hp_rows = half * f->hp.proj_in_channels;
             P3D_CUDA(ctx, cudaMemcpyAsync(f->proj_model, proj, sizeof(float) * hp_rows, cudaMemcpyDeviceToDevice,

@@ -263,6 +263,17 @@ __device__ __forceinline__ int32_t gather_src(const GemmParams &p, int t, int64_
     return (s >= p.M || s < 0) ? -1 : s;
 }
 
+// Residual epilogues read-modify-write the f32 output: pull this lane's row
+// segment into L2 while the tile's MMAs run, so the epilogue's loads hit L2.
+__device__ __forceinline__ void prefetch_residual(const GemmParams &p, int64_t row, int64_t n0, int cols) {
+    if (!(p.epi & P3D_EPI_RESIDUAL) || row >= p.M || n0 >= p.N) return;
+    const float *rp = reinterpret_cast<const float *>(p.out) + row * p.ldo + n0;
+    const int64_t c = p.N - n0 < cols ? p.N - n0 : cols;
+    const uint32_t bytes = static_cast<uint32_t>(c * 4) & ~15u;
+    if (bytes == 0 || (reinterpret_cast<uintptr_t>(rp) & 15) != 0) return;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rp), "r"(bytes) : "memory");
+}
+
 // One producer stage of the gather variant, issued by the 128 producer
 // threads: A rows [m0, m0+128), columns [kc, kc+64) of x[src(row)], where
 // thread t holds src of row m0 + t.  Warp w owns tile rows [32w, 32w+32);
@@ -453,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
+            prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
             if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             epilogue_rows<BN>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
@@ -744,6 +756,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
             const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
             const int64_t n0 = (tile % n_tiles) * PAIR_N;
+            prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
             if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             epilogue_rows<C::ACC_COLS>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
