@@ -2,6 +2,8 @@
 // LayerNorm (+affine) (+AdaLN modulate), per-head RMS norm + 3D RoPE,
 // activations, GroupNorm (+SiLU), and the Euler/CFG flow update.
 // All are HBM-bound: one read and one write of each row, f32 math.
+#include <algorithm>
+
 #include "p3d_common.cuh"
 
 namespace p3d {
@@ -286,6 +288,7 @@ __global__ void groupnorm_stats_kernel(const float *__restrict__ x, int64_t n, i
     const int rows_step = blockDim.x / tpr;
     const int t = threadIdx.x;
     const int col4 = t % tpr, rsub = t / tpr;
+    if (rsub >= rows_step) return;  // blockDim not a multiple of tpr: spare threads
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
     const int64_t r1 = min(n, r0 + rows_per_block);
     const int gs4 = (C / groups) / 4;  // float4 per group
@@ -315,6 +318,84 @@ __global__ void groupnorm_stats_kernel(const float *__restrict__ x, int64_t n, i
     }
 }
 
+// Stats, rows layout (C = 128 * NV): a block owns a contiguous row range,
+// split at batch-item boundaries; each warp reads whole rows (lane l holds
+// float4 l + 32j, j < NV: every load instruction covers 512 contiguous bytes,
+// NV loads in flight per lane) and keeps per-j f32 partial sums over its few
+// rows (a handful of rows x 4 channels per lane).  Lanes sharing a group are
+// combined in double by shuffles when the group is a power-of-two number of
+// float4 wide (or a multiple of 128 channels), then per block in shared
+// memory (double), then one global double atomic per group and batch segment.
+template <int NV>
+__global__ void __launch_bounds__(256, 3) groupnorm_stats_rows_kernel(const float *__restrict__ x, int64_t n,
+                                                                     int groups, const int32_t *__restrict__ offsets,
+                                                                     int nbatch, int64_t rows_per_block,
+                                                                     double *__restrict__ stats) {
+    extern __shared__ double gsum[];  // [2 * groups]
+    constexpr int C = 128 * NV;
+    const int gs = C / groups;
+    const int w = gs >> 2;  // lanes per group within one 128-channel block
+    const int mode = (gs % 128 == 0) ? 2 : ((w & (w - 1)) == 0 ? 1 : 0);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+    const int64_t r1 = min(n, r0 + rows_per_block);
+    for (int i = threadIdx.x; i < 2 * groups; i += blockDim.x) gsum[i] = 0.0;
+    __syncthreads();
+    for (int b = 0; b < nbatch; ++b) {
+        const int64_t s0 = max(r0, static_cast<int64_t>(offsets[b]));
+        const int64_t s1 = min(r1, static_cast<int64_t>(offsets[b + 1]));
+        if (s0 >= s1) continue;  // block-uniform
+        float sum[NV], sq[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) sum[j] = sq[j] = 0.0f;
+        for (int64_t r = s0 + warp; r < s1; r += nwarps) {
+            const float4 *xr = reinterpret_cast<const float4 *>(x + r * C) + lane;
+            float4 v[NV];
+#pragma unroll
+            for (int j = 0; j < NV; ++j) v[j] = __ldg(xr + 32 * j);
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                sum[j] += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+                sq[j] += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            double su = sum[j], qu = sq[j];
+            const int g = (128 * j + 4 * lane) / gs;
+            if (mode == 2) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    su += __shfl_xor_sync(0xffffffffu, su, o);
+                    qu += __shfl_xor_sync(0xffffffffu, qu, o);
+                }
+                if (lane == 0) {
+                    atomicAdd(&gsum[2 * g], su);
+                    atomicAdd(&gsum[2 * g + 1], qu);
+                }
+            } else if (mode == 1) {
+                for (int o = 1; o < w; o <<= 1) {
+                    su += __shfl_xor_sync(0xffffffffu, su, o);
+                    qu += __shfl_xor_sync(0xffffffffu, qu, o);
+                }
+                if ((lane & (w - 1)) == 0) {
+                    atomicAdd(&gsum[2 * g], su);
+                    atomicAdd(&gsum[2 * g + 1], qu);
+                }
+            } else {
+                atomicAdd(&gsum[2 * g], su);
+                atomicAdd(&gsum[2 * g + 1], qu);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 2 * groups; i += blockDim.x) {
+            if (gsum[i] != 0.0) atomicAdd(stats + 2 * b * groups + i, gsum[i]);
+            gsum[i] = 0.0;
+        }
+        __syncthreads();
+    }
+}
+
 // mean / rstd per (batch, group) from the double sums.
 __global__ void groupnorm_finalize_kernel(const double *__restrict__ stats, const int32_t *__restrict__ offsets,
                                           int nbatch, int groups, int C, float eps, float *__restrict__ mr) {
@@ -328,37 +409,111 @@ __global__ void groupnorm_finalize_kernel(const double *__restrict__ stats, cons
     mr[2 * i + 1] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
 }
 
-// y = silu((x - mean) * rstd * gamma + beta): one float4 per thread.
-template <typename TO>
-__global__ void groupnorm_apply_kernel(const float *__restrict__ x, int64_t n, int C, int groups,
-                                       const float *__restrict__ gamma, const float *__restrict__ beta,
-                                       const int32_t *__restrict__ offsets, int nbatch, const float *__restrict__ mr,
-                                       int silu, TO *__restrict__ out) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int c4 = C / 4;
-    if (i >= n * c4) return;
-    const int64_t row = i / c4;
-    const int cb = static_cast<int>(i - row * c4);
-    const int b = batch_of_row(offsets, nbatch, row);
-    const int g = (cb * 4) / (C / groups);
-    const float mean = mr[2 * (b * groups + g)], rstd = mr[2 * (b * groups + g) + 1];
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
-    float y[4] = {v.x, v.y, v.z, v.w};
+// Apply, rows layout (C = 128 * NV): a warp per row (grid-stride), lane l
+// holds float4 l + 32j as in the stats kernel, so neither a row index
+// division nor a per-element batch search is needed; all NV loads of a row
+// are issued before its math.
+template <int NV, typename TO>
+__global__ void __launch_bounds__(256, 3) groupnorm_apply_rows_kernel(const float *__restrict__ x, int64_t n,
+                                                                      int groups, const float *__restrict__ gamma,
+                                                                      const float *__restrict__ beta,
+                                                                      const int32_t *__restrict__ offsets, int nbatch,
+                                                                      const float *__restrict__ mr, int silu,
+                                                                      TO *__restrict__ out) {
+    constexpr int C = 128 * NV;
+    const int gs = C / groups;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += warps) {
+        const float4 *xr = reinterpret_cast<const float4 *>(x + r * C) + lane;
+        float4 v[NV];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const int c = cb * 4 + e;
-        float t = (y[e] - mean) * rstd;
-        if (gamma) t = t * __ldg(gamma + c) + __ldg(beta + c);
-        y[e] = silu ? silu_f(t) : t;
+        for (int j = 0; j < NV; ++j) v[j] = __ldg(xr + 32 * j);
+        const float *mrb = mr + 2 * batch_of_row(offsets, nbatch, r) * groups;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int cb = lane + 32 * j;  // float4 index within the row
+            const int g = (cb * 4) / gs;
+            const float mean = __ldg(mrb + 2 * g), rstd = __ldg(mrb + 2 * g + 1);
+            float y[4] = {(v[j].x - mean) * rstd, (v[j].y - mean) * rstd, (v[j].z - mean) * rstd,
+                          (v[j].w - mean) * rstd};
+            if (gamma) {
+                const float4 ga = __ldg(reinterpret_cast<const float4 *>(gamma) + cb);
+                const float4 be = __ldg(reinterpret_cast<const float4 *>(beta) + cb);
+                y[0] = y[0] * ga.x + be.x;
+                y[1] = y[1] * ga.y + be.y;
+                y[2] = y[2] * ga.z + be.z;
+                y[3] = y[3] * ga.w + be.w;
+            }
+            if (silu) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) y[e] = silu_f(y[e]);
+            }
+            TO *o = out + r * C + cb * 4;
+            if constexpr (sizeof(TO) == 2) {
+                uint2 pk;
+                pk.x = pack2<TO>(y[0], y[1]);
+                pk.y = pack2<TO>(y[2], y[3]);
+                *reinterpret_cast<uint2 *>(o) = pk;
+            } else {
+                *reinterpret_cast<float4 *>(o) = make_float4(y[0], y[1], y[2], y[3]);
+            }
+        }
     }
-    TO *o = out + i * 4;
-    if constexpr (sizeof(TO) == 2) {
-        uint2 pk;
-        pk.x = pack2<TO>(y[0], y[1]);
-        pk.y = pack2<TO>(y[2], y[3]);
-        *reinterpret_cast<uint2 *>(o) = pk;
-    } else {
-        *reinterpret_cast<float4 *>(o) = make_float4(y[0], y[1], y[2], y[3]);
+}
+
+// y = silu((x - mean) * rstd * gamma + beta).  Each thread handles 4 float4
+// spaced blockDim apart (coalesced), all 4 loads issued before any math.
+constexpr int kGnApplyVec = 4;
+template <typename TO>
+__global__ void __launch_bounds__(256) groupnorm_apply_kernel(const float *__restrict__ x, int64_t n, int C,
+                                                              int groups, const float *__restrict__ gamma,
+                                                              const float *__restrict__ beta,
+                                                              const int32_t *__restrict__ offsets, int nbatch,
+                                                              const float *__restrict__ mr, int silu,
+                                                              TO *__restrict__ out) {
+    const int c4 = C / 4;
+    const int gs = C / groups;
+    const int64_t total = n * c4;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x * kGnApplyVec + threadIdx.x;
+    float4 v[kGnApplyVec];
+#pragma unroll
+    for (int k = 0; k < kGnApplyVec; ++k) {
+        const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
+        if (i < total) v[k] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kGnApplyVec; ++k) {
+        const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
+        if (i >= total) break;
+        const int64_t row = i / c4;
+        const int cb = static_cast<int>(i - row * c4);
+        const int b = batch_of_row(offsets, nbatch, row);
+        const int g = (cb * 4) / gs;
+        const float mean = __ldg(mr + 2 * (b * groups + g)), rstd = __ldg(mr + 2 * (b * groups + g) + 1);
+        float y[4] = {(v[k].x - mean) * rstd, (v[k].y - mean) * rstd, (v[k].z - mean) * rstd,
+                      (v[k].w - mean) * rstd};
+        if (gamma) {
+            const float4 ga = __ldg(reinterpret_cast<const float4 *>(gamma) + cb);
+            const float4 be = __ldg(reinterpret_cast<const float4 *>(beta) + cb);
+            y[0] = y[0] * ga.x + be.x;
+            y[1] = y[1] * ga.y + be.y;
+            y[2] = y[2] * ga.z + be.z;
+            y[3] = y[3] * ga.w + be.w;
+        }
+        if (silu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) y[e] = silu_f(y[e]);
+        }
+        TO *o = out + i * 4;
+        if constexpr (sizeof(TO) == 2) {
+            uint2 pk;
+            pk.x = pack2<TO>(y[0], y[1]);
+            pk.y = pack2<TO>(y[2], y[3]);
+            *reinterpret_cast<uint2 *>(o) = pk;
+        } else {
+            *reinterpret_cast<float4 *>(o) = make_float4(y[0], y[1], y[2], y[3]);
+        }
     }
 }
 
@@ -572,12 +727,33 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
                 "p3d_group_norm_silu: channels/groups must be a multiple of 4");
     P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
                 "p3d_group_norm_silu: x/out must be 16-byte aligned");
+    P3D_REQUIRE(ctx, !gamma || (beta && (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 &&
+                                (reinterpret_cast<uintptr_t>(beta) & 15) == 0),
+                "p3d_group_norm_silu: gamma/beta must be 16-byte aligned");
     // stats scratch: [nbatch*groups*2] double sums, then [nbatch*groups*2] float mean/rstd
     P3D_CUDA(ctx, cudaMemsetAsync(stats, 0, sizeof(double) * 2 * nbatch * groups, ctx->stream));
     if (n == 0) return P3D_OK;
-    const int rows_per_block = 64;
-    groupnorm_stats_kernel<<<blocks_for(n, rows_per_block), 256, 0, ctx->stream>>>(
-        x, n, channels, groups, batch_offsets, nbatch, rows_per_block, stats);
+    // Rows-layout kernels for C = 128 * NV (NV in 1, 2, 4, 8, 16).
+    const int nv = channels % 128 == 0 ? channels / 128 : 0;
+    const bool rows = nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 16;
+    if (rows) {
+        // ~4 resident blocks per SM, each a contiguous row range
+        const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 16), 4 * ctx->num_sms));
+        const int64_t rpb = ceil_div(n, blocks);
+        const unsigned grid = static_cast<unsigned>(ceil_div(n, rpb));
+        const size_t sm = 2 * groups * sizeof(double);
+        switch (nv) {
+            case 1: groupnorm_stats_rows_kernel<1><<<grid, 256, sm, ctx->stream>>>(x, n, groups, batch_offsets, nbatch, rpb, stats); break;
+            case 2: groupnorm_stats_rows_kernel<2><<<grid, 256, sm, ctx->stream>>>(x, n, groups, batch_offsets, nbatch, rpb, stats); break;
+            case 4: groupnorm_stats_rows_kernel<4><<<grid, 256, sm, ctx->stream>>>(x, n, groups, batch_offsets, nbatch, rpb, stats); break;
+            case 8: groupnorm_stats_rows_kernel<8><<<grid, 256, sm, ctx->stream>>>(x, n, groups, batch_offsets, nbatch, rpb, stats); break;
+            default: groupnorm_stats_rows_kernel<16><<<grid, 256, sm, ctx->stream>>>(x, n, groups, batch_offsets, nbatch, rpb, stats); break;
+        }
+    } else {
+        const int rows_per_block = 64;
+        groupnorm_stats_kernel<<<blocks_for(n, rows_per_block), 256, 0, ctx->stream>>>(
+            x, n, channels, groups, batch_offsets, nbatch, rows_per_block, stats);
+    }
     int rc = check_launch(ctx, "groupnorm_stats");
     if (rc) return rc;
     float *mr = reinterpret_cast<float *>(stats + 2 * nbatch * groups);
@@ -585,8 +761,24 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
         stats, batch_offsets, nbatch, groups, channels, eps, mr);
     if ((rc = check_launch(ctx, "groupnorm_finalize"))) return rc;
     const int64_t count4 = n * (channels / 4);
+    if (rows) {
+        const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(n, 8), 16 * ctx->num_sms));
+#define P3D_GN_APPLY(NV_)                                                                                      \
+    P3D_DISPATCH(out_dtype, TO,                                                                                \
+                 groupnorm_apply_rows_kernel<NV_, TO><<<grid, 256, 0, ctx->stream>>>(                          \
+                     x, n, groups, gamma, beta, batch_offsets, nbatch, mr, silu, static_cast<TO *>(out)))
+        switch (nv) {
+            case 1: P3D_GN_APPLY(1); break;
+            case 2: P3D_GN_APPLY(2); break;
+            case 4: P3D_GN_APPLY(4); break;
+            case 8: P3D_GN_APPLY(8); break;
+            default: P3D_GN_APPLY(16); break;
+        }
+#undef P3D_GN_APPLY
+        return check_launch(ctx, "groupnorm_apply");
+    }
     P3D_DISPATCH(out_dtype, TO,
-                 groupnorm_apply_kernel<TO><<<blocks_for(count4, 256), 256, 0, ctx->stream>>>(
+                 groupnorm_apply_kernel<TO><<<blocks_for(count4, 256 * kGnApplyVec), 256, 0, ctx->stream>>>(
                      x, n, channels, groups, gamma, beta, batch_offsets, nbatch, mr, silu, static_cast<TO *>(out)));
     return check_launch(ctx, "groupnorm_apply");
 }

@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "p3d_common.cuh"
@@ -66,7 +67,17 @@ struct GemmParams {
     int64_t norm_cols, rope_cols;
     const float *norm_gamma;
     const float2 *rope;
+    // 1: the epilogue stages 32 x 32 boxes in shared memory and writes them
+    // with TMA through tmap_o (store, or reduce-add for the residual).
+    int tma_out;
 };
+
+// TMA-store epilogue staging: each of the 4 epilogue warps owns two 4 KB
+// slots, each one 32-row x 128-byte box (32 f32 or 64 16-bit columns) in the
+// 128-byte swizzle.
+constexpr int EPI_SLOT_BYTES = 4096;
+constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT_BYTES;
+constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 // 1-CTA tile: 128 x BN, BK = 64; accumulators double-buffered in TMEM.
 template <int BN>
@@ -78,7 +89,7 @@ struct Cfg {
     static constexpr int ACC_COLS = BN;
     static constexpr int ACC_BUFS = 2;
     static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // CTA-pair tile: 256 x (NSUB * 256).  Each CTA of the pair stages its own 128
@@ -95,7 +106,7 @@ struct Cfg2 {
     static constexpr int ACC_COLS = NSUB * 256;
     static constexpr int ACC_BUFS = NSUB == 1 ? 2 : 1;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 template <typename T>
@@ -253,6 +264,231 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc
     }
 }
 
+// v[i] += b[i] for a warp-uniform 32-column vector (bias, gamma): float4
+// loads when the vector is 16-byte aligned and whole.
+__device__ __forceinline__ void add_vec32(float (&v)[32], const float *b, int ncols) {
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(b) & 15) == 0) {
+#pragma unroll
+        for (int h = 0; h < 8; h += 4) {  // 4 vector loads in flight at a time
+            float4 t[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[i] = __ldg(reinterpret_cast<const float4 *>(b) + h + i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[4 * (h + i)] += t[i].x;
+                v[4 * (h + i) + 1] += t[i].y;
+                v[4 * (h + i) + 2] += t[i].z;
+                v[4 * (h + i) + 3] += t[i].w;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < ncols) v[i] += __ldg(b + i);
+    }
+}
+
+__device__ __forceinline__ void mul_vec32(float (&v)[32], const float *g, int ncols) {
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+#pragma unroll
+        for (int h = 0; h < 8; h += 4) {  // 4 vector loads in flight at a time
+            float4 t[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[i] = __ldg(reinterpret_cast<const float4 *>(g) + h + i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[4 * (h + i)] *= t[i].x;
+                v[4 * (h + i) + 1] *= t[i].y;
+                v[4 * (h + i) + 2] *= t[i].z;
+                v[4 * (h + i) + 3] *= t[i].w;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < ncols) v[i] *= __ldg(g + i);
+    }
+}
+
+// Staging slot for the next box: wait until the box last issued from this
+// slot (two boxes ago) has been read by the TMA unit.
+__device__ __forceinline__ uint8_t *acquire_slot(uint8_t *wbuf, int slot, int lane) {
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    return wbuf + slot * EPI_SLOT_BYTES;
+}
+
+// This lane's 32 values as row `lane` of the slot, in the 128-byte swizzle
+// (16-byte chunk c of a 128-byte row at c ^ (row & 7)).  f32: the whole
+// 128-byte row; 16-bit: half `half` (columns 32*half .. +31) of a 64-column row.
+__device__ __forceinline__ void stage_row(int out_dtype, uint8_t *buf, int lane, const float (&v)[32], int half) {
+    uint8_t *rowp = buf + lane * 128;
+    if (out_dtype == P3D_F32) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        return;
+    }
+    const bool bf = out_dtype == P3D_BF16;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint4 pk;
+        pk.x = bf ? pack2<__nv_bfloat16>(v[8 * c], v[8 * c + 1]) : pack2<__half>(v[8 * c], v[8 * c + 1]);
+        pk.y = bf ? pack2<__nv_bfloat16>(v[8 * c + 2], v[8 * c + 3]) : pack2<__half>(v[8 * c + 2], v[8 * c + 3]);
+        pk.z = bf ? pack2<__nv_bfloat16>(v[8 * c + 4], v[8 * c + 5]) : pack2<__half>(v[8 * c + 4], v[8 * c + 5]);
+        pk.w = bf ? pack2<__nv_bfloat16>(v[8 * c + 6], v[8 * c + 7]) : pack2<__half>(v[8 * c + 6], v[8 * c + 7]);
+        *reinterpret_cast<uint4 *>(rowp + (((4 * half + c) ^ (lane & 7)) << 4)) = pk;
+    }
+}
+
+// Lane 0 writes the staged 32-row box at (col0, row0): a TMA store, or for
+// the residual epilogue a TMA reduce-add into the f32 stream.  Rows >= M and
+// columns >= N of the box are clipped by the tensor map's bounds.
+__device__ __forceinline__ void issue_box(const GemmParams &p, const CUtensorMap *tmo, const uint8_t *buf, int lane,
+                                          int64_t col0, int64_t row0, int &slot) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        if (p.epi & P3D_EPI_RESIDUAL)
+            tma_reduce_add_2d(tmo, buf, static_cast<int>(col0), static_cast<int>(row0));
+        else
+            tma_store_2d(tmo, buf, static_cast<int>(col0), static_cast<int>(row0));
+        bulk_commit();
+    }
+    slot ^= 1;
+}
+
+// Bias, activation and residual gate of one 32-column chunk of row `row`;
+// false when the chunk lies entirely at or beyond column N (warp-uniform).
+__device__ __forceinline__ bool prep_chunk(const GemmParams &p, int64_t row, int64_t col0, float (&v)[32]) {
+    if (col0 >= p.N) return false;
+    const int ncols = static_cast<int>(p.N - col0 < 32 ? p.N - col0 : 32);
+    if (p.bias) add_vec32(v, p.bias + col0, ncols);
+    if (p.epi & P3D_EPI_GELU_TANH) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
+    } else if (p.epi & P3D_EPI_SILU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu_f(v[i]);
+    }
+    if ((p.epi & P3D_EPI_RESIDUAL) && p.gate) {
+        const int b = batch_of_row(p.batch_offsets, p.nbatch, row);
+        mul_vec32(v, p.gate + static_cast<int64_t>(b) * p.gate_ld + col0, ncols);
+    }
+    return true;
+}
+
+// Rotate the 16 (even, odd) pairs of v by (cos, sin) = (r[i/2].x, .y) for
+// even i and (r[i/2].z, .w) for odd i.
+__device__ __forceinline__ void rope_rotate16(float (&v)[32], const float4 (&r)[8]) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float c = (i & 1) ? r[i >> 1].z : r[i >> 1].x;
+        const float sn = (i & 1) ? r[i >> 1].w : r[i >> 1].y;
+        const float e = v[2 * i], o = v[2 * i + 1];
+        v[2 * i] = e * c - o * sn;
+        v[2 * i + 1] = e * sn + o * c;
+    }
+}
+
+// TMA-store epilogue of one warp for one accumulator buffer (rows row0 ..
+// row0+31, accumulator columns [0, COLS) = output columns n0 + c).  Boxes
+// are 32 rows x 128 bytes: 32 f32 columns, or 64 16-bit columns staged from
+// two 32-column chunks.  The next chunk's tcgen05.ld is in flight while the
+// current one is finished.
+template <int COLS>
+__device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUtensorMap *tmo, uint32_t tacc,
+                                                  int64_t row0, int lane, int64_t n0, uint8_t *wbuf, int &slot) {
+    static_assert(COLS % 64 == 0, "epilogue column count");
+    const int64_t row = row0 + lane;
+    const bool f32 = p.out_dtype == P3D_F32;
+    float a[32], b[32];
+    if (p.norm_cols > 0 || p.rope_cols > 0) {
+        // Per-head RMS norm + RoPE over 64-column heads (N % 64 == 0).  The
+        // head's second half is read from TMEM twice (for the norm, then
+        // for its output) so only one half plus its RoPE pairs stay live.
+#pragma unroll 1
+        for (int cs = 0; cs < COLS; cs += 64) {
+            const int64_t col0 = n0 + cs;
+            if (col0 >= p.N) break;  // warp-uniform
+            __syncwarp();
+            tmem_ld32(tacc + cs, a);
+            tmem_ld32(tacc + cs + 32, b);
+            const bool rope = col0 < p.rope_cols;
+            const bool norm = col0 < p.norm_cols;
+            const float4 *rp = reinterpret_cast<const float4 *>(p.rope + (row < p.M ? row : 0) * 32);
+            tmem_ld_wait_regs(a);
+            tmem_ld_wait_regs(b);
+            if (p.bias) {
+                add_vec32(a, p.bias + col0, 32);
+                add_vec32(b, p.bias + col0 + 32, 32);
+            }
+            float inv = 1.0f;
+            if (norm) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ss += a[i] * a[i] + b[i] * b[i];
+                inv = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) / max(||v||, eps)
+            }
+            uint8_t *buf = acquire_slot(wbuf, slot, lane);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                if (half == 1) {
+                    __syncwarp();
+                    tmem_ld32(tacc + cs + 32, a);
+                    tmem_ld_wait_regs(a);
+                    if (p.bias) add_vec32(a, p.bias + col0 + 32, 32);
+                    if (f32) buf = acquire_slot(wbuf, slot, lane);
+                }
+                if (norm) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) a[i] *= inv;
+                    mul_vec32(a, p.norm_gamma + col0 + 32 * half, 32);
+                }
+                if (rope) {
+                    float4 r4[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) r4[i] = __ldg(rp + 8 * half + i);
+                    rope_rotate16(a, r4);
+                }
+                stage_row(p.out_dtype, buf, lane, a, f32 ? 0 : half);
+                if (f32) issue_box(p, tmo, buf, lane, col0 + 32 * half, row0, slot);
+            }
+            if (!f32) issue_box(p, tmo, buf, lane, col0, row0, slot);
+        }
+        return;
+    }
+    __syncwarp();
+    tmem_ld32(tacc, a);
+    tmem_ld_wait_regs(a);
+#pragma unroll 1
+    for (int cs = 0; cs < COLS; cs += 64) {
+        const int64_t col0 = n0 + cs;
+        const bool more = cs + 64 < COLS;
+        __syncwarp();
+        tmem_ld32(tacc + cs + 32, b);
+        uint8_t *buf = acquire_slot(wbuf, slot, lane);
+        const bool any = prep_chunk(p, row, col0, a);
+        if (any) {
+            stage_row(p.out_dtype, buf, lane, a, 0);
+            if (f32) issue_box(p, tmo, buf, lane, col0, row0, slot);
+        }
+        tmem_ld_wait_regs(b);
+        if (more) {
+            __syncwarp();
+            tmem_ld32(tacc + cs + 64, a);
+        }
+        if (f32) buf = acquire_slot(wbuf, slot, lane);
+        if (prep_chunk(p, row, col0 + 32, b)) {
+            stage_row(p.out_dtype, buf, lane, b, f32 ? 0 : 1);
+            if (f32) issue_box(p, tmo, buf, lane, col0 + 32, row0, slot);
+        }
+        if (!f32 && any) issue_box(p, tmo, buf, lane, col0, row0, slot);
+        if (more) tmem_ld_wait_regs(a);
+    }
+}
+
 // Source row of tile row m0 + (t & 127) for tap `tap` (sentinel or out of
 // range -> -1, i.e. zero fill).  Loaded one tap ahead of its use so the
 // gather's issue never waits on this load.
@@ -305,7 +541,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *f
 template <int BN, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
     using C = Cfg<BN>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -313,7 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t *smem_a = smem;
     uint8_t *smem_b = smem + STAGES * C::A_BYTES;
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_b + STAGES * C::B_BYTES);
+    uint8_t *smem_o = smem_b + STAGES * C::B_BYTES;  // epilogue staging, EPI_BYTES
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_o + EPI_BYTES);
     uint64_t *empty_bar = full_bar + STAGES;
     uint64_t *tfull_bar = empty_bar + STAGES;  // [2]
     uint64_t *tempty_bar = tfull_bar + 2;      // [2]
@@ -461,14 +698,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;  // TMEM lane quarter accessible to this warp
         int acc = 0;
         uint32_t acc_phase = 0;
+        int slot = 0;
         for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
-            prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
+            if (!p.tma_out) prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
             if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            epilogue_rows<BN>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
-                              m0 + q * 32 + lane, n0);
+            const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+            if (p.tma_out)
+                epilogue_rows_tma<BN>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES, slot);
+            else
+                epilogue_rows<BN>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -477,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1;
             }
         }
+        if (p.tma_out && lane == 0) bulk_wait_all();  // staging slots stay live until the stores land
     }
 
     __syncwarp();
@@ -519,7 +761,7 @@ __device__ __forceinline__ int4 gather_src4(const GemmParams &p, int lane, int64
 template <int NSUB, bool GATHER, bool TMAG = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
     using C = Cfg2<NSUB>;
     constexpr int STAGES = C::STAGES;
     constexpr int PAIR_N = NSUB * 256;
@@ -528,7 +770,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t *smem_a = smem;
     uint8_t *smem_b = smem + STAGES * C::A_BYTES;
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_b + STAGES * C::B_BYTES);
+    uint8_t *smem_o = smem_b + STAGES * C::B_BYTES;  // epilogue staging, EPI_BYTES
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_o + EPI_BYTES);
     uint64_t *empty_bar = full_bar + STAGES;
     uint64_t *tfull_bar = empty_bar + STAGES;  // [2]
     uint64_t *tempty_bar = tfull_bar + 2;      // [2]
@@ -753,14 +996,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
+        int slot = 0;
         for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
             const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
             const int64_t n0 = (tile % n_tiles) * PAIR_N;
-            prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
+            if (!p.tma_out) prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
             if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            epilogue_rows<C::ACC_COLS>(p, tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16),
-                                       m0 + q * 32 + lane, n0);
+            const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+            if (p.tma_out)
+                epilogue_rows_tma<C::ACC_COLS>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
+                                               slot);
+            else
+                epilogue_rows<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -775,6 +1023,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1;
             }
         }
+        if (p.tma_out && lane == 0) bulk_wait_all();  // staging slots stay live until the stores land
     }
 
     __syncwarp();
@@ -803,7 +1052,8 @@ EncodeFn get_encode_fn() {
 }
 
 template <int BN, bool GATHER>
-int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
+int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &to,
+                const GemmParams &p) {
     using C = Cfg<BN>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -813,12 +1063,13 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     }
     const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
-    gemm_tc_kernel<BN, GATHER><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    gemm_tc_kernel<BN, GATHER><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
 template <int NSUB, bool GATHER, bool TMAG = false>
-int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p) {
+int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &to,
+                 const GemmParams &p) {
     using C = Cfg2<NSUB>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -841,7 +1092,7 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
     }
     const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
-    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, p);
+    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
     return check_launch(ctx, "gemm2_tc_kernel");
 }
 
@@ -879,6 +1130,47 @@ bool conv_tma_gather() {
     return on;
 }
 
+// P3D_GEMM_TMA_STORE=0 selects the direct-store epilogue (lane = row,
+// vector stores / read-modify-write residual) instead of the TMA one.
+bool tma_store_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("P3D_GEMM_TMA_STORE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// The TMA epilogue needs a 16-byte aligned output with a 16-byte row pitch
+// and row coordinates that fit the map's int32 coordinates.
+bool tma_out_ok(const GemmParams &p) {
+    const int es = p.out_dtype == P3D_F32 ? 4 : 2;
+    return (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * es) % 16 == 0 && p.M < (int64_t(1) << 31) &&
+           p.N < (int64_t(1) << 31);
+}
+
+// Output map for the TMA epilogue: [M rows, N cols] at pitch ldo, boxes of
+// 32 rows x 128 bytes (32 f32 or 64 16-bit columns) in the 128-byte swizzle,
+// matching the staging layout of stage_row.
+int make_tmap_out(p3d_ctx *ctx, CUtensorMap *map, void *base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld) {
+    EncodeFn fn = get_encode_fn();
+    if (!fn) return set_error(ctx, P3D_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const bool f32 = dtype == P3D_F32;
+    const uint64_t es = f32 ? 4 : 2;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * es};
+    cuuint32_t box[2] = {f32 ? 32u : 64u, 32};  // 128-byte box rows
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : (dtype == P3D_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    CUresult r = fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(ctx, P3D_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string(r));
+    return P3D_OK;
+}
+
 // x == nullptr selects the gather (sparse conv) variant, whose B operand is
 // the [27 * N, K] tap stack.  Builds the tensor maps and instruction
 // descriptor for the chosen kernel and launches it.
@@ -886,7 +1178,14 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
     const bool gather = x == nullptr;
     const bool bf16 = ab_dtype == P3D_BF16;
     const int64_t w_rows = gather ? 27 * p.N : p.N;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, to;
+    std::memset(&to, 0, sizeof(to));
+    p.tma_out = 0;
+    if (tma_store_enabled() && tma_out_ok(p)) {
+        int rc = make_tmap_out(ctx, &to, p.out, p.out_dtype, p.M, p.N, p.ldo);
+        if (rc) return rc;
+        p.tma_out = 1;
+    }
     // The pair kernel serves the gather (conv) path, whose 27*Cin-long K loop
     // streams the most B bytes per output tile; for the dense linears
     // (K <= 4096) it measured no faster than the 1-CTA kernel on B200
@@ -902,11 +1201,11 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
         if (gather && conv_tma_gather()) {
             // A rows by TMA tile::gather4 from x [M][K] (box 64 x 1 row)
             if ((rc = make_tmap_16bit_2d(ctx, &ta, p.x, ab_dtype, p.M, p.K, p.ldx, 1))) return rc;
-            return nsub == 2 ? launch_gemm2<2, true, true>(ctx, ta, tb, p) : launch_gemm2<1, true, true>(ctx, ta, tb, p);
+            return nsub == 2 ? launch_gemm2<2, true, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true, true>(ctx, ta, tb, to, p);
         }
         if (gather) ta = tb;
-        if (gather) return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, p) : launch_gemm2<1, true>(ctx, ta, tb, p);
-        return launch_gemm2<1, false>(ctx, ta, tb, p);
+        if (gather) return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true>(ctx, ta, tb, to, p);
+        return launch_gemm2<1, false>(ctx, ta, tb, to, p);
     }
     const int bn = pick_bn(p.N);
     int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, bn);
@@ -915,13 +1214,13 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
     if (gather) ta = tb;
     p.idesc = idesc_f32acc(BM, bn, bf16);
     if (gather) {
-        if (bn == 64) return launch_gemm<64, true>(ctx, ta, tb, p);
-        if (bn == 128) return launch_gemm<128, true>(ctx, ta, tb, p);
-        return launch_gemm<256, true>(ctx, ta, tb, p);
+        if (bn == 64) return launch_gemm<64, true>(ctx, ta, tb, to, p);
+        if (bn == 128) return launch_gemm<128, true>(ctx, ta, tb, to, p);
+        return launch_gemm<256, true>(ctx, ta, tb, to, p);
     }
-    if (bn == 64) return launch_gemm<64, false>(ctx, ta, tb, p);
-    if (bn == 128) return launch_gemm<128, false>(ctx, ta, tb, p);
-    return launch_gemm<256, false>(ctx, ta, tb, p);
+    if (bn == 64) return launch_gemm<64, false>(ctx, ta, tb, to, p);
+    if (bn == 128) return launch_gemm<128, false>(ctx, ta, tb, to, p);
+    return launch_gemm<256, false>(ctx, ta, tb, to, p);
 }
 
 }  // namespace

@@ -1,4 +1,5 @@
-"""Micro-benchmarks of single kernels of the SLat path (device time, CUDA events).
+"""Micro-benchmarks of single kernels of the SLat path (device time: CUDA
+events around a CUDA-graph replay of --reps calls).
 
     python -m pixal3d.cpp_b200.kernel_bench --kernel conv1024 [--reps 10]
 
@@ -8,6 +9,10 @@ Kernels (config-2 shapes unless noted):
   qkv        trunk qkv linear, 8,184 x 1024 -> 3072
   mlp0       trunk MLP up-projection with GELU, 8,184 x 1024 -> 4096
   qkvn       qkv linear with the fused q/k head RMS norm + RoPE epilogue
+  out        attention output projection into the f32 residual, gated
+  mlp2       MLP down-projection (K = 4096) into the f32 residual, gated
+  proj       fine-level input projection, 43,532 x 64 -> 1024, f32 out
+  gn         GroupNorm(32) + SiLU, 43,532 x 1024 f32 -> f16 (stats + apply)
   ln         trunk LayerNorm + AdaLN modulation, 8,184 x 1024 f32 -> f16
   attn       trunk self-attention, 2 sequences x 4,092, 16 heads x 64
   cross      trunk cross-attention, 2 x 4,092 queries x 1,029 keys
@@ -30,13 +35,30 @@ C = 1024
 
 
 def _time(fn, reps):
+    """Device time per call: `reps` calls captured in one CUDA graph and
+    replayed between two events (no host launch cost in the interval);
+    eager launches when the call cannot be captured."""
     for _ in range(2):
         fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+    except RuntimeError:
+        graph = None
+        torch.cuda.synchronize()
     e0.record()
-    for _ in range(reps):
-        fn()
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(reps):
+            fn()
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / reps
@@ -74,6 +96,37 @@ def run(kernel: str, reps: int) -> dict:
         ms = _time(lambda: ops.linear(x, w, b, out=out, epilogue=epi), reps)
         flops = 2.0 * m * C * nout
         return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "m": m, "n": nout, "k": C}
+    if kernel in ("out", "mlp2", "proj"):
+        # gated residual linears of the trunk (f32 residual stream), and the
+        # fine-level input projection (f32 output, K = 64)
+        m = 2 * 4092 if kernel != "proj" else 2 * 21766
+        k = {"out": C, "mlp2": 4 * C, "proj": 64}[kernel]
+        x = torch.randn((m, k), device=dev, generator=g).to(h)
+        w = (torch.randn((C, k), device=dev, generator=g) / math.sqrt(k)).to(h)
+        b = torch.zeros(C, device=dev)
+        out = torch.zeros((m, C), device=dev)
+        if kernel == "proj":
+            ms = _time(lambda: ops.linear(x, w, b, out=out), reps)
+        else:
+            gate = torch.randn((2, C), device=dev, generator=g)
+            offs = torch.tensor([0, m // 2, m], dtype=torch.int32, device=dev)
+            ms = _time(lambda: ops.linear(x, w, b, out=out, epilogue=L.EPI_RESIDUAL, gate=gate,
+                                          batch_offsets=offs), reps)
+        flops = 2.0 * m * C * k
+        bytes_ = m * k * 2 + C * k * 2 + m * C * 4 * (1 if kernel == "proj" else 2)
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6, "flops": flops,
+                "m": m, "n": C, "k": k}
+    if kernel == "gn":
+        # io-resblock GroupNorm(32) + SiLU on the fine level, f32 -> f16
+        cc = batched(shell_coords(), 2)
+        n = cc.shape[0]
+        x = torch.randn((n, C), device=dev, generator=g)
+        gam = torch.ones(C, device=dev)
+        bet = torch.zeros(C, device=dev)
+        offs = torch.tensor([0, n // 2, n], dtype=torch.int32, device=dev)
+        ms = _time(lambda: ops.group_norm_silu(x, 32, 1e-5, gam, bet, offs, True, h), reps)
+        bytes_ = 2 * n * C * 4 + n * C * 2  # stats read + apply read + f16 write
+        return {"kernel": kernel, "ms": ms, "gbs": bytes_ / ms / 1e6, "bytes": bytes_, "rows": n}
     if kernel == "qkvn":
         m = 2 * 4092
         coords = torch.from_numpy(batched(shell_coords(), 2)[:m]).to(dev)

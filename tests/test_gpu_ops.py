@@ -173,7 +173,7 @@ def test_c2s_bitexact():
 # -------------------------------------------------------- contractions
 
 @pytest.mark.parametrize("m,n,k", [(1, 64, 64), (130, 8, 8), (300, 96, 72), (4133, 256, 64), (1000, 384, 1024),
-                                   (777, 200, 136), (8192, 1024, 1024)])
+                                   (777, 200, 136), (8192, 1024, 1024), (65, 100, 64)])
 def test_linear_shapes(m, n, k):
     rng = np.random.default_rng(m + n + k)
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -210,6 +210,76 @@ def test_linear_epilogues():
     bidx = np.where(np.arange(m) < 600, 0, 1)
     exp = res + gate[bidx] * ref
     check(out.cpu().numpy(), exp, max_abs=bf16_out_tol(exp) / 4, what="residual epilogue")
+
+
+def test_linear_residual_output_view():
+    """Gated residual into a column slice of a wider f32 buffer: ragged rows
+    and columns (the TMA epilogue's boxes are clipped at the view's bounds),
+    three batch items; columns outside the view stay untouched."""
+    rng = np.random.default_rng(31)
+    m, n, k, ld = 777, 200, 128, 256
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    big = rng.standard_normal((m, ld)).astype(np.float32)
+    gate = rng.standard_normal((3, n)).astype(np.float32)
+    offs = np.array([0, 100, 500, m], np.int32)
+    buf = dev(big.copy())
+    view = buf[:, 32:32 + n]
+    o = ops()
+    o.linear(bf(x), bf(w), dev(b), out=view, epilogue=L().EPI_RESIDUAL, gate=dev(gate), batch_offsets=dev(offs))
+    got = buf.cpu().numpy()
+    bidx = np.searchsorted(offs, np.arange(m), side="right") - 1
+    exp = big[:, 32:32 + n] + gate[bidx] * (rounded(x) @ rounded(w).T + b)
+    check(got[:, 32:32 + n], exp, max_abs=1e-3 * max(1.0, float(np.abs(exp).max())), rel_l2=1e-5,
+          what="residual into a view")
+    np.testing.assert_array_equal(got[:, :32], big[:, :32])
+    np.testing.assert_array_equal(got[:, 32 + n:], big[:, 32 + n:])
+
+
+def test_linear_direct_store_epilogue_subprocess(tmp_path):
+    """The direct-store epilogue (P3D_GEMM_TMA_STORE=0, read once per process)
+    agrees with the TMA epilogue on f32, 16-bit, residual and head-norm
+    outputs: bit for bit where both round the same expression once; within
+    one rounding where they differ (the residual: fused multiply-add against
+    gate*v then the add in L2; the head norm's sum of squares order)."""
+    import subprocess
+    import sys
+    import os
+    code = r"""
+import math, numpy as np, torch
+from pixal3d.cpp_b200 import ops, _lib as L
+from pixal3d.cpp_b200.workloads import shell_coords
+rng = np.random.default_rng(44)
+m, n, k = 1000, 384, 256
+x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda().half()
+w = torch.from_numpy((rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)).cuda().half()
+b = torch.from_numpy((rng.standard_normal(n) * 0.1).astype(np.float32)).cuda()
+res = torch.from_numpy(rng.standard_normal((m, n)).astype(np.float32)).cuda()
+gate = torch.from_numpy(rng.standard_normal((2, n)).astype(np.float32)).cuda()
+offs = torch.tensor([0, 600, m], dtype=torch.int32, device="cuda")
+coords = torch.from_numpy(shell_coords(24, 8.0, 1.0)[:m]).cuda()
+table = ops.rope_table(coords, 64)
+gam = torch.from_numpy((1 + 0.1 * rng.standard_normal(2 * 128)).astype(np.float32)).cuda()
+outs = [ops.linear(x, w, b, out_dtype=torch.float32), ops.linear(x, w, b, out_dtype=torch.float16, epilogue=L.EPI_GELU_TANH)]
+r = res.clone(); ops.linear(x, w, b, out=r, epilogue=L.EPI_RESIDUAL, gate=gate, batch_offsets=offs); outs.append(r)
+outs.append(ops.linear_headnorm(x, w, b, 128, gam, 256, table, out=torch.empty((m, n), device="cuda", dtype=torch.float16)))
+torch.save([t.cpu() for t in outs], "OUT")
+print("ok")
+"""
+    env = os.environ.copy()
+    got = []
+    for flag in ("1", "0"):
+        out = tmp_path / f"epilogue_{flag}.pt"
+        env["P3D_GEMM_TMA_STORE"] = flag
+        r = subprocess.run([sys.executable, "-c", code.replace("OUT", str(out))], env=env, capture_output=True,
+                           text=True, timeout=600, cwd=str(FX.GOLDEN.parent.parent))
+        assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+        got.append(torch.load(out))
+    tma, direct = got
+    assert torch.equal(tma[0], direct[0]) and torch.equal(tma[1], direct[1])
+    torch.testing.assert_close(tma[2], direct[2], rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(tma[3].float(), direct[3].float(), rtol=1e-3, atol=1e-3)
 
 
 def test_linear_strided_input():
@@ -431,18 +501,25 @@ def test_attention_strided_qkv_views():
     check(got.float().cpu().numpy(), exp, what="strided attention")
 
 
-def test_group_norm_silu():
-    rng = np.random.default_rng(21)
-    c = batched(shell_coords(24, 8.0, 1.0), 2)
-    n, C = c.shape[0], 256
+@pytest.mark.parametrize("C,groups", [(256, 32), (1024, 32), (512, 2), (384, 4), (192, 8)])
+def test_group_norm_silu(C, groups):
+    """Group widths that take each reduction of the stats kernel (shuffle over
+    a power-of-two lane group, whole warp, per-lane atomics) and a channel
+    count outside its rows layout (C % 128 != 0); three batch items."""
+    rng = np.random.default_rng(21 + C)
+    c = batched(shell_coords(24, 8.0, 1.0), 3)
+    n = c.shape[0]
     x = (rng.standard_normal((n, C)) * 2 + 0.5).astype(np.float32)
     gam = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
     bet = (rng.standard_normal(C) * 0.1).astype(np.float32)
     o = ops()
-    offs = o.batch_offsets_of(dev(c), 2)
-    got = o.group_norm_silu(dev(x), 32, 1e-5, dev(gam), dev(bet), offs, True, torch.float32).cpu().numpy()
-    exp = O.silu(O.group_norm(c[:, 0].astype(np.int64), x, 32, 1e-5, gam, bet))
+    offs = o.batch_offsets_of(dev(c), 3)
+    got = o.group_norm_silu(dev(x), groups, 1e-5, dev(gam), dev(bet), offs, True, torch.float32).cpu().numpy()
+    exp = O.silu(O.group_norm(c[:, 0].astype(np.int64), x, groups, 1e-5, gam, bet))
     check(got, exp, max_abs=1e-4, rel_l2=1e-5, what="groupnorm+silu")
+    h = o.group_norm_silu(dev(x), groups, 1e-5, dev(gam), dev(bet), offs, False, torch.float16).float().cpu().numpy()
+    exp = O.group_norm(c[:, 0].astype(np.int64), x, groups, 1e-5, gam, bet)
+    check(h, exp, max_abs=4e-3 * max(1.0, float(np.abs(exp).max())), what="groupnorm f16 out")
 
 
 @pytest.mark.parametrize("g,gr", [(1.0, 0.0), (3.0, 0.0), (2.35, 0.41)])
