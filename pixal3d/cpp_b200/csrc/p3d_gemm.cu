@@ -43,6 +43,10 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kProducerThreads = 128;
 constexpr int kThreads = 9 * 32;
+// The pair kernel's cp.async gather variant adds 4 producer warps (9-12), so
+// 8 warps share each stage's row gathers (4 cp.async per lane per stage).
+constexpr int kThreadsG = 13 * 32;
+constexpr int kGatherThreads = 256;
 constexpr int kMmaWarp = 8;
 
 struct GemmParams {
@@ -79,13 +83,20 @@ constexpr int EPI_SLOT_BYTES = 4096;
 constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT_BYTES;
 constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
+// Shared memory for the operand stages of one CTA (the rest of the 227 KB
+// holds the epilogue staging and the barriers).
+#ifndef P3D_GEMM_STAGE_BUDGET
+#define P3D_GEMM_STAGE_BUDGET 196608
+#endif
+constexpr int kStageBudget = P3D_GEMM_STAGE_BUDGET;
+
 // 1-CTA tile: 128 x BN, BK = 64; accumulators double-buffered in TMEM.
 template <int BN>
 struct Cfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr int STAGES = (kStageBudget / STAGE_BYTES) > 8 ? 8 : (kStageBudget / STAGE_BYTES);
     static constexpr int ACC_COLS = BN;
     static constexpr int ACC_BUFS = 2;
     static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
@@ -102,7 +113,7 @@ struct Cfg2 {
     static constexpr int B_SUB = 128 * BK * 2;
     static constexpr int B_BYTES = NSUB * B_SUB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+    static constexpr int STAGES = (kStageBudget / STAGE_BYTES) > 8 ? 8 : (kStageBudget / STAGE_BYTES);
     static constexpr int ACC_COLS = NSUB * 256;
     static constexpr int ACC_BUFS = NSUB == 1 ? 2 : 1;
     static constexpr int TMEM_COLS = 512;
@@ -185,9 +196,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int64_t row, in
 // 0; accumulator column c is output column n0 + c.  Bias, then per-head RMS
 // norm + RoPE (64-column heads) or the activation, then the store / gated
 // residual add.  Every tcgen05.ld is issued by the whole (converged) warp.
-template <int COLS>
+template <int COLS, bool HEADNORM>
 __device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc, int64_t row, int64_t n0) {
-    if (p.norm_cols > 0 || p.rope_cols > 0) {
+    if (HEADNORM && (p.norm_cols > 0 || p.rope_cols > 0)) {
 #pragma unroll 1
         for (int cs = 0; cs < COLS; cs += 64) {
             float v[64];
@@ -397,14 +408,14 @@ __device__ __forceinline__ void rope_rotate16(float (&v)[32], const float4 (&r)[
 // are 32 rows x 128 bytes: 32 f32 columns, or 64 16-bit columns staged from
 // two 32-column chunks.  The next chunk's tcgen05.ld is in flight while the
 // current one is finished.
-template <int COLS>
+template <int COLS, bool HEADNORM>
 __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUtensorMap *tmo, uint32_t tacc,
                                                   int64_t row0, int lane, int64_t n0, uint8_t *wbuf, int &slot) {
     static_assert(COLS % 64 == 0, "epilogue column count");
     const int64_t row = row0 + lane;
     const bool f32 = p.out_dtype == P3D_F32;
     float a[32], b[32];
-    if (p.norm_cols > 0 || p.rope_cols > 0) {
+    if (HEADNORM && (p.norm_cols > 0 || p.rope_cols > 0)) {
         // Per-head RMS norm + RoPE over 64-column heads (N % 64 == 0).  The
         // head's second half is read from TMEM twice (for the norm, then
         // for its output) so only one half plus its RoPE pairs stay live.
@@ -524,6 +535,22 @@ __device__ __forceinline__ void gather_stage_a(const GemmParams &p, uint8_t *sa,
     for (int i = 0; i < 8; ++i) {
         const int r = wrow0 + i * 4 + (lane_ >> 3);
         const int32_t src = __shfl_sync(0xffffffffu, my_src, i * 4 + (lane_ >> 3));
+        const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
+        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
+    }
+}
+
+// One producer warp's share of a gather stage when 8 warps fill it: tile
+// rows [16 pw, 16 pw + 16), 4 cp.async instructions of 4 rows each (8 lanes
+// per 128-byte row); lane l < 16 holds the source of row 16 pw + l.
+__device__ __forceinline__ void gather_stage_a16(const GemmParams &p, uint8_t *sa, int pw, int lane, int32_t my_src,
+                                                 int kc) {
+    const int chunk = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = i * 4 + (lane >> 3);
+        const int r = 16 * pw + rr;
+        const int32_t src = __shfl_sync(0xffffffffu, my_src, rr);
         const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
         cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
     }
@@ -707,9 +734,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
             if (p.tma_out)
-                epilogue_rows_tma<BN>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES, slot);
+                epilogue_rows_tma<BN, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
+                                               slot);
             else
-                epilogue_rows<BN>(p, tacc, m0 + q * 32 + lane, n0);
+                epilogue_rows<BN, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -759,7 +787,7 @@ __device__ __forceinline__ int4 gather_src4(const GemmParams &p, int lane, int64
 }
 
 template <int NSUB, bool GATHER, bool TMAG = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? kThreadsG : kThreads, 1)
     gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
     using C = Cfg2<NSUB>;
@@ -795,7 +823,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
         // the odd CTA's forwarded gather completion); odd CTA (gather): its
         // 128 row-gather threads, forwarded by its warp 8.
-        const uint32_t full_count = (GATHER && !TMAG) ? (rank == 0 ? kProducerThreads + 2 : kProducerThreads) : 1;
+        const uint32_t full_count = (GATHER && !TMAG) ? (rank == 0 ? kGatherThreads + 2 : kGatherThreads) : 1;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full_bar[s], full_count);
             mbar_init(&empty_bar[s], 1);
@@ -861,9 +889,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < 4 || (GATHER && !TMAG && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
-        const int t = threadIdx.x;
+        // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) gathers tile
+        // rows [16 pw, 16 pw + 16); lane l < 16 holds row 16 pw + l's source
+        const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
+        const int t = warp < 4 ? threadIdx.x : 0;
+        const int grow = 16 * pw + (lane & 15);
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
@@ -872,8 +904,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int64_t n0 = (tile % n_tiles) * PAIR_N;
             int32_t cur_src = 0, next_src = 0;
             if (GATHER) {
-                cur_src = gather_src(p, t, m0, 0);
-                next_src = gather_src(p, t, m0, 1);
+                cur_src = gather_src(p, grow, m0, 0);
+                next_src = gather_src(p, grow, m0, 1);
             }
             for (int kb = 0; kb < num_kb; ++kb) {
                 if (GATHER) {
@@ -894,11 +926,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (GATHER) {
                     if (kc == 0 && tap > 0) {
                         cur_src = next_src;
-                        next_src = gather_src(p, t, m0, tap + 1);
+                        next_src = gather_src(p, grow, m0, tap + 1);
                     }
-                    gather_stage_a(p, sa, t, cur_src, kc);
+                    gather_stage_a16(p, sa, pw, lane, cur_src, kc);
                 }
-                if (t == 0) {
+                if (warp == 0 && lane == 0) {
                     const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
                     if (rank == 0)
                         mbar_arrive_expect_tx(&full_bar[stage], 2 * (GATHER ? C::B_BYTES : C::A_BYTES + C::B_BYTES));
@@ -1005,10 +1037,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
             if (p.tma_out)
-                epilogue_rows_tma<C::ACC_COLS>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
-                                               slot);
+                epilogue_rows_tma<C::ACC_COLS, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0,
+                                                        smem_o + q * EPI_WARP_BYTES, slot);
             else
-                epilogue_rows<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0);
+                epilogue_rows<C::ACC_COLS, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -1083,7 +1115,7 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
     if (max_pairs == 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (ctx->num_sms / 2), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.blockDim = dim3((GATHER && !TMAG) ? kThreadsG : kThreads, 1, 1);
         cfg.dynamicSmemBytes = C::SMEM;
         cfg.stream = ctx->stream;
         int n = 0;
@@ -1092,7 +1124,8 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
     }
     const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
-    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
+    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, (GATHER && !TMAG) ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(
+        ta, tb, to, p);
     return check_launch(ctx, "gemm2_tc_kernel");
 }
 
