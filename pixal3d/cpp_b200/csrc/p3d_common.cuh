@@ -466,7 +466,10 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
     const float y2 = -1.5957691216057308f * (x + 0.044715f * x * x * x);  // -2y
     return __fdividef(x, 1.0f + __expf(y2));
 }
-__device__ __forceinline__ float silu_f(float x) { return x * (1.0f / (1.0f + expf(-x))); }
+// SiLU x / (1 + exp(-x)) with the fast exp and divide (a few ulp; for
+// x < -87 the denominator exceeds 2^126 and the result flushes to 0, as the
+// exact value underflows there too).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ int batch_of_row(const int32_t *offsets, int nbatch, int64_t row) {
     int b = 0;
