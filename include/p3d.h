@@ -242,6 +242,34 @@ int p3d_varlen_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k
                          const int32_t *cu_k, int nseq, int64_t max_q, int64_t rows_q, int64_t rows_k,
                          int heads, int head_dim, float scale, int dtype);
 
+/* Shifted-window sparse self-attention (no reference implementation: the
+ * 8^3-window blocks of the config-3 SLat decoder).  Row i with coords
+ * (b, x, y, z) lies in window (b, (x+shift)/window, (y+shift)/window,
+ * (z+shift)/window) of a grid with ceil((s_d + shift)/window) windows per
+ * axis; window index w = ((b*nwx + wx)*nwy + wy)*nwz + wz.
+ * p3d_window_count: batch*nwx*nwy*nwz (0 for bad arguments).
+ * p3d_window_partition: perm[j] = row at window-order position j (rows
+ * ordered by window, then by row index; -1 marks a position left empty by a
+ * row outside [0, batch) x grid, which also latches P3D_ERR_INVALID), and
+ * cu[w] = first position of window w, cu[num_windows] = number of rows
+ * placed.  window^3 <= 1024, 0 <= shift < window.  ws: at least
+ * p3d_window_partition_workspace(n, num_windows) bytes. */
+int64_t p3d_window_count(int batch, int window, int shift, int sx, int sy, int sz);
+size_t p3d_window_partition_workspace(int64_t n, int64_t num_windows);
+int p3d_window_partition(p3d_ctx *ctx, const int32_t *coords, int64_t n, int batch, int window, int shift, int sx,
+                         int sy, int sz, int32_t *perm, int32_t *cu, void *ws, size_t ws_bytes);
+/* Attention of every row to the rows of its window (the partition above):
+ * q/k/v rows gathered into window order, p3d_varlen_attention semantics per
+ * window (head_dim 64, 16-bit dtype), output rows written back in the
+ * canonical order (out row i belongs to input row i).  max_window_rows
+ * bounds the rows of one window (window^3).  scratch: at least
+ * p3d_window_attention_scratch(n, heads) bytes, 16-byte aligned. */
+size_t p3d_window_attention_scratch(int64_t n, int heads);
+int p3d_window_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
+                         int64_t ldv, const int32_t *perm, const int32_t *cu, int64_t num_windows,
+                         int max_window_rows, int64_t n, int heads, int head_dim, float scale, int dtype,
+                         void *scratch, size_t scratch_bytes, void *out, int64_t ldo);
+
 /* ------------------------------------------------------ fused elementwise */
 
 /* LayerNorm over channels of f32 rows (two-pass, like sparse_layer_norm,

@@ -699,3 +699,30 @@ def varlen_attention(q, k, v, cu_q, cu_k, heads, head_dim, scale):
                 q[q0:q1, h * head_dim:(h + 1) * head_dim], k[k0:k1, h * head_dim:(h + 1) * head_dim],
                 v[k0:k1, h * vd:(h + 1) * vd], scale)
     return out
+
+
+def window_partition_grid(coords, batch, window, shift, spatial):
+    """No reference.  window_partition over the full window grid, the layout
+    of p3d_window_partition: windows numbered w = ((b*nwx + wx)*nwy + wy)*nwz
+    + wz with nw_d = ceil((s_d + shift) / window) (the same lexicographic
+    window order), cu over every window, empty ones included (cu[-1] = N).
+    perm lists rows by window, then by row index."""
+    c = np.asarray(coords, dtype=np.int64)
+    nw = [-(-(int(s) + shift) // window) for s in spatial]
+    w = ((c[:, 0] * nw[0] + (c[:, 1] + shift) // window) * nw[1] + (c[:, 2] + shift) // window) * nw[2] + \
+        (c[:, 3] + shift) // window
+    m = batch * nw[0] * nw[1] * nw[2]
+    perm = np.argsort(w, kind="stable").astype(np.int32)
+    cu = np.zeros(m + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(np.bincount(w, minlength=m))
+    return perm, cu
+
+
+def window_attention(q, k, v, coords, window, shift, heads, head_dim, scale):
+    """No reference.  Each row attends to the rows of its shifted window
+    (window_partition), per head; output rows in the input order."""
+    order, cu = window_partition(coords, window, shift)
+    o = varlen_attention(q[order], k[order], v[order], cu, cu, heads, head_dim, scale)
+    out = np.empty_like(o)
+    out[order] = o
+    return out

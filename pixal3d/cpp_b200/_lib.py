@@ -123,6 +123,12 @@ _sig("p3d_linear", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i
 _sig("p3d_subm_conv3d", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i32, i32, vp, i64, vp, i32)
 _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, i64, i64, i64, i32, i32, f32,
      i32)
+_sig("p3d_window_count", i64, i32, i32, i32, i32, i32, i32)
+_sig("p3d_window_partition_workspace", C.c_size_t, i64, i64)
+_sig("p3d_window_partition", i32, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp, vp, vp, C.c_size_t)
+_sig("p3d_window_attention_scratch", C.c_size_t, i64, i32)
+_sig("p3d_window_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, vp, i64, i32, i64, i32, i32, f32, i32, vp,
+     C.c_size_t, vp, i64)
 _sig("p3d_layernorm_modulate", i32, vp, vp, i64, i32, f32, vp, vp, vp, i64, vp, i32, vp, i32)
 _sig("p3d_qk_rmsnorm_rope", i32, vp, vp, i64, i64, i32, i32, vp, vp, f32, f32, i32)
 _sig("p3d_linear_headnorm", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i64, vp, i64, vp)

@@ -255,6 +255,40 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: to
     return out
 
 
+def window_partition(coords: torch.Tensor, batch: int, window: int, shift: int, spatial) -> tuple:
+    """Shifted-window partition (no reference; the config-3 decoder's 8^3
+    windows): (perm, cu) with rows in window order and per-window offsets
+    over all batch*nwx*nwy*nwz windows (empty ones included)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    sx, sy, sz = spatial
+    m = int(L.lib.p3d_window_count(batch, window, shift, sx, sy, sz))
+    assert m > 0, "bad window grid"
+    perm = torch.empty(n, dtype=torch.int32, device=coords.device)
+    cu = torch.empty(m + 1, dtype=torch.int32, device=coords.device)
+    wsb = int(L.lib.p3d_window_partition_workspace(n, m))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=coords.device)
+    c.check(L.lib.p3d_window_partition(c.h, _p(coords), n, batch, window, shift, sx, sy, sz, _p(perm), _p(cu), _p(ws),
+                                       wsb))
+    return perm, cu
+
+
+def window_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: torch.Tensor, cu: torch.Tensor,
+                     window: int, heads: int, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Self-attention of each row to the rows of its window (p3d_window_attention)."""
+    c = ctx(q.device)
+    assert q.dtype in HALF and k.dtype == q.dtype and v.dtype == q.dtype
+    n = q.shape[0]
+    if out is None:
+        out = torch.empty((n, heads * 64), dtype=q.dtype, device=q.device)
+    sb = int(L.lib.p3d_window_attention_scratch(n, heads))
+    scratch = torch.empty(max(sb, 16), dtype=torch.uint8, device=q.device)
+    c.check(L.lib.p3d_window_attention(c.h, _p(q), _rows(q), _p(k), _rows(k), _p(v), _rows(v), _p(perm), _p(cu),
+                                       cu.shape[0] - 1, window ** 3, n, heads, 64, scale, _dt(q), _p(scratch), sb,
+                                       _p(out), _rows(out)))
+    return out
+
+
 # ------------------------------------------------------------ elementwise
 
 def layernorm_modulate(x: torch.Tensor, eps: float, gamma=None, beta=None, mod: torch.Tensor | None = None,
