@@ -187,6 +187,10 @@ int p3d_c2s_topology(p3d_ctx *ctx, const int32_t *coords, int64_t n, int factor,
 /* Feature half of channel-to-spatial: out[j] = x[src_row[j], src_child[j]*cout : +cout],
  * optionally repeating each channel `repeat` times (repeat_channels,
  * src/slat_decoder.cpp:80-109). */
+/* offsets[b] = first row of batch item b in a batch-contiguous coordinate
+ * list, offsets[batch] = n (the per-item row ranges every batch-aware call
+ * takes).  offsets: device int32 [batch + 1]. */
+int p3d_batch_offsets(p3d_ctx *ctx, const int32_t *coords, int64_t n, int batch, int32_t *offsets);
 int p3d_c2s_gather(p3d_ctx *ctx, const void *x, int64_t in_channels, const int32_t *src_row,
                    const int8_t *src_child, int64_t m, int cout, int repeat, int dtype, void *out);
 
@@ -271,6 +275,13 @@ int p3d_window_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k
                          void *scratch, size_t scratch_bytes, void *out, int64_t ldo);
 
 /* ------------------------------------------------------ fused elementwise */
+
+/* x[i, c] += sinusoidal absolute 3D position embedding of coords[i] (no
+ * reference: the configs' "sinusoidal 3D absolute PE"): with fd = channels/6
+ * frequencies f_j = 10000^(-j/fd), axis a (x, y, z) fills channels
+ * [2*fd*a, 2*fd*a + fd) with sin(coord_a * f_j) and the next fd with cos;
+ * channels >= 6*fd are left unchanged.  x: f32 [n, channels]. */
+int p3d_ape_add(p3d_ctx *ctx, const int32_t *coords, int64_t n, int channels, float *x);
 
 /* LayerNorm over channels of f32 rows (two-pass, like sparse_layer_norm,
  * src/sparse.cpp:490-534), then optional affine (gamma/beta) and optional

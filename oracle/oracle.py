@@ -726,3 +726,69 @@ def window_attention(q, k, v, coords, window, shift, heads, head_dim, scale):
     out = np.empty_like(o)
     out[order] = o
     return out
+
+
+# --------------------------------------------------------------------------
+# Config-3 decoder (shifted-window transformer + subdivide stages): NO
+# reference implementation; restated from the benchmark configuration.
+# --------------------------------------------------------------------------
+
+def swin_block(coords, x, w, heads, window, shift, spatial, eps=1e-6):
+    """No reference.  Pre-norm transformer block with shifted-window
+    self-attention: x += Wo·attn_window(LN1(x)); x += W2·gelu_tanh(W1·LN2(x)).
+    LayerNorms with affine (eps 1e-6), head_dim 64, scale 1/8, no q/k norm.
+    w keys: norm1_w/b, qkv_w [3C, C], qkv_b, out_w [C, C], out_b, norm2_w/b,
+    mlp0_w [rC, C], mlp0_b, mlp2_w [C, rC], mlp2_b."""
+    c = x.shape[1]
+    a = layer_norm(x, eps, w["norm1_w"], w["norm1_b"])
+    qkv = linear(a, w["qkv_w"], w["qkv_b"])
+    o = window_attention(qkv[:, :c], qkv[:, c:2 * c], qkv[:, 2 * c:], coords, window, shift, heads, 64,
+                         1.0 / 8.0)
+    x = (x + linear(o, w["out_w"], w["out_b"])).astype(F32)
+    a = layer_norm(x, eps, w["norm2_w"], w["norm2_b"])
+    h = gelu_tanh(linear(a, w["mlp0_w"], w["mlp0_b"]))
+    return (x + linear(h, w["mlp2_w"], w["mlp2_b"])).astype(F32)
+
+
+def subdivide(coords, x, mask):
+    """No reference.  SparseSubdivide x2: every parent row spawns the children
+    (2x+dx, 2y+dy, 2z+dz), child c = dx + 2 dy + 4 dz, kept where mask[:, c] > 0;
+    each kept child copies its parent's features.  Output in parent order,
+    then child order (the channel_to_spatial layout)."""
+    return channel_to_spatial(coords, np.tile(x, (1, 8)), 2, mask)
+
+
+def resblock3d_io(coords, x, w, groups=32, eps=1e-5, nbr=None):
+    """No reference.  SparseResBlock3d with a channel change:
+    conv2(SiLU(GN(conv1(SiLU(GN(x)))))) + skip(x), skip = linear C_in -> C_out.
+    w keys: gn1_w/b, conv1_w [27, Co, Ci], conv1_b, gn2_w/b, conv2_w [27, Co, Co],
+    conv2_b, skip_w [Co, Ci], skip_b."""
+    if nbr is None:
+        nbr = neighbor_map27(coords)
+    bidx = coords[:, 0].astype(np.int64)
+    h = silu(group_norm(bidx, x, groups, eps, w["gn1_w"], w["gn1_b"]))
+    h = subm_conv3d(coords, h, w["conv1_w"], w["conv1_b"], nbr)
+    h = silu(group_norm(bidx, h, groups, eps, w["gn2_w"], w["gn2_b"]))
+    h = subm_conv3d(coords, h, w["conv2_w"], w["conv2_b"], nbr)
+    return (h + linear(x, w["skip_w"], w["skip_b"])).astype(F32)
+
+
+def swin_decoder_forward(coords, x, cfg: dict, w: dict, masks):
+    """No reference.  Config-3 SLat decoder: latent -> linear to C0 + absolute
+    3D PE -> num_blocks shifted-window blocks (shift 0 on even blocks,
+    window/2 on odd) -> per stage s: subdivide with masks[s], then
+    resblock3d_io to stage_channels[s] -> LayerNorm (eps 1e-5, no affine) ->
+    linear to out_channels.  cfg: model_channels, num_heads, window, spatial
+    (grid extent of the input level), groups.  w: from_latent_w/b, blocks,
+    stages, output_w/b.  Returns (coords, out)."""
+    c0 = cfg["model_channels"]
+    h = (linear(x, w["from_latent_w"], w["from_latent_b"]) + absolute_pe(coords, c0)).astype(F32)
+    sp = (cfg["spatial"],) * 3
+    for i, bw in enumerate(w["blocks"]):
+        shift = 0 if i % 2 == 0 else cfg["window"] // 2
+        h = swin_block(coords, h, bw, cfg["num_heads"], cfg["window"], shift, sp)
+    for s, sw in enumerate(w["stages"]):
+        coords, h = subdivide(coords, h, masks[s])
+        h = resblock3d_io(coords, h, sw, cfg.get("groups", 32))
+    out = linear(layer_norm(h, 1e-5), w["output_w"], w["output_b"])
+    return coords, out

@@ -123,6 +123,8 @@ _sig("p3d_linear", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i
 _sig("p3d_subm_conv3d", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i32, i32, vp, i64, vp, i32)
 _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, i64, i64, i64, i32, i32, f32,
      i32)
+_sig("p3d_ape_add", i32, vp, vp, i64, i32, vp)
+_sig("p3d_batch_offsets", i32, vp, vp, i64, i32, vp)
 _sig("p3d_window_count", i64, i32, i32, i32, i32, i32, i32)
 _sig("p3d_window_partition_workspace", C.c_size_t, i64, i64)
 _sig("p3d_window_partition", i32, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp, vp, vp, C.c_size_t)

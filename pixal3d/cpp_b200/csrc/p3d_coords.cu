@@ -296,12 +296,27 @@ __global__ void c2s_gather_kernel(const T *__restrict__ x, int64_t in_ch, const 
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= m) return;
     const int lane = threadIdx.x & 31;
+    // the child's channel slice must lie inside the source row
+    if ((static_cast<int64_t>(src_child[row]) + 1) * cout > in_ch || src_child[row] < 0) return;
     const T *src = x + static_cast<int64_t>(src_row[row]) * in_ch + static_cast<int64_t>(src_child[row]) * cout;
     const int oc = cout * repeat;
     for (int c = lane; c < oc; c += 32) out[row * oc + c] = src[c / repeat];
 }
 
 unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>(ceil_div(n, threads)); }
+
+// offsets[b] = first row whose batch index is >= b (binary search over the
+// batch-contiguous coordinate list), offsets[batch] = n.
+__global__ void batch_offsets_kernel(const int4 *__restrict__ coords, int64_t n, int batch, int32_t *__restrict__ off) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b > batch) return;
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (coords[mid].x < b) lo = mid + 1; else hi = mid;
+    }
+    off[b] = static_cast<int32_t>(b == batch ? n : lo);
+}
 
 }  // namespace
 }  // namespace p3d
@@ -529,10 +544,21 @@ extern "C" int p3d_c2s_topology(p3d_ctx *ctx, const int32_t *coords, int64_t n, 
     return check_launch(ctx, "i32_to_i64");
 }
 
+extern "C" int p3d_batch_offsets(p3d_ctx *ctx, const int32_t *coords, int64_t n, int batch, int32_t *offsets) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, coords && offsets && batch > 0 && n >= 0 && n < (int64_t(1) << 31),
+                "p3d_batch_offsets: bad argument");
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(coords) & 15) == 0, "p3d_batch_offsets: coords must be 16-byte aligned");
+    batch_offsets_kernel<<<blocks_for(batch + 1, 128), 128, 0, ctx->stream>>>(reinterpret_cast<const int4 *>(coords), n,
+                                                                             batch, offsets);
+    return check_launch(ctx, "batch_offsets");
+}
+
 extern "C" int p3d_c2s_gather(p3d_ctx *ctx, const void *x, int64_t in_channels, const int32_t *src_row,
                               const int8_t *src_child, int64_t m, int cout, int repeat, int dtype, void *out) {
     if (!ctx) return P3D_ERR_INVALID;
-    P3D_REQUIRE(ctx, x && src_row && src_child && out && cout > 0 && repeat > 0, "p3d_c2s_gather: bad argument");
+    P3D_REQUIRE(ctx, x && src_row && src_child && out && cout > 0 && repeat > 0 && cout <= in_channels,
+                "p3d_c2s_gather: bad argument");
     if (m == 0) return P3D_OK;
     const unsigned grid = blocks_for(m, 8);
     if (dtype == P3D_F32)

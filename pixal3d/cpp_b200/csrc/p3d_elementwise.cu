@@ -275,11 +275,12 @@ __global__ void activation_kernel(const T *__restrict__ x, int64_t n, int act, T
 }
 
 // ------------------------------------------------------------- GroupNorm
-// Stats: each block walks a contiguous row range with one float4 per thread
-// per row step (C/4 threads span a row, coalesced), accumulating sum and
-// sum of squares of its group in double; the group's threads reduce by
-// shuffles and one lane per group issues an atomicAdd whenever the batch item
-// changes or the range ends.  Requires C % 4 == 0 and (C/groups) % 4 == 0.
+// Stats, generic layout: each block walks a contiguous row range with one
+// float4 per thread per row step (C/4 threads span a row, coalesced),
+// accumulating per element e of the float4 the sum and sum of squares of its
+// group (4*cb + e) / gs in double (a float4 may span several groups when the
+// group is narrower than 4 channels); one atomicAdd per element and group
+// whenever the batch item changes or the range ends.  Requires C % 4 == 0.
 __global__ void groupnorm_stats_kernel(const float *__restrict__ x, int64_t n, int C, int groups,
                                        const int32_t *__restrict__ offsets, int nbatch, int rows_per_block,
                                        double *__restrict__ stats) {
@@ -291,30 +292,38 @@ __global__ void groupnorm_stats_kernel(const float *__restrict__ x, int64_t n, i
     if (rsub >= rows_step) return;  // blockDim not a multiple of tpr: spare threads
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
     const int64_t r1 = min(n, r0 + rows_per_block);
-    const int gs4 = (C / groups) / 4;  // float4 per group
+    const int gs = C / groups;
     for (int cb = col4; cb < c4; cb += tpr) {
-        const int g = cb / gs4;
-        double sum = 0.0, sq = 0.0;
+        int g[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) g[e] = (4 * cb + e) / gs;
+        double sum[4] = {0.0, 0.0, 0.0, 0.0}, sq[4] = {0.0, 0.0, 0.0, 0.0};
         int cur_b = -1;
+        auto flush = [&](int b) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (sum[e] != 0.0 || sq[e] != 0.0) {
+                    atomicAdd(stats + 2 * (b * groups + g[e]), sum[e]);
+                    atomicAdd(stats + 2 * (b * groups + g[e]) + 1, sq[e]);
+                }
+                sum[e] = sq[e] = 0.0;
+            }
+        };
         for (int64_t r = r0 + rsub; r < r1; r += rows_step) {
             const int b = batch_of_row(offsets, nbatch, r);
             if (b != cur_b) {
-                if (cur_b >= 0 && (sum != 0.0 || sq != 0.0)) {
-                    atomicAdd(stats + 2 * (cur_b * groups + g), sum);
-                    atomicAdd(stats + 2 * (cur_b * groups + g) + 1, sq);
-                }
-                sum = sq = 0.0;
+                if (cur_b >= 0) flush(cur_b);
                 cur_b = b;
             }
             const float4 v = __ldg(reinterpret_cast<const float4 *>(x + r * C) + cb);
-            sum += static_cast<double>(v.x) + v.y + v.z + v.w;
-            sq += static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
-                  static_cast<double>(v.w) * v.w;
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                sum[e] += static_cast<double>(vv[e]);
+                sq[e] += static_cast<double>(vv[e]) * vv[e];
+            }
         }
-        if (cur_b >= 0) {
-            atomicAdd(stats + 2 * (cur_b * groups + g), sum);
-            atomicAdd(stats + 2 * (cur_b * groups + g) + 1, sq);
-        }
+        if (cur_b >= 0) flush(cur_b);
     }
 }
 
@@ -489,10 +498,13 @@ __global__ void __launch_bounds__(256) groupnorm_apply_kernel(const float *__res
         const int64_t row = i / c4;
         const int cb = static_cast<int>(i - row * c4);
         const int b = batch_of_row(offsets, nbatch, row);
-        const int g = (cb * 4) / gs;
-        const float mean = __ldg(mr + 2 * (b * groups + g)), rstd = __ldg(mr + 2 * (b * groups + g) + 1);
-        float y[4] = {(v[k].x - mean) * rstd, (v[k].y - mean) * rstd, (v[k].z - mean) * rstd,
-                      (v[k].w - mean) * rstd};
+        const float vv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        float y[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // a float4 may span groups narrower than 4 channels
+            const int g = (cb * 4 + e) / gs;
+            y[e] = (vv[e] - __ldg(mr + 2 * (b * groups + g))) * __ldg(mr + 2 * (b * groups + g) + 1);
+        }
         if (gamma) {
             const float4 ga = __ldg(reinterpret_cast<const float4 *>(gamma) + cb);
             const float4 be = __ldg(reinterpret_cast<const float4 *>(beta) + cb);
@@ -723,8 +735,8 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
                                    int silu, double *stats, void *out, int out_dtype) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && out && stats && batch_offsets && nbatch > 0, "p3d_group_norm_silu: null pointer");
-    P3D_REQUIRE(ctx, groups > 0 && channels % groups == 0 && (channels / groups) % 4 == 0,
-                "p3d_group_norm_silu: channels/groups must be a multiple of 4");
+    P3D_REQUIRE(ctx, groups > 0 && channels % groups == 0 && channels % 4 == 0,
+                "p3d_group_norm_silu: channels must be a multiple of 4 and of groups");
     P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
                 "p3d_group_norm_silu: x/out must be 16-byte aligned");
     P3D_REQUIRE(ctx, !gamma || (beta && (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 &&
@@ -733,9 +745,10 @@ extern "C" int p3d_group_norm_silu(p3d_ctx *ctx, const float *x, int64_t n, int 
     // stats scratch: [nbatch*groups*2] double sums, then [nbatch*groups*2] float mean/rstd
     P3D_CUDA(ctx, cudaMemsetAsync(stats, 0, sizeof(double) * 2 * nbatch * groups, ctx->stream));
     if (n == 0) return P3D_OK;
-    // Rows-layout kernels for C = 128 * NV (NV in 1, 2, 4, 8, 16).
+    // Rows-layout kernels for C = 128 * NV (NV in 1, 2, 4, 8, 16) and groups of
+    // whole float4s; the generic kernels take every other shape.
     const int nv = channels % 128 == 0 ? channels / 128 : 0;
-    const bool rows = nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 16;
+    const bool rows = (nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 16) && (channels / groups) % 4 == 0;
     if (rows) {
         // ~4 resident blocks per SM, each a contiguous row range
         const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 16), 4 * ctx->num_sms));

@@ -512,6 +512,19 @@ void p3d_flow::reset_topology() {
     h_trunk_off.clear();
 }
 
+// Sinusoidal absolute 3D position embedding added to f32 rows (no
+// reference: the benchmark configs' "sinusoidal 3D absolute PE").
+extern "C" int p3d_ape_add(p3d_ctx *ctx, const int32_t *coords, int64_t n, int channels, float *x) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, coords && x && channels > 0 && n >= 0, "p3d_ape_add: bad argument");
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(coords) & 15) == 0, "p3d_ape_add: coords must be 16-byte aligned");
+    if (n == 0) return P3D_OK;
+    DeviceGuard dg(ctx->device);
+    ape_add_kernel<<<blocks_for(n * channels, 256), 256, 0, ctx->stream>>>(x, reinterpret_cast<const int4 *>(coords), n,
+                                                                          channels);
+    return check_launch(ctx, "ape_add");
+}
+
 extern "C" int p3d_timestep_mlp(p3d_ctx *ctx, const float *timesteps, int batch, int channels, const float *w0,
                                 const float *b0, const float *w2, const float *b2, const float *mod_w,
                                 const float *mod_b, float *scratch, float *tmod) {

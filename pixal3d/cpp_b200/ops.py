@@ -291,6 +291,14 @@ def window_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: to
 
 # ------------------------------------------------------------ elementwise
 
+def ape_add_(x: torch.Tensor, coords: torch.Tensor) -> torch.Tensor:
+    """x += sinusoidal absolute 3D PE of coords (in place, f32)."""
+    assert x.dtype == torch.float32 and x.is_contiguous()
+    c = ctx(x.device)
+    c.check(L.lib.p3d_ape_add(c.h, _p(coords), x.shape[0], x.shape[1], _p(x)))
+    return x
+
+
 def layernorm_modulate(x: torch.Tensor, eps: float, gamma=None, beta=None, mod: torch.Tensor | None = None,
                        batch_offsets: torch.Tensor | None = None, out_dtype=torch.bfloat16,
                        out: torch.Tensor | None = None) -> torch.Tensor:
@@ -351,6 +359,23 @@ def convert(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     x = x.contiguous()
     out = torch.empty(x.shape, dtype=dtype, device=x.device)
     c.check(L.lib.p3d_convert(c.h, _p(x), _dt(x), x.numel(), _p(out), _dt(out)))
+    return out
+
+
+def batch_offsets(coords: torch.Tensor, batch: int) -> torch.Tensor:
+    """int32 [batch+1] row offsets of a batch-contiguous coordinate list (p3d_batch_offsets)."""
+    c = ctx(coords.device)
+    off = torch.empty(batch + 1, dtype=torch.int32, device=coords.device)
+    c.check(L.lib.p3d_batch_offsets(c.h, _p(coords), coords.shape[0], batch, _p(off)))
+    return off
+
+
+def pack_operand(x: torch.Tensor, ld: int, dtype: torch.dtype) -> torch.Tensor:
+    """f32 [rows, cols] -> 16-bit [rows, ld] with zero columns cols..ld (p3d_pack_operand)."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and ld >= x.shape[1]
+    c = ctx(x.device)
+    out = torch.empty((x.shape[0], ld), dtype=dtype, device=x.device)
+    c.check(L.lib.p3d_pack_operand(c.h, _p(x), x.shape[0], x.shape[1], _p(out), ld, _dt(out)))
     return out
 
 

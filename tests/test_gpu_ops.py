@@ -501,11 +501,14 @@ def test_attention_strided_qkv_views():
     check(got.float().cpu().numpy(), exp, what="strided attention")
 
 
-@pytest.mark.parametrize("C,groups", [(256, 32), (1024, 32), (512, 2), (384, 4), (192, 8)])
+@pytest.mark.parametrize("C,groups", [(256, 32), (1024, 32), (512, 2), (384, 4), (192, 8), (32, 32), (128, 64),
+                                      (768, 32)])
 def test_group_norm_silu(C, groups):
-    """Group widths that take each reduction of the stats kernel (shuffle over
-    a power-of-two lane group, whole warp, per-lane atomics) and a channel
-    count outside its rows layout (C % 128 != 0); three batch items."""
+    """Group widths that take each reduction of the rows-layout stats kernel
+    (shuffle over a power-of-two lane group, whole warp, per-lane atomics),
+    channel counts outside its layout (C % 128 != 0, C = 768) and groups
+    narrower than a float4 (1 and 2 channels: GroupNorm32 at C = 32); three
+    batch items."""
     rng = np.random.default_rng(21 + C)
     c = batched(shell_coords(24, 8.0, 1.0), 3)
     n = c.shape[0]
