@@ -35,6 +35,11 @@ bool fail(std::string *error, const char *message) {
     return false;
 }
 
+bool fail(std::string *error, const std::string &message) {
+    if (error) *error = message;
+    return false;
+}
+
 bool ok(p3d_ctx *ctx, int rc, std::string *error) {
     if (rc == P3D_OK) return true;
     if (error) *error = ctx ? p3d_last_error(ctx) : "p3d call failed";

@@ -24,6 +24,7 @@ p3d_ctx *context(std::string *error);
 // rc != P3D_OK -> false with the context's message in *error.
 bool ok(p3d_ctx *ctx, int rc, std::string *error);
 bool fail(std::string *error, const char *message);
+bool fail(std::string *error, const std::string &message);
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 

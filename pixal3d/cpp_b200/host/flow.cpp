@@ -4,7 +4,11 @@
 #include <cmath>
 #include <cstring>
 
+#include <map>
+#include <memory>
+
 #include "device.h"
+#include "gguf.h"
 #include "ops_internal.h"
 #include "pixal3d/flow_sampler.h"
 #include "pixal3d/slat_flow.h"
@@ -431,10 +435,82 @@ struct SLatFlowModel::Impl {
     p3d_flow *flow = nullptr;  // device-resident model, or
     HostWeights host;          // weights for the composed path
     int tensors = 0;
+    bool has_data = true;
+    std::string alias;                                 // pack component prefix (load())
+    std::vector<std::string> pack_tensors;             // this component's tensor names in the pack
+    std::map<std::string, std::vector<float>> values;  // loaded tensors, f32
     ~Impl() {
         if (flow) p3d_flow_destroy(flow);
     }
 };
+
+namespace {
+
+// Component name -> tensor-name prefix of the compact-v1 pack scheme
+// (compact_prefix, src/slat_flow.cpp:353-358).
+std::string compact_prefix(const std::string &component) {
+    if (component == "shape_flow_512") return "sh512";
+    if (component == "shape_flow_1024") return "sh1024";
+    if (component == "texture_flow_1024") return "tx1024";
+    return {};
+}
+
+bool starts_with(const std::string &s, const std::string &p) { return s.size() >= p.size() && s.compare(0, p.size(), p) == 0; }
+
+// Hyperparameters under "pixal3d.<component>." (read_hparams,
+// src/slat_flow.cpp:397-427): the integer and mlp_ratio keys are required,
+// the rest optional with the reference's defaults.
+bool read_flow_hparams(const b200::GgufFile &f, const std::string &component, SLatFlowHParams &hp,
+                       std::string *error) {
+    const std::string k = "pixal3d." + component + ".";
+    uint32_t v = 0;
+    if (!f.get_string(k + "model_class", hp.model_class, true, error)) return false;
+    struct IntKey {
+        const char *name;
+        int *dst;
+    } ints[] = {{"resolution", &hp.resolution},         {"in_channels", &hp.in_channels},
+                {"out_channels", &hp.out_channels},     {"model_channels", &hp.model_channels},
+                {"cond_channels", &hp.cond_channels},   {"num_blocks", &hp.num_blocks},
+                {"num_heads", &hp.num_heads}};
+    for (const IntKey &ik : ints) {
+        if (!f.get_u32(k + ik.name, v, true, error)) return false;
+        *ik.dst = static_cast<int>(v);
+    }
+    v = 0;
+    if (!f.get_f32(k + "mlp_ratio", hp.mlp_ratio, true, error) ||
+        !f.get_string(k + "pe_mode", hp.pe_mode, false, error) ||
+        !f.get_bool(k + "share_mod", hp.share_mod, false, error) ||
+        !f.get_bool(k + "qk_rms_norm", hp.qk_rms_norm, false, error) ||
+        !f.get_bool(k + "qk_rms_norm_cross", hp.qk_rms_norm_cross, false, error) ||
+        !f.get_f32(k + "rope_freq_min", hp.rope_freq_min, false, error) ||
+        !f.get_f32(k + "rope_freq_base", hp.rope_freq_base, false, error) ||
+        !f.get_string(k + "image_attn_mode", hp.image_attn_mode, false, error) ||
+        !f.get_u32(k + "proj_in_channels", v, false, error))
+        return false;
+    if (hp.pe_mode.empty()) hp.pe_mode = "rope";
+    if (hp.image_attn_mode.empty()) hp.image_attn_mode = "cross";
+    hp.proj_in_channels = v == 0 ? hp.cond_channels : static_cast<int>(v);
+    // the reference's valid_hparams (src/slat_flow.cpp:113-138)
+    if (hp.resolution <= 0 || hp.in_channels <= 0 || hp.out_channels <= 0 || hp.model_channels <= 0 ||
+        hp.cond_channels <= 0 || hp.num_blocks <= 0 || hp.num_heads <= 0 || hp.model_channels % hp.num_heads != 0 ||
+        hp.head_dim() % 2 != 0 || !(hp.mlp_ratio > 0.0f) || !std::isfinite(hp.mlp_ratio) ||
+        !(hp.rope_freq_min > 0.0f) || !(hp.rope_freq_base > 0.0f) || !std::isfinite(hp.rope_freq_min) ||
+        !std::isfinite(hp.rope_freq_base))
+        return fail(error, "invalid SLat flow hyperparameters");
+    if (hp.pe_mode != "rope" || !hp.share_mod)
+        return fail(error, "SLat flow currently requires pe_mode=rope and share_mod=true");
+    if (hp.image_attn_mode != "cross" && hp.image_attn_mode != "proj")
+        return fail(error, "SLat flow supports image_attn_mode cross or proj");
+    if (hp.image_attn_mode == "proj" && hp.proj_in_channels <= 0)
+        return fail(error, "SLat flow projection channels must be positive");
+    return true;
+}
+
+// Weight pointers into the loaded tensors, each checked for its element
+// count (the names of SLatFlowModel::forward, src/slat_flow.cpp:1347-1393).
+bool pack_weights(const SLatFlowModel::Impl &m, SLatFlowWeightsF32 &w, std::string *error);
+
+}  // namespace
 
 SLatFlowModel::~SLatFlowModel() { close(); }
 
@@ -443,10 +519,121 @@ void SLatFlowModel::close() noexcept {
     impl_ = nullptr;
 }
 
-bool SLatFlowModel::load(const std::string &path, const std::string &component, bool, std::string *error) {
-    (void)path;
-    (void)component;
-    return fail(error, "SLat flow weight packs are not read by the B200 build; bind host weights with bind()");
+namespace {
+bool pack_weights(const SLatFlowModel::Impl &m, SLatFlowWeightsF32 &w, std::string *error) {
+    const SLatFlowHParams &h = m.hp;
+    const std::size_t C = h.model_channels, mlp = static_cast<std::size_t>(static_cast<float>(C) * h.mlp_ratio);
+    const std::size_t cc = h.cond_channels, pin = h.proj_in_channels;
+    bool okay = true;
+    // required tensor of `count` elements (optional: nullptr when absent)
+    auto get = [&](const std::string &local, std::size_t count, bool required) -> const float * {
+        if (!okay) return nullptr;
+        const std::string full = m.alias + "." + local;
+        auto it = m.values.find(full);
+        if (it == m.values.end()) {
+            if (required) okay = fail(error, "missing SLat flow tensor: " + full);
+            return nullptr;
+        }
+        if (it->second.size() != count) {
+            okay = fail(error, "SLat flow tensor " + full + " has " + std::to_string(it->second.size()) +
+                                   " values, expected " + std::to_string(count));
+            return nullptr;
+        }
+        return it->second.data();
+    };
+    w.input_weight = get("input_layer.weight", C * h.in_channels, true);
+    w.input_bias = get("input_layer.bias", C, true);
+    w.timestep_weight0 = get("t_embedder.mlp.0.weight", C * 256, true);
+    w.timestep_bias0 = get("t_embedder.mlp.0.bias", C, true);
+    w.timestep_weight2 = get("t_embedder.mlp.2.weight", C * C, true);
+    w.timestep_bias2 = get("t_embedder.mlp.2.bias", C, true);
+    w.modulation_weight = get("adaLN_modulation.1.weight", 6 * C * C, true);
+    w.modulation_bias = get("adaLN_modulation.1.bias", 6 * C, true);
+    w.output_weight = get("out_layer.weight", h.out_channels * C, true);
+    w.output_bias = get("out_layer.bias", h.out_channels, true);
+    w.blocks.clear();
+    for (int b = 0; b < h.num_blocks && okay; ++b) {
+        const std::string p = "blocks." + std::to_string(b);
+        const std::string cross = p + ".cross_attn.cross_attn_block";
+        const std::string mp = p + ".mlp.mlp";
+        SparseTransformerBlockWeightsF32 o;
+        o.modulation = get(p + ".modulation", 6 * C, true);
+        o.self_to_qkv_weight = get(p + ".self_attn.to_qkv.weight", 3 * C * C, true);
+        o.self_to_qkv_bias = get(p + ".self_attn.to_qkv.bias", 3 * C, true);
+        o.self_q_gamma = get(p + ".self_attn.q_rms_norm.gamma", C, h.qk_rms_norm);
+        o.self_k_gamma = get(p + ".self_attn.k_rms_norm.gamma", C, h.qk_rms_norm);
+        o.self_to_out_weight = get(p + ".self_attn.to_out.weight", C * C, true);
+        o.self_to_out_bias = get(p + ".self_attn.to_out.bias", C, true);
+        o.norm2_weight = get(p + ".norm2.weight", C, true);
+        o.norm2_bias = get(p + ".norm2.bias", C, true);
+        o.cross_to_q_weight = get(cross + ".to_q.weight", C * C, true);
+        o.cross_to_q_bias = get(cross + ".to_q.bias", C, true);
+        o.cross_to_kv_weight = get(cross + ".to_kv.weight", 2 * C * cc, true);
+        o.cross_to_kv_bias = get(cross + ".to_kv.bias", 2 * C, true);
+        o.cross_q_gamma = get(cross + ".q_rms_norm.gamma", C, h.qk_rms_norm_cross);
+        o.cross_k_gamma = get(cross + ".k_rms_norm.gamma", C, h.qk_rms_norm_cross);
+        o.cross_to_out_weight = get(cross + ".to_out.weight", C * C, true);
+        o.cross_to_out_bias = get(cross + ".to_out.bias", C, true);
+        if (h.image_attn_mode == "proj") {
+            o.proj_weight = get(p + ".cross_attn.proj_linear.weight", C * pin, true);
+            o.proj_bias = get(p + ".cross_attn.proj_linear.bias", C, true);
+        }
+        o.mlp0_weight = get(mp + ".0.weight", mlp * C, true);
+        o.mlp0_bias = get(mp + ".0.bias", mlp, true);
+        o.mlp2_weight = get(mp + ".2.weight", C * mlp, true);
+        o.mlp2_bias = get(mp + ".2.bias", C, true);
+        w.blocks.push_back(o);
+    }
+    return okay;
+}
+}  // namespace
+
+// GGUF pack loading (SLatFlowModel::load, src/slat_flow.cpp:1239-1281, with
+// the pack checks of load_pack_info, src/pack.cpp:127-176): version 3,
+// architecture "pixal3d", tensor-name scheme "compact-v1", component prefix
+// sh512 / sh1024 / tx1024.  F32, F16 and BF16 tensors are widened to f32 on
+// the host, then uploaded as for bind() (16-bit device copies).
+bool SLatFlowModel::load(const std::string &path, const std::string &component, bool load_tensors,
+                         std::string *error) {
+    close();
+    const std::string alias = compact_prefix(component);
+    if (alias.empty()) return fail(error, "unsupported SLat flow component: " + component);
+    b200::GgufFile f;
+    if (!f.open(path, error)) return false;
+    std::string arch, scheme;
+    if (!f.get_string("general.architecture", arch, true, error)) return false;
+    if (arch != "pixal3d") return fail(error, "unexpected GGUF architecture: " + arch);
+    if (!f.get_string("pixal3d.tensor_name_scheme", scheme, true, error)) return false;
+    if (scheme != "compact-v1") return fail(error, "unsupported Pixal3D tensor name scheme: " + scheme);
+    const std::string prefix = alias + ".";
+    if (!f.find(prefix + "input_layer.weight"))
+        return fail(error, "GGUF pack does not contain SLat flow component: " + component);
+    std::unique_ptr<Impl> impl(new Impl());
+    impl->hp.component = component;
+    impl->alias = alias;
+    if (!read_flow_hparams(f, component, impl->hp, error)) return false;
+    for (const b200::GgufTensor &t : f.tensors())
+        if (starts_with(t.name, prefix)) impl->pack_tensors.push_back(t.name);
+    if (impl->pack_tensors.empty()) return fail(error, "SLat flow component has no tensors: " + component);
+    impl->tensors = static_cast<int>(impl->pack_tensors.size());
+    impl->has_data = load_tensors;
+    if (load_tensors) {
+        for (const std::string &name : impl->pack_tensors)
+            if (!f.read_f32(*f.find(name), impl->values[name], error)) return false;
+        SLatFlowWeightsF32 w;
+        if (!pack_weights(*impl, w, error)) return false;
+        p3d_ctx *ctx = b200::context(error);
+        if (!ctx) return false;
+        if (device_flow_supported(impl->hp)) {
+            if (!create_flow(ctx, impl->hp, w, &impl->flow, error)) return false;
+        } else {
+            p3d_flow_hparams check;
+            if (!to_hparams(impl->hp, check, error)) return false;
+            impl->host.copy(impl->hp, w);
+        }
+    }
+    impl_ = impl.release();
+    return true;
 }
 
 bool SLatFlowModel::bind(const SLatFlowHParams &hparams, const SLatFlowWeightsF32 &weights, std::string *error) {
@@ -474,18 +661,25 @@ bool SLatFlowModel::bind(const SLatFlowHParams &hparams, const SLatFlowWeightsF3
 }
 
 bool SLatFlowModel::is_loaded() const noexcept { return impl_ != nullptr; }
-bool SLatFlowModel::has_data() const noexcept { return impl_ != nullptr; }
+bool SLatFlowModel::has_data() const noexcept { return impl_ != nullptr && impl_->has_data; }
 const SLatFlowHParams &SLatFlowModel::hparams() const noexcept {
     static const SLatFlowHParams empty;
     return impl_ ? impl_->hp : empty;
 }
 int SLatFlowModel::tensor_count() const noexcept { return impl_ ? impl_->tensors : 0; }
-bool SLatFlowModel::has_tensor(const std::string &) const noexcept { return false; }
+bool SLatFlowModel::has_tensor(const std::string &name) const noexcept {
+    if (!impl_ || impl_->alias.empty()) return false;
+    const std::string full = starts_with(name, impl_->alias + ".") ? name : impl_->alias + "." + name;
+    for (const std::string &t : impl_->pack_tensors)
+        if (t == full) return true;
+    return false;
+}
 
 bool SLatFlowModel::forward(const SparseTensorF32 &input, const float *timesteps, std::size_t timestep_count,
                             const VarLenTensorF32 &global_context, const SparseTensorF32 *projection_context,
                             SparseTensorF32 &output, std::string *error, const SparseTensorF32 *concat_condition) {
     if (!impl_) return fail(error, "SLat flow model is not loaded");
+    if (!impl_->has_data) return fail(error, "SLat flow model was loaded without tensor data");
     p3d_ctx *ctx = b200::context(error);
     if (!ctx) return false;
     if (!timesteps) return fail(error, "SLat flow timesteps are null");
@@ -503,6 +697,7 @@ bool SLatFlowModel::sample(const SparseTensorF32 &noise, const FlowEulerSamplerC
                            const VarLenTensorF32 &global_context, const SparseTensorF32 *projection_context,
                            FlowEulerSampleF32 &output, std::string *error, const SparseTensorF32 *concat_condition) {
     if (!impl_) return fail(error, "SLat flow model is not loaded");
+    if (!impl_->has_data) return fail(error, "SLat flow model was loaded without tensor data");
     p3d_ctx *ctx = b200::context(error);
     if (!ctx) return false;
     const SLatFlowHParams &h = impl_->hp;

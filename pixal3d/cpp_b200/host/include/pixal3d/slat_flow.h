@@ -68,8 +68,9 @@ public:
     SLatFlowModel(const SLatFlowModel &) = delete;
     SLatFlowModel &operator=(const SLatFlowModel &) = delete;
 
-    // Weight packs (GGUF) are not read by this build: returns false with a
-    // message.  Use bind() with host weights instead.
+    // Load a component (shape_flow_512 / shape_flow_1024 / texture_flow_1024)
+    // of a Pixal3D GGUF pack (compact-v1 tensor names; F32/F16/BF16); with
+    // load_tensors the weights are uploaded to the device as by bind().
     bool load(const std::string &path, const std::string &component, bool load_tensors = true,
               std::string *error = nullptr);
     // B200 extension: upload host f32 weights once (16-bit, device-resident).
@@ -96,7 +97,10 @@ public:
                 const SparseTensorF32 *concat_condition = nullptr);
 
 private:
-    struct Impl;
+public:
+    struct Impl;  // defined by the implementation
+
+private:
     Impl *impl_ = nullptr;
 };
 

@@ -316,6 +316,50 @@ void flow_device() {
     else put_error("device_flow_sample", e);
 }
 
+// SLatFlowModel::load from a GGUF pack (written by tests/gguf_pack.py with
+// the bf.* model's weights): header-only load, a missing component, then
+// the full load and one forward on the bf.* inputs.
+void flow_gguf(const std::string &path) {
+    std::string e;
+    {
+        SLatFlowModel info;
+        if (info.load(path, "shape_flow_512", false, &e)) {
+            const SLatFlowHParams &h = info.hparams();
+            put("gguf_info", std::vector<float>{static_cast<float>(info.tensor_count()), info.has_data() ? 1.f : 0.f,
+                                                info.has_tensor("input_layer.weight") ? 1.f : 0.f,
+                                                info.has_tensor("sh512.blocks.0.modulation") ? 1.f : 0.f,
+                                                info.has_tensor("no.such.tensor") ? 1.f : 0.f,
+                                                static_cast<float>(h.model_channels), static_cast<float>(h.num_blocks),
+                                                static_cast<float>(h.num_heads), static_cast<float>(h.cond_channels),
+                                                h.mlp_ratio, static_cast<float>(h.resolution)});
+        } else put_error("gguf_info", e);
+        SparseTensorF32 o;
+        const float t = 0.5f;
+        const bool fwd = info.forward(sparse(I("bf.coords"), F("bf.noise"), 8, 1, 16, 16, 16), &t, 1,
+                                      varlen(F("bf.ctx"), 64, {0, F("bf.ctx").size() / 64}), nullptr, o, &e);
+        put("gguf_no_data_forward_refused", std::vector<float>{fwd ? 0.f : 1.f});
+    }
+    {
+        SLatFlowModel missing;
+        const bool ok = missing.load(path, "texture_flow_1024", true, &e);
+        put("gguf_missing_component_refused",
+            std::vector<float>{!ok && e.find("does not contain") != std::string::npos ? 1.f : 0.f});
+    }
+    SLatFlowModel model;
+    if (!model.load(path, "shape_flow_512", true, &e)) {
+        put_error("gguf_load", e);
+        return;
+    }
+    const SLatFlowHParams &h = model.hparams();
+    const int T = static_cast<int>(F("bf.ctx").size()) / h.cond_channels;
+    const SparseTensorF32 x = sparse(I("bf.coords"), F("bf.noise"), h.in_channels, 1, 16, 16, 16);
+    const VarLenTensorF32 ctx = varlen(F("bf.ctx"), h.cond_channels, {0, static_cast<std::size_t>(T)});
+    SparseTensorF32 o;
+    const float t = F("bf.timestep")[0];
+    if (model.forward(x, &t, 1, ctx, nullptr, o, &e)) put("gguf_flow_forward", o.feats);
+    else put_error("gguf_flow_forward", e);
+}
+
 SLatDecoderBlockWeightsF32 dec_block(int i, bool c2s, int C, int O, int mlp) {
     SLatDecoderBlockWeightsF32 b;
     const std::string p = "dec.b" + std::to_string(i) + ".";
@@ -433,8 +477,8 @@ void sampler() {
 }  // namespace
 
 int main(int argc, char **argv) {
-    if (argc != 3 || !read_inputs(argv[1])) {
-        std::cerr << "usage: host_api_check <inputs.bin> <outputs.bin>\n";
+    if ((argc != 3 && argc != 4) || !read_inputs(argv[1])) {
+        std::cerr << "usage: host_api_check <inputs.bin> <outputs.bin> [<flow pack.gguf>]\n";
         return 2;
     }
     out_file.open(argv[2], std::ios::binary);
@@ -445,6 +489,7 @@ int main(int argc, char **argv) {
         flow_device();
         decoder();
         sampler();
+        if (argc == 4) flow_gguf(argv[3]);
     } catch (const std::exception &ex) {
         std::cerr << "exception: " << ex.what() << "\n";
         return 3;

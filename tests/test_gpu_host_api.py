@@ -107,6 +107,22 @@ def _device_hp():
                          num_heads=2)
 
 
+def _pack_weights():
+    """The bf.* model's weights and the values the test pack stores for them
+    (MLP matrices BF16, other matrices F16, vectors F32)."""
+    from tests._models import random_flow_weights
+    from tests import gguf_pack as G
+    w = random_flow_weights(np.random.default_rng(5), _device_hp())
+    return w, G.stored_flow_weights(w, G.GGML_F16)
+
+
+def _write_flow_pack(path):
+    from tests import gguf_pack as G
+    w, _ = _pack_weights()
+    G.write_pack(path, G.flow_metadata("shape_flow_512", _device_hp(), resolution=16),
+                 G.flow_tensors("sh512", w, G.GGML_F16))
+
+
 @pytest.fixture(scope="module")
 def harness(tmp_path_factory):
     d = tmp_path_factory.mktemp("host_api")
@@ -115,7 +131,9 @@ def harness(tmp_path_factory):
            f"-L{PKG}", "-lpixal3d_b200", "-lp3dcuda", f"-Wl,-rpath,{PKG}", "-o", str(exe)]
     subprocess.run(cmd, check=True, capture_output=True, text=True)
     _write(d / "in.bin", _inputs())
-    r = subprocess.run([str(exe), str(d / "in.bin"), str(d / "out.bin")], capture_output=True, text=True, timeout=600)
+    _write_flow_pack(d / "flow.gguf")
+    r = subprocess.run([str(exe), str(d / "in.bin"), str(d / "out.bin"), str(d / "flow.gguf")], capture_output=True,
+                       text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     return _read(d / "out.bin")
 
@@ -204,3 +222,24 @@ def test_slat_decoder_matches_reference_fixture(harness):
     np.testing.assert_array_equal(harness["dec_c2s_coords"], cc.ravel())
     _close(harness["dec_c2s_output"], hh.ravel(), "c2s block")
     _close(harness["dec_c2s_subdiv"], pp.ravel(), "c2s predicted subdivision")
+
+
+def test_flow_gguf_pack_through_host_api(harness):
+    """SLatFlowModel::load of a GGUF v3 pack (compact-v1 names, F16 matrices,
+    F32 vectors): hyperparameters and tensor index from the header, loading
+    without data refuses forward, a missing component is refused, and the
+    loaded model's forward matches the oracle on the pack's stored values."""
+    from oracle import oracle as O
+    info = harness["gguf_info"]
+    hp = _device_hp()
+    n_tensors = 10 + 21 * hp.num_blocks  # cross mode: no proj_linear
+    np.testing.assert_array_equal(info, [n_tensors, 0, 1, 1, 0, hp.model_channels, hp.num_blocks, hp.num_heads,
+                                         hp.cond_channels, hp.mlp_ratio, 16])
+    assert harness["gguf_no_data_forward_refused"][0] == 1
+    assert harness["gguf_missing_component_refused"][0] == 1
+    a = _inputs()
+    _, st = _pack_weights()
+    c, x, ctx = a["bf.coords"], a["bf.noise"], a["bf.ctx"]
+    one = np.array([0, ctx.shape[0]], np.int64)
+    exp = O.slat_flow_forward(c, x, a["bf.timestep"], one, ctx, None, hp, st)
+    _close(harness["gguf_flow_forward"], exp.ravel(), "GGUF-loaded forward")
