@@ -10,12 +10,14 @@
 // gathered with cp.async into the same 128B-swizzled layout TMA produces
 // (missing neighbour = zero fill), B = W[t] [Cout, Cin] by TMA.
 //
-// CTA = 9 warps, one CTA per SM, persistent over output tiles (n fastest so
-// concurrently running CTAs share A tiles through L2):
-//   warps 0-3  producers: thread 0 issues TMA; for the gather variant all
-//              128 threads issue the row gathers (cp.async, 8 x 16 B each)
+// CTA = 9 warps (13 for the gather variant), one CTA per SM, persistent over
+// output tiles (n fastest so concurrently running CTAs share A tiles through L2):
+//   warps 0-3  producers: thread 0 issues TMA; the gather variant adds
+//              warps 9-12 and all 8 producer warps issue the row gathers
+//              (cp.async, 16 rows per warp, 4 x 16 B per lane per stage)
 //   warps 4-7  epilogue: tcgen05.ld 32 lanes x 32 columns per warp, bias /
-//              activation / gated residual, vector stores
+//              activation / gate, staged in shared memory and written by TMA
+//              box stores (the residual by TMA reduce-add)
 //   warp  8    TMEM allocator + single-thread tcgen05.mma issuer
 // Tile 128 x BN (BN in {64,128,256}), BK = 64 (one 128-byte swizzle atom),
 // UMMA 128 x BN x 16; accumulators double-buffered in TMEM (2*BN columns) so
@@ -41,10 +43,10 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kProducerThreads = 128;
 constexpr int kThreads = 9 * 32;
-// The pair kernel's cp.async gather variant adds 4 producer warps (9-12), so
-// 8 warps share each stage's row gathers (4 cp.async per lane per stage).
+// The cp.async gather variants add 4 producer warps (9-12), so 8 warps share
+// each stage's row gathers (4 cp.async per lane per stage): a warp completes
+// its cp.async instructions slowly, and the stage fill latency bounds the conv.
 constexpr int kThreadsG = 13 * 32;
 constexpr int kGatherThreads = 256;
 constexpr int kMmaWarp = 8;
@@ -521,25 +523,6 @@ __device__ __forceinline__ void prefetch_residual(const GemmParams &p, int64_t r
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rp), "r"(bytes) : "memory");
 }
 
-// One producer stage of the gather variant, issued by the 128 producer
-// threads: A rows [m0, m0+128), columns [kc, kc+64) of x[src(row)], where
-// thread t holds src of row m0 + t.  Warp w owns tile rows [32w, 32w+32);
-// each cp.async instruction copies 4 whole rows, 8 lanes per 128-byte row
-// (source indices exchanged by shuffles): coalesced global reads and
-// conflict-free swizzled shared writes.
-__device__ __forceinline__ void gather_stage_a(const GemmParams &p, uint8_t *sa, int t, int32_t my_src, int kc) {
-    const int lane_ = t & 31;
-    const int chunk = lane_ & 7;
-    const int wrow0 = (t >> 5) * 32;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int r = wrow0 + i * 4 + (lane_ >> 3);
-        const int32_t src = __shfl_sync(0xffffffffu, my_src, i * 4 + (lane_ >> 3));
-        const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
-        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
-    }
-}
-
 // One producer warp's share of a gather stage when 8 warps fill it: tile
 // rows [16 pw, 16 pw + 16), 4 cp.async instructions of 4 rows each (8 lanes
 // per 128-byte row); lane l < 16 holds the source of row 16 pw + l.
@@ -566,7 +549,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *f
 }
 
 template <int BN, bool GATHER>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
     using C = Cfg<BN>;
@@ -595,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full_bar[s], GATHER ? (kProducerThreads + 1) : 1);
+            mbar_init(&full_bar[s], GATHER ? (kGatherThreads + 1) : 1);
             mbar_init(&empty_bar[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -616,9 +599,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp < 4) {
+    if (warp < 4 || (GATHER && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
-        const int t = threadIdx.x;  // 0..127
+        // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) gathers tile
+        // rows [16 pw, 16 pw + 16); lane l < 16 holds row 16 pw + l's source
+        const int t = warp < 4 ? threadIdx.x : 0;  // dense: thread 0 issues the TMA loads
+        const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
+        const int grow = 16 * pw + (lane & 15);
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
@@ -627,8 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t n0 = (tile % n_tiles) * BN;
             int32_t cur_src = 0, next_src = 0;
             if (GATHER) {
-                cur_src = gather_src(p, t, m0, 0);
-                next_src = gather_src(p, t, m0, 1);
+                cur_src = gather_src(p, grow, m0, 0);
+                next_src = gather_src(p, grow, m0, 1);
             }
             for (int kb = 0; kb < num_kb; ++kb) {
                 if (GATHER) {
@@ -649,10 +636,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int kc = (kb % kblocks_per_tap) * BK;
                     if (kc == 0 && tap > 0) {
                         cur_src = next_src;
-                        next_src = gather_src(p, t, m0, tap + 1);
+                        next_src = gather_src(p, grow, m0, tap + 1);
                     }
-                    gather_stage_a(p, sa, t, cur_src, kc);
-                    if (t == 0) {
+                    gather_stage_a16(p, sa, pw, lane, cur_src, kc);
+                    if (warp == 0 && lane == 0) {
                         mbar_arrive_expect_tx(&full_bar[stage], C::B_BYTES);
                         // Tap t's weights are rows [t*N, (t+1)*N) of the stacked [27*N, K] map.
                         tma_load_2d(sb, &tmap_b, &full_bar[stage], kc, static_cast<int>(tap * p.N + n0));
@@ -1095,7 +1082,7 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     }
     const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
-    gemm_tc_kernel<BN, GATHER><<<grid, kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
+    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
