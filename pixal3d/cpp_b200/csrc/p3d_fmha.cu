@@ -113,6 +113,49 @@ __device__ __forceinline__ uint32_t ex2_pair<__nv_bfloat16>(float x0, float x1) 
     return r;
 }
 
+// (a0, a1) * s + (c, c) as one packed f32x2 FMA.
+__device__ __forceinline__ void ffma2(float a0, float a1, float s, float c, float &d0, float &d1) {
+    unsigned long long a, sc, cc, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(sc) : "f"(s));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(cc) : "f"(c));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(sc), "l"(cc));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Row max of 64 scores: 8 chains of 3-input max, then a 3-input tree.
+__device__ __forceinline__ float row_max64(const float *s) {
+    float m[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float a = max3f(s[c], s[8 + c], s[16 + c]);
+        const float b = max3f(a, s[24 + c], s[32 + c]);
+        const float d = max3f(b, s[40 + c], s[48 + c]);
+        m[c] = fmaxf(d, s[56 + c]);
+    }
+    return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// P for 64 scores: x = s * scale_log2 - m by packed f32x2 FMAs, 2^x in
+// packed 16-bit pairs on MUFU.  (Computing part of the exponentials on the
+// FMA pipe by a polynomial measured slower here: the softmax warps are bound
+// by FMA-pipe issue, not by MUFU.)
+template <typename T>
+__device__ __forceinline__ void softmax_p64(const float *s, float scale_log2, float nm, uint32_t (&pk)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float x0, x1;
+        ffma2(s[2 * i], s[2 * i + 1], scale_log2, nm, x0, x1);
+        pk[i] = ex2_pair<T>(x0, x1);
+    }
+}
+
 struct FmhaParams {
     const int32_t *cu_q, *cu_k;
     void *out;
@@ -282,17 +325,7 @@ __global__ void __launch_bounds__(kThreadsF, 2)
 #pragma unroll
                 for (int i = 0; i < kN; ++i) s[i] = i < valid ? s[i] : -INFINITY;
             }
-            // row max as a tree (8 independent chains), not one 64-long chain
-            float m8[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) m8[c] = s[c];
-#pragma unroll
-            for (int i = 8; i < kN; i += 8)
-#pragma unroll
-                for (int c = 0; c < 8; ++c) m8[c] = fmaxf(m8[c], s[i + c]);
-            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-            mx *= p.scale_log2;  // the scale is positive
+            float mx = row_max64(s) * p.scale_log2;
             const bool need = j > 0 && mx > m_run + kRescaleLog2;
             if (j == 0) m_run = mx;
             if (__any_sync(0xffffffffu, need)) {
@@ -318,11 +351,8 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                 tmem_st1(tmem + lane_base + L_COL, l * alpha);
                 tmem_st_wait();
             }
-            const float nm = -m_run;
             uint32_t pk[32];
-#pragma unroll
-            for (int i = 0; i < kN; i += 2)
-                pk[i / 2] = ex2_pair<T>(fmaf(s[i], p.scale_log2, nm), fmaf(s[i + 1], p.scale_log2, nm));
+            softmax_p64<T>(s, p.scale_log2, -m_run, pk);
             tmem_st32(tmem + lane_base + sp_col(b), pk);
             tmem_st_wait();
             tc_fence_before();
