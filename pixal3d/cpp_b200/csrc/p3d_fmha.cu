@@ -22,7 +22,8 @@
 //   O  += P_b V_j              tcgen05.mma with A read from TMEM (P_b),
 //                              B = V (smem, MN-major); O stays in TMEM
 //   l  += P_b 1                the row sums, by the tensor core from the same
-//                              16-bit P (N = 16 against a ones tile)
+//                              16-bit P: the P V MMA has N = 80, its last 16
+//                              columns reading a ones tile (l = O column 64)
 // The running max m is raised lazily: only when a block's max exceeds it by
 // more than 8 (a factor 2^8 in P) does the row's owner wait for the pending
 // P V, rescale O and l in TMEM (ld, scale, st); otherwise P is computed
@@ -46,7 +47,11 @@ constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int Q_BYTES = kM * kD * 2;   // 16 KB
 constexpr int KV_BYTES = kN * kD * 2;  // 8 KB each
-constexpr int ONES_BYTES = 16 * kN * 2;  // B operand of the row-sum MMA: 16 x 64 ones
+// Ones companion of the V stages: the P V MMA runs with N = 80 (64 value
+// dims + 16 ones columns), its second 64-wide MN group read kStages * KV_BYTES
+// past each V stage, so the accumulator's columns 64..79 receive the row sums
+// of the same 16-bit P.
+constexpr int ONES_BYTES = kStages * KV_BYTES;
 constexpr int USED_BYTES = Q_BYTES + kStages * 2 * KV_BYTES + ONES_BYTES + 1024 + 512;
 // Request enough dynamic shared memory that at most two CTAs fit on an SM:
 // two CTAs use 2 x 256 = 512 TMEM columns, a third would wait in tcgen05.alloc.
@@ -55,6 +60,7 @@ static_assert(USED_BYTES <= SMEM_BYTES, "smem layout exceeds the request");
 constexpr uint32_t TMEM_COLS = 256;  // S/P 0 (64) | S/P 1 (64) | O (64) | l (16) | unused
 constexpr uint32_t O_COL = 128;
 constexpr uint32_t L_COL = 192;
+static_assert(L_COL == O_COL + kD, "the row sum is accumulator column 64 of the N = 80 P V MMA");
 
 __device__ __forceinline__ uint32_t sp_col(int b) { return b ? 64u : 0u; }
 
@@ -250,10 +256,8 @@ __global__ void __launch_bounds__(kThreadsF, 2)
         // ------------------------------------------------------------- MMA
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f32acc(kM, kN, kBf16);
-            const uint32_t idesc_o = idesc_f32acc(kM, kD, kBf16, true);
-            const uint32_t idesc_l = idesc_f32acc(kM, 16, kBf16);
+            const uint32_t idesc_ol = idesc_f32acc(kM, kD + 16, kBf16, true);  // O and l together
             const uint32_t q_addr = smem_u32(sQ);
-            const uint32_t ones_addr = smem_u32(sOnes);
             bool ok = mbar_wait(q_full, 0, p.fault);
             auto issue_pv = [&](int i) -> bool {
                 const int b = i & 1, st = i % kStages;
@@ -261,12 +265,10 @@ __global__ void __launch_bounds__(kThreadsF, 2)
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV + st * KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < kN / 16; ++kk) {  // 16 keys = 8 packed TMEM columns of P
-                    umma_f16_ts(tmem + O_COL, tmem + sp_col(b) + kk * 8, sw128_desc_mn(v_addr + kk * 2048, kN * 128),
-                                idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_f16_ts(tmem + L_COL, tmem + sp_col(b) + kk * 8, sw128_desc(ones_addr + kk * 32), idesc_l,
+                for (int kk = 0; kk < kN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
+                    umma_f16_ts(tmem + O_COL, tmem + sp_col(b) + kk * 8,
+                                sw128_desc_mn(v_addr + kk * 2048, kStages * KV_BYTES), idesc_ol,
                                 (i > 0 || kk > 0) ? 1u : 0u);
-                }
                 umma_commit(&pv_done[b]);
                 umma_commit(&kv_empty[st]);
                 return true;
