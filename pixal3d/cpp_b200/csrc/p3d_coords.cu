@@ -249,6 +249,42 @@ __global__ void down_mean_kernel(const T *__restrict__ x, int64_t m, int channel
     }
 }
 
+// f32 rows, 8 children, channels % 4 == 0: one warp per parent row, float4
+// per lane, the 8 children's loads issued before the sums (added in child
+// order, as the scalar kernel does).
+__global__ void down_mean8_f32_kernel(const float *__restrict__ x, int64_t m, int channels,
+                                      const int32_t *__restrict__ child, float *__restrict__ out) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= m) return;
+    const int lane = threadIdx.x & 31;
+    int32_t src[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) src[o] = __ldg(child + row * 8 + o);
+    const int c4 = channels / 4;
+    for (int c = lane; c < c4; c += 32) {
+        float4 v[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o)
+            v[o] = src[o] >= 0 ? __ldg(reinterpret_cast<const float4 *>(x + static_cast<int64_t>(src[o]) * channels) + c)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        int cnt = 0;
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            if (src[o] >= 0) {
+                s.x += v[o].x;
+                s.y += v[o].y;
+                s.z += v[o].z;
+                s.w += v[o].w;
+                ++cnt;
+            }
+        }
+        const float inv = cnt ? static_cast<float>(cnt) : 1.0f;
+        reinterpret_cast<float4 *>(out + row * channels)[c] =
+            cnt ? make_float4(s.x / inv, s.y / inv, s.z / inv, s.w / inv) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
 template <typename T>
 __global__ void gather_rows_kernel(const T *__restrict__ x, int64_t n, int channels, const int32_t *__restrict__ idx,
                                    T *__restrict__ out) {
@@ -494,6 +530,12 @@ extern "C" int p3d_downsample_mean(p3d_ctx *ctx, const void *x, int64_t m, int c
     if (m == 0) return P3D_OK;
     const int nchild = factor * factor * factor;
     const unsigned grid = blocks_for(m, 8);
+    if (dtype == P3D_F32 && nchild == 8 && channels % 4 == 0 &&
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+        down_mean8_f32_kernel<<<grid, 256, 0, ctx->stream>>>(static_cast<const float *>(x), m, channels, child,
+                                                              static_cast<float *>(out));
+        return check_launch(ctx, "down_mean");
+    }
     P3D_DISPATCH(dtype, T,
                  down_mean_kernel<T><<<grid, 256, 0, ctx->stream>>>(static_cast<const T *>(x), m, channels, nchild,
                                                                     child, static_cast<T *>(out)));

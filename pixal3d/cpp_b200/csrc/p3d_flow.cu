@@ -67,10 +67,17 @@ __device__ __forceinline__ float act_f(float v, int act) {
     return v;
 }
 
+// y[r, n] = act_out(bias[n] + sum_k W[n, k] act_in(x[r, k])) for a few rows
+// (timestep MLP, modulation): one warp per output n, W rows read coalesced
+// with 4 loads in flight per lane; act_in(x) is applied once per block into
+// shared memory (rows * K floats, dynamic).
 template <int B>
 __global__ void small_linear_kernel(const float *__restrict__ x, int K, const float *__restrict__ W,
                                     const float *__restrict__ bias, int N, float *__restrict__ y, int act_in,
                                     int act_out, int rows) {
+    extern __shared__ float xs[];  // [rows][K]
+    for (int i = threadIdx.x; i < rows * K; i += blockDim.x) xs[i] = act_f(x[i], act_in);
+    __syncthreads();
     const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (n >= N) return;
     const int lane = threadIdx.x & 31;
@@ -78,11 +85,21 @@ __global__ void small_linear_kernel(const float *__restrict__ x, int K, const fl
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[b] = 0.0f;
     const float *w = W + static_cast<int64_t>(n) * K;
-    for (int k = lane; k < K; k += 32) {
-        const float wv = w[k];
+    int k = lane;
+    for (; k + 96 < K; k += 128) {
+        const float w0 = __ldg(w + k), w1 = __ldg(w + k + 32), w2 = __ldg(w + k + 64), w3 = __ldg(w + k + 96);
 #pragma unroll
         for (int b = 0; b < B; ++b)
-            if (b < rows) acc[b] += wv * act_f(x[b * K + k], act_in);
+            if (b < rows) {
+                const float *xb = xs + b * K + k;
+                acc[b] += w0 * xb[0] + w1 * xb[32] + w2 * xb[64] + w3 * xb[96];
+            }
+    }
+    for (; k < K; k += 32) {
+        const float wv = __ldg(w + k);
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (b < rows) acc[b] += wv * xs[b * K + k];
     }
 #pragma unroll
     for (int b = 0; b < B; ++b) {
@@ -93,10 +110,14 @@ __global__ void small_linear_kernel(const float *__restrict__ x, int K, const fl
 
 int small_linear(p3d_ctx *ctx, const float *x, int rows, int K, const float *W, const float *b, int N, float *y,
                  int act_in, int act_out) {
-    for (int r0 = 0; r0 < rows; r0 += 16) {
-        const int r = rows - r0 < 16 ? rows - r0 : 16;
-        small_linear_kernel<16><<<blocks_for(N, 8), 256, 0, ctx->stream>>>(x + r0 * K, K, W, b, N, y + r0 * N, act_in,
-                                                                          act_out, r);
+    // up to 4 rows per call, rows * K floats of shared memory (<= 48 KB)
+    const int per_call = std::min(4, (48 * 1024 / 4) / std::max(K, 1));
+    if (per_call < 1) return set_error(ctx, P3D_ERR_UNSUPPORTED, "small_linear: K too large");
+    for (int r0 = 0; r0 < rows; r0 += per_call) {
+        const int r = rows - r0 < per_call ? rows - r0 : per_call;
+        const size_t smem = sizeof(float) * static_cast<size_t>(r) * K;
+        small_linear_kernel<4><<<blocks_for(N, 8), 256, smem, ctx->stream>>>(
+            x + static_cast<int64_t>(r0) * K, K, W, b, N, y + static_cast<int64_t>(r0) * N, act_in, act_out, r);
         int rc = check_launch(ctx, "small_linear");
         if (rc) return rc;
     }
