@@ -319,6 +319,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        # NCCL's own log lines (e.g. "NCCL version ..." under NCCL_DEBUG) go to
+        # stderr, so rank 0's stdout carries only the JSON result line.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     from pixal3d.cpp_b200 import dist as D
