@@ -274,6 +274,50 @@ int p3d_window_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k
                          int max_window_rows, int64_t n, int heads, int head_dim, float scale, int dtype,
                          void *scratch, size_t scratch_bytes, void *out, int64_t ldo);
 
+/* ------------------------------------------------- projection conditioning */
+
+/* One camera view of an image feature map (ProjectionView plus the view's
+ * ProjectionGridOptions::image_resolution, include/pixal3d/projection.h:13-55).
+ * feature_map: DEVICE f32 [height][width][channels], row-major.  The camera
+ * is the canonical front view at `distance` unless has_transform, in which
+ * case transform_matrix is the row-major camera-to-world matrix. */
+typedef struct p3d_projection_view {
+    const float *feature_map;
+    int height, width, channels;
+    int image_resolution;
+    float camera_angle_x, distance, mesh_scale;
+    int has_transform;
+    float transform_matrix[16];
+} p3d_projection_view;
+
+/* Project points of a grid_resolution^3 grid into each view and sample its
+ * map with grid_sample's bilinear / align_corners=False / border rules.
+ * coords: sparse rows (0, x, y, z) with 0 <= x, y, z < grid_resolution
+ * (project_grid_features_at_coords, src/projection.cpp:359-434), or NULL
+ * for all n == grid_resolution^3 cells in meshgrid "ij" order
+ * (project_grid_features, :342-357).  With nviews > 1 (at most 8, equal
+ * channel counts) the output is the f32 sum over views in order times
+ * 1/nviews (project_grid_features_average, :436-481; the per-view sum of
+ * project_condition_stage_multiview_average_f32, src/condition.cpp:
+ * 878-940).  out: [n][ldo] f32/bf16/f16, columns [0, channels) written, so a
+ * second call at out + channels appends another map's channels (the DINO |
+ * NAF concatenation of src/condition.cpp:797-812).  valid: u8 [n] or NULL,
+ * 1 where some view projects the point inside the image and in front of the
+ * camera.  Features and flags equal the reference's f32 CPU results bit for
+ * bit.  Option / camera errors carry the reference's messages; a coordinate
+ * outside the grid latches P3D_ERR_INVALID (its row is written as zeros).
+ * n == 0 validates the views and options only. */
+int p3d_project_features(p3d_ctx *ctx, const p3d_projection_view *views, int nviews, int grid_resolution,
+                         const int32_t *coords, int64_t n, void *out, int64_t ldo, int out_dtype,
+                         uint8_t *valid);
+
+/* Host math, no device work: relative[i] = F(distances[0]) *
+ * inverse(c2w[0]) * c2w[i] for row-major 4x4 matrices (HOST pointers,
+ * c2w/relative [nviews][16]); compute_relative_calc_matrices,
+ * src/projection.cpp:528-561.  ctx may be NULL (no message kept). */
+int p3d_projection_relative_matrices(p3d_ctx *ctx, const float *c2w, const float *distances, int nviews,
+                                     float *relative);
+
 /* ------------------------------------------------------ fused elementwise */
 
 /* x[i, c] += sinusoidal absolute 3D position embedding of coords[i] (no

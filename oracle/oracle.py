@@ -792,3 +792,215 @@ def swin_decoder_forward(coords, x, cfg: dict, w: dict, masks):
         h = resblock3d_io(coords, h, sw, cfg.get("groups", 32))
     out = linear(layer_norm(h, 1e-5), w["output_w"], w["output_b"])
     return coords, out
+
+
+# --------------------------------------------------------------------------
+# Projection conditioning (image_attn_mode=proj producer)
+# --------------------------------------------------------------------------
+
+@dataclass
+class ProjCamera:
+    """ProjectionCamera (include/pixal3d/projection.h:13-27)."""
+    camera_angle_x: float = 0.2
+    distance: float = 2.0
+    mesh_scale: float = 1.0
+    transform: np.ndarray | None = None  # row-major [16] camera-to-world, or None (front view)
+
+
+def front_matrix(distance: float) -> np.ndarray:
+    """src/projection.cpp:21-29: canonical front-view camera-to-world."""
+    d = F32(distance)
+    return np.array([1, 0, 0, 0, 0, 0, -1, -d, 0, 1, 0, 0, 0, 0, 0, 1], F32)
+
+
+def matmul4(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """multiply4x4 (src/projection.cpp:31-45): f32 sum over k in order."""
+    a = np.asarray(a, F32).reshape(4, 4)
+    b = np.asarray(b, F32).reshape(4, 4)
+    out = np.zeros((4, 4), F32)
+    for r in range(4):
+        for c in range(4):
+            v = F32(0)
+            for k in range(4):
+                v = F32(v + F32(a[r, k] * b[k, c]))
+            out[r, c] = v
+    return out.reshape(16)
+
+
+def invert4(m: np.ndarray):
+    """invert4x4 (src/projection.cpp:47-98): Gauss-Jordan on [M | I] with
+    partial pivoting (first row of largest |pivot|), f32 arithmetic; None when
+    the pivot is not > 1e-8 or not finite."""
+    a = np.zeros((4, 8), F32)
+    a[:, :4] = np.asarray(m, F32).reshape(4, 4)
+    for r in range(4):
+        a[r, r + 4] = 1
+    for col in range(4):
+        piv = col
+        pabs = abs(a[piv, col])
+        for row in range(col + 1, 4):
+            if abs(a[row, col]) > pabs:
+                piv, pabs = row, abs(a[row, col])
+        if not (pabs > F32(1e-8)) or not np.isfinite(pabs):
+            return None
+        if piv != col:
+            a[[piv, col]] = a[[col, piv]]
+        s = a[col, col]
+        a[col] = (a[col] / s).astype(F32)
+        for row in range(4):
+            if row == col:
+                continue
+            f = a[row, col]
+            if f == 0:
+                continue
+            a[row] = (a[row] - (f * a[col]).astype(F32)).astype(F32)
+    return np.ascontiguousarray(a[:, 4:]).reshape(16)
+
+
+def projection_constants(cam: ProjCamera, image_resolution: int) -> dict:
+    """prepare_projection_view (src/projection.cpp:233-259) and the option
+    checks of validate_options (:205-231).  Raises ValueError with the
+    reference's messages."""
+    if image_resolution <= 0:
+        raise ValueError("image_resolution must be positive")
+    ang = F32(cam.camera_angle_x)
+    if not (F32(0) < ang < F32(math.pi)) or not np.isfinite(ang):
+        raise ValueError("camera_angle_x must be finite and in (0, pi)")
+    if not (F32(cam.mesh_scale) > 0) or not np.isfinite(F32(cam.mesh_scale)):
+        raise ValueError("mesh_scale must be finite and positive")
+    if cam.transform is None and (not (F32(cam.distance) > 0) or not np.isfinite(F32(cam.distance))):
+        raise ValueError("distance must be finite and positive")
+    c2w = front_matrix(cam.distance) if cam.transform is None else np.asarray(cam.transform, F32).reshape(16)
+    w2c = invert4(c2w)
+    if w2c is None:
+        raise ValueError("camera transform matrix is singular")
+    focal = F32(F32(16.0) / F32(math.tan(float(F32(ang * F32(0.5))))))
+    return {"w2c": w2c, "scale": F32(F32(1.0) / F32(F32(cam.mesh_scale) * F32(2.0))),
+            "focal_px": F32(F32(focal * F32(image_resolution)) / F32(32.0)),
+            "half": F32(F32(image_resolution) * F32(0.5))}
+
+
+def grid_base(i: np.ndarray, r: int) -> np.ndarray:
+    """-1 + 2 i / (r - 1) as in project_one (src/projection.cpp:276-291)."""
+    if r == 1:
+        return np.zeros(i.shape, F32)
+    return (F32(-1.0) + ((F32(2.0) * i.astype(F32)) / F32(r - 1)).astype(F32)).astype(F32)
+
+
+def project_points(ix, iy, iz, r: int, k: dict, image_resolution: int):
+    """project_point (src/projection.cpp:116-146) of grid cells (ix, iy, iz)
+    after the (x, y, z) -> (x, -z, y) * scale map (:293-298).  Returns
+    x_pixel, y_pixel, valid (float32, float32, bool arrays)."""
+    bx, by, bz = grid_base(ix, r), grid_base(iy, r), grid_base(iz, r)
+    s = k["scale"]
+    x = (bx * s).astype(F32)
+    y = (-bz * s).astype(F32)
+    z = (by * s).astype(F32)
+    w = k["w2c"]
+
+    def row(o):
+        t = (F32(w[o]) * x).astype(F32) + (F32(w[o + 1]) * y).astype(F32)
+        t = t.astype(F32) + (F32(w[o + 2]) * z).astype(F32)
+        return (t.astype(F32) + F32(w[o + 3])).astype(F32)
+
+    xc, yc, zc = row(0), row(4), row(8)
+    depth = (-zc).astype(F32)
+    den = ((-zc).astype(F32) + F32(1e-8)).astype(F32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        xn = ((k["focal_px"] * xc).astype(F32) / den).astype(F32)
+        yn = ((k["focal_px"] * yc).astype(F32) / den).astype(F32)
+    xp = (xn + k["half"]).astype(F32)
+    yp = ((-yn).astype(F32) + k["half"]).astype(F32)
+    res = F32(image_resolution)
+    valid = (xp >= 0) & (xp < res) & (yp >= 0) & (yp < res) & (depth > 0)
+    return xp, yp, valid
+
+
+def _clamp_ref(v, hi):
+    """std::max(0, std::min(v, hi)) with the std:: comparison semantics
+    (a NaN input ends at 0)."""
+    t = np.where(F32(hi) < v, F32(hi), v)
+    return np.where(F32(0) < t, t, F32(0)).astype(F32)
+
+
+def bilinear_sample(fmap: np.ndarray, xp, yp, image_resolution: int) -> np.ndarray:
+    """bilinear_weights + sample_bilinear_channel (src/projection.cpp:155-203):
+    grid_sample bilinear, align_corners=False, padding border.  fmap f32
+    [H, W, C]; returns [P, C]."""
+    h, w, _ = fmap.shape
+    res = F32(image_resolution)
+    x = (((xp + F32(0.5)).astype(F32) * F32(w)).astype(F32) / res).astype(F32) - F32(0.5)
+    y = (((yp + F32(0.5)).astype(F32) * F32(h)).astype(F32) / res).astype(F32) - F32(0.5)
+    x = _clamp_ref(x.astype(F32), w - 1)
+    y = _clamp_ref(y.astype(F32), h - 1)
+    x0 = np.floor(x).astype(np.int64)
+    y0 = np.floor(y).astype(np.int64)
+    x1 = np.minimum(x0 + 1, w - 1)
+    y1 = np.minimum(y0 + 1, h - 1)
+    wx = (x - x0.astype(F32)).astype(F32)[:, None]
+    wy = (y - y0.astype(F32)).astype(F32)[:, None]
+    fm = np.asarray(fmap, F32)
+    tl, tr = fm[y0, x0], fm[y0, x1]
+    bl, br = fm[y1, x0], fm[y1, x1]
+    omx = (F32(1) - wx).astype(F32)
+    omy = (F32(1) - wy).astype(F32)
+    top = ((tl * omx).astype(F32) + (tr * wx).astype(F32)).astype(F32)
+    bot = ((bl * omx).astype(F32) + (br * wx).astype(F32)).astype(F32)
+    return ((top * omy).astype(F32) + (bot * wy).astype(F32)).astype(F32)
+
+
+def project_features_at_coords(fmap, grid_resolution: int, image_resolution: int, cam: ProjCamera, coords):
+    """project_grid_features_at_coords (src/projection.cpp:359-434): features
+    [N, C] and valid [N] (uint8) for sparse (0, x, y, z) rows of a
+    grid_resolution^3 grid.  Raises ValueError like the reference."""
+    if grid_resolution <= 0:
+        raise ValueError("grid_resolution must be positive")
+    k = projection_constants(cam, image_resolution)
+    c = np.asarray(coords, np.int32).reshape(-1, 4)
+    bad = (c[:, 0] != 0) | (c[:, 1:] < 0).any(1) | (c[:, 1:] >= grid_resolution).any(1)
+    if bad.any():
+        raise ValueError("sparse projection coordinate is outside the requested grid")
+    xp, yp, valid = project_points(c[:, 1], c[:, 2], c[:, 3], grid_resolution, k, image_resolution)
+    return bilinear_sample(np.asarray(fmap, F32), xp, yp, image_resolution), valid.astype(np.uint8)
+
+
+def dense_grid_coords(r: int) -> np.ndarray:
+    """All r^3 cells in torch.meshgrid(indexing="ij") order as (0, x, y, z)."""
+    i = np.arange(r ** 3, dtype=np.int64)
+    return np.stack([np.zeros_like(i), i // (r * r), (i // r) % r, i % r], 1).astype(np.int32)
+
+
+def project_features_average(fmaps, grid_resolution: int, image_resolution: int, cams, coords=None):
+    """project_grid_features_average (src/projection.cpp:436-481) when coords
+    is None (dense grid), else the per-view sum of the multi-view condition
+    projection (src/condition.cpp:878-940): f32 sum over views in order, then
+    * (1 / views); valid = any view's valid."""
+    if len(fmaps) == 0:
+        raise ValueError("at least one projection view is required")
+    if coords is None:
+        coords = dense_grid_coords(grid_resolution)
+    acc, val = None, None
+    for fm, cam in zip(fmaps, cams):
+        f, v = project_features_at_coords(fm, grid_resolution, image_resolution, cam, coords)
+        acc = f if acc is None else (acc + f).astype(F32)
+        val = v if val is None else (val | v)
+    if len(fmaps) > 1:
+        acc = (acc * F32(F32(1.0) / F32(len(fmaps)))).astype(F32)
+    return acc, val
+
+
+def relative_calc_matrices(c2w, distances):
+    """compute_relative_calc_matrices (src/projection.cpp:528-561):
+    relative[i] = F(distance[0]) * inverse(c2w[0]) * c2w[i]."""
+    if len(c2w) == 0:
+        raise ValueError("at least one camera transform is required")
+    if len(c2w) != len(distances):
+        raise ValueError("camera transform and distance counts must match")
+    d0 = F32(distances[0])
+    if not (d0 > 0) or not np.isfinite(d0):
+        raise ValueError("main-view distance must be finite and positive")
+    inv = invert4(c2w[0])
+    if inv is None:
+        raise ValueError("main-view camera transform matrix is singular")
+    f = front_matrix(d0)
+    return [matmul4(f, matmul4(inv, m)) for m in c2w]

@@ -13,6 +13,7 @@
 #include "pixal3d/cpu_threads.h"
 #include "pixal3d/flow.h"
 #include "pixal3d/flow_sampler.h"
+#include "pixal3d/projection.h"
 #include "pixal3d/slat_decoder.h"
 #include "pixal3d/slat_flow.h"
 #include "pixal3d/sparse.h"
@@ -99,6 +100,16 @@ SparseTransformerBlockWeightsF32 block_weights(const float * const * p) {
     w.mlp2_weight = p[21];
     w.mlp2_bias = p[22];
     return w;
+}
+
+// ProjectionCamera from plain values (include/pixal3d/projection.h:13-27).
+ProjectionCamera make_camera(float angle, float distance, float mesh_scale, int has_transform, const float * m16) {
+    ProjectionCamera cam = ProjectionCamera::front(angle, distance, mesh_scale);
+    if (has_transform) {
+        cam.has_transform = true;
+        for (int i = 0; i < 16; ++i) cam.transform_matrix[static_cast<size_t>(i)] = m16[i];
+    }
+    return cam;
 }
 
 }  // namespace
@@ -539,6 +550,67 @@ int p3dref_resblock_c2s(const int32_t * coords, int64_t n, int batch, int sx, in
     copy_out(o.feats, out_feats);
     *out_n = static_cast<int64_t>(o.points());
     if (pred && pred_subdiv) copy_out(pr.feats, pred);
+    return 0;
+}
+
+// project_grid_features_at_coords (src/projection.cpp:359-434): feats [n][c], valid [n].
+int p3dref_project_at_coords(const float * fmap, int h, int w, int c, int grid_resolution, int image_resolution,
+                             float angle, float distance, float mesh_scale, int has_transform, const float * m16,
+                             const int32_t * coords, int64_t n, float * feats, uint8_t * valid, char * err,
+                             int errlen) {
+    ProjectionGridOptions opt;
+    opt.grid_resolution = grid_resolution;
+    opt.image_resolution = image_resolution;
+    std::vector<std::int32_t> cv(coords, coords + 4 * n);
+    std::vector<float> f;
+    std::vector<std::uint8_t> v;
+    std::string e;
+    if (!project_grid_features_at_coords(fmap, h, w, c, opt, make_camera(angle, distance, mesh_scale, has_transform, m16),
+                                         cv, f, v, &e))
+        return fail(e, err, errlen);
+    copy_out(f, feats);
+    std::memcpy(valid, v.data(), v.size());
+    return 0;
+}
+
+// project_grid_features_average (src/projection.cpp:436-481) over nviews maps
+// of one shape: feats [r^3][c], valid [r^3].  cams: [nviews][4] (angle,
+// distance, mesh_scale, has_transform), m16: [nviews][16].
+int p3dref_project_average(const float * const * fmaps, int nviews, int h, int w, int c, int grid_resolution,
+                           int image_resolution, const float * cams, const float * m16, float * feats,
+                           uint8_t * valid, char * err, int errlen) {
+    ProjectionGridOptions opt;
+    opt.grid_resolution = grid_resolution;
+    opt.image_resolution = image_resolution;
+    std::vector<ProjectionView> views;
+    for (int i = 0; i < nviews; ++i) {
+        ProjectionView view;
+        view.feature_map = fmaps[i];
+        view.height = h;
+        view.width = w;
+        view.channels = c;
+        view.camera = make_camera(cams[4 * i], cams[4 * i + 1], cams[4 * i + 2], cams[4 * i + 3] != 0.0f, m16 + 16 * i);
+        views.push_back(view);
+    }
+    ProjectedGrid g;
+    std::string e;
+    if (!project_grid_features_average(views, opt, g, &e)) return fail(e, err, errlen);
+    copy_out(g.features, feats);
+    std::memcpy(valid, g.valid.data(), g.valid.size());
+    return 0;
+}
+
+// compute_relative_calc_matrices (src/projection.cpp:528-561): relative [n][16].
+int p3dref_relative_matrices(const float * c2w, const float * distances, int n, float * relative, char * err,
+                             int errlen) {
+    std::vector<std::array<float, 16>> m(static_cast<size_t>(n)), out;
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < 16; ++j) m[static_cast<size_t>(i)][static_cast<size_t>(j)] = c2w[16 * i + j];
+    std::vector<float> d(distances, distances + n);
+    std::string e;
+    if (!compute_relative_calc_matrices(m, d, out, &e)) return fail(e, err, errlen);
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < 16; ++j) relative[16 * i + j] = out[static_cast<size_t>(i)][static_cast<size_t>(j)];
     return 0;
 }
 

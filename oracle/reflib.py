@@ -343,3 +343,52 @@ def resblock_c2s(coords, x, w, eps, out_channels, pred_subdiv, subdiv=None, batc
                                      err, 512), err)
     m = on.value
     return oc[:m].copy(), of[:m].copy(), pred
+
+
+def _m16(cam):
+    return _c(cam.transform if cam.transform is not None else np.zeros(16, np.float32), np.float32).reshape(16)
+
+
+def project_at_coords(fmap, grid_resolution, image_resolution, cam, coords):
+    """project_grid_features_at_coords (src/projection.cpp:359-434); cam is an
+    oracle.ProjCamera.  Returns (features [N, C], valid [N] uint8)."""
+    fmap, coords = _c(fmap, np.float32), _c(coords, np.int32)
+    h, w, c = fmap.shape
+    n = coords.shape[0]
+    m16 = _m16(cam)
+    feats = np.empty((n, c), np.float32)
+    valid = np.empty(n, np.uint8)
+    err = _err()
+    _check(lib().p3dref_project_at_coords(fmap.ctypes, h, w, c, grid_resolution, image_resolution,
+                                          C.c_float(cam.camera_angle_x), C.c_float(cam.distance),
+                                          C.c_float(cam.mesh_scale), int(cam.transform is not None), m16.ctypes,
+                                          coords.ctypes, C.c_int64(n), feats.ctypes, valid.ctypes, err, 512), err)
+    return feats, valid
+
+
+def project_average(fmaps, grid_resolution, image_resolution, cams):
+    """project_grid_features_average (src/projection.cpp:436-481) over views of
+    one map shape: (features [r^3, C], valid [r^3] uint8)."""
+    fmaps = [_c(f, np.float32) for f in fmaps]
+    h, w, c = fmaps[0].shape
+    ptrs = (C.c_void_p * len(fmaps))(*[f.ctypes.data for f in fmaps])
+    camv = np.array([[k.camera_angle_x, k.distance, k.mesh_scale, float(k.transform is not None)] for k in cams],
+                    np.float32)
+    m16 = np.ascontiguousarray(np.stack([_m16(k) for k in cams]))
+    pts = grid_resolution ** 3
+    feats = np.empty((pts, c), np.float32)
+    valid = np.empty(pts, np.uint8)
+    err = _err()
+    _check(lib().p3dref_project_average(ptrs, len(fmaps), h, w, c, grid_resolution, image_resolution, camv.ctypes,
+                                        m16.ctypes, feats.ctypes, valid.ctypes, err, 512), err)
+    return feats, valid
+
+
+def relative_matrices(c2w, distances):
+    """compute_relative_calc_matrices (src/projection.cpp:528-561): [n, 16]."""
+    m = np.ascontiguousarray(np.asarray(c2w, np.float32).reshape(-1, 16))
+    d = _c(distances, np.float32)
+    out = np.empty_like(m)
+    err = _err()
+    _check(lib().p3dref_relative_matrices(m.ctypes, d.ctypes, m.shape[0], out.ctypes, err, 512), err)
+    return out

@@ -79,6 +79,13 @@ class FlowWeights(C.Structure):
         ("io_out", C.POINTER(ResBlockWeights))]
 
 
+class ProjectionView(C.Structure):
+    """p3d_projection_view (include/p3d.h)."""
+    _fields_ = [("feature_map", vp), ("height", i32), ("width", i32), ("channels", i32), ("image_resolution", i32),
+                ("camera_angle_x", f32), ("distance", f32), ("mesh_scale", f32), ("has_transform", i32),
+                ("transform_matrix", f32 * 16)]
+
+
 class SamplerConfig(C.Structure):
     _fields_ = [("steps", i32), ("sigma_min", f32), ("rescale_t", f32), ("guidance_strength", f32),
                 ("guidance_rescale", f32), ("guidance_interval_min", f32), ("guidance_interval_max", f32),
@@ -124,6 +131,8 @@ _sig("p3d_subm_conv3d", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i3
 _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, i64, i64, i64, i32, i32, f32,
      i32)
 _sig("p3d_ape_add", i32, vp, vp, i64, i32, vp)
+_sig("p3d_project_features", i32, vp, C.POINTER(ProjectionView), i32, i32, vp, i64, vp, i64, i32, vp)
+_sig("p3d_projection_relative_matrices", i32, vp, vp, vp, i32, vp)
 _sig("p3d_batch_offsets", i32, vp, vp, i64, i32, vp)
 _sig("p3d_window_count", i64, i32, i32, i32, i32, i32, i32)
 _sig("p3d_window_partition_workspace", C.c_size_t, i64, i64)

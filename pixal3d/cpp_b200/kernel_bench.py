@@ -160,6 +160,23 @@ def run(kernel: str, reps: int) -> dict:
         ms = _time(lambda: ops.varlen_attention(q, k, v, cq, ck, nq, 16, 0.125, out=out), reps)
         flops = 2 * 4.0 * nq * nk * C
         return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
+    if kernel in ("project", "project3"):
+        # projection conditioning: the 64^3 shell sampled from 37 x 37 x 1024
+        # DINO-sized maps (1 or 3 views), f16 rows for the proj_linear GEMM
+        nv = 1 if kernel == "project" else 3
+        coords = torch.from_numpy(shell_coords()).to(dev)
+        coords[:, 0] = 0
+        n = coords.shape[0]
+        maps = [torch.randn((37, 37, C), device=dev, generator=g) for _ in range(nv)]
+        views = [{"feature_map": m, "image_resolution": 518, "camera_angle_x": 0.6, "distance": 2.0,
+                  "mesh_scale": 1.0} for m in maps]
+        out = torch.empty((n, C), device=dev, dtype=torch.float16)
+        valid = torch.empty(n, device=dev, dtype=torch.uint8)
+        ms = _time(lambda: ops.project_features(views, 64, coords, out=out, valid=valid), reps)
+        write = n * C * 2 + n * 17
+        corner = 4 * n * C * 4 * nv
+        return {"kernel": kernel, "ms": ms, "points": n, "views": nv, "write_bytes": write, "corner_bytes": corner,
+                "write_gbs": write / ms / 1e6, "corner_gbs": corner / ms / 1e6}
     raise SystemExit(f"unknown kernel {kernel}")
 
 

@@ -299,6 +299,56 @@ def ape_add_(x: torch.Tensor, coords: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def project_features(views, grid_resolution: int, coords: torch.Tensor | None = None, out_dtype=torch.float32,
+                     out: torch.Tensor | None = None, valid: torch.Tensor | None = None):
+    """Projected image features of grid points (p3d_project_features): views
+    is a list of dicts with "feature_map" (f32 [H, W, C] on the device),
+    "image_resolution", "camera_angle_x", "distance", "mesh_scale" and an
+    optional row-major camera-to-world "transform" (16 floats).  coords None
+    projects the whole grid in meshgrid "ij" order.  Returns (out, valid)."""
+    fm0 = views[0]["feature_map"]
+    dev = fm0.device
+    c = ctx(dev)
+    arr = (L.ProjectionView * len(views))()
+    for i, v in enumerate(views):
+        fm = v["feature_map"]
+        assert fm.dtype == torch.float32 and fm.is_contiguous() and fm.dim() == 3
+        pv = arr[i]
+        pv.feature_map = fm.data_ptr()
+        pv.height, pv.width, pv.channels = fm.shape
+        pv.image_resolution = int(v["image_resolution"])
+        pv.camera_angle_x = float(v["camera_angle_x"])
+        pv.distance = float(v.get("distance", 2.0))
+        pv.mesh_scale = float(v.get("mesh_scale", 1.0))
+        t = v.get("transform")
+        pv.has_transform = int(t is not None)
+        if t is not None:
+            for j, x in enumerate([float(a) for a in list(t)]):
+                pv.transform_matrix[j] = x
+    n = coords.shape[0] if coords is not None else grid_resolution ** 3
+    ch = fm0.shape[2]
+    if out is None:
+        out = torch.empty((n, ch), dtype=out_dtype, device=dev)
+    if valid is None:
+        valid = torch.empty(n, dtype=torch.uint8, device=dev)
+    c.check(L.lib.p3d_project_features(c.h, arr, len(views), grid_resolution, _p(coords), n, _p(out), out.stride(0),
+                                       _dt(out), _p(valid)))
+    return out, valid
+
+
+def projection_relative_matrices(c2w, distances):
+    """Host math (p3d_projection_relative_matrices, no device needed):
+    [n, 16] float32 numpy."""
+    import numpy as np
+    m = np.ascontiguousarray(np.asarray(c2w, np.float32).reshape(-1, 16))
+    d = np.ascontiguousarray(np.asarray(distances, np.float32))
+    out = np.empty_like(m)
+    rc = L.lib.p3d_projection_relative_matrices(None, m.ctypes.data, d.ctypes.data, m.shape[0], out.ctypes.data)
+    if rc != 0:
+        raise P3DError(rc, "p3d_projection_relative_matrices failed")
+    return out
+
+
 def layernorm_modulate(x: torch.Tensor, eps: float, gamma=None, beta=None, mod: torch.Tensor | None = None,
                        batch_offsets: torch.Tensor | None = None, out_dtype=torch.bfloat16,
                        out: torch.Tensor | None = None) -> torch.Tensor:

@@ -9,7 +9,8 @@ Run where the reference checkout is mounted (it is not on the GPU box):
 2. Runs each fixture and stores its stdout verbatim as <fixture>.txt.  These
    are the reference's own known-answer outputs (max_digits10 floats).
 3. Calls the compiled reference through oracle/reflib.py on small seeded
-   inputs and stores inputs + outputs in ref_vectors.npz.
+   inputs and stores inputs + outputs in ref_vectors.npz (sparse path) and
+   projection_vectors.npz (projection conditioning).
 """
 from __future__ import annotations
 
@@ -32,6 +33,7 @@ FIXTURES = [
     ("slat_flow_numeric_fixture", []),
     ("slat_decoder_numeric_fixture", ["--upsample"]),
     ("flow_numeric_fixture", []),
+    ("projection_numeric_fixture", []),
 ]
 
 
@@ -45,6 +47,11 @@ def run_fixtures() -> None:
         out = subprocess.run([str(exe), *args], check=True, capture_output=True, text=True).stdout
         (HERE / f"{name}.txt").write_text(out)
         print("wrote", name, len(out), "bytes")
+    # tests/cpp/projection_check.cpp built against the reference (oracle/Makefile)
+    exe = REPO / "oracle" / "_ref" / "bin" / "projection_check_ref"
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    (HERE / "projection_check_reference.txt").write_text(out)
+    print("wrote projection_check_reference", len(out), "bytes")
 
 
 def ref_vectors() -> None:
@@ -88,13 +95,75 @@ def ref_vectors() -> None:
     print("wrote ref_vectors.npz", n, "points")
 
 
+def _rot(ax: float, ay: float, az: float) -> np.ndarray:
+    cx, sx, cy, sy, cz, sz = np.cos(ax), np.sin(ax), np.cos(ay), np.sin(ay), np.cos(az), np.sin(az)
+    rx = np.array([[1, 0, 0], [0, cx, -sx], [0, sx, cx]])
+    ry = np.array([[cy, 0, sy], [0, 1, 0], [-sy, 0, cy]])
+    rz = np.array([[cz, -sz, 0], [sz, cz, 0], [0, 0, 1]])
+    return rz @ ry @ rx
+
+
+def _c2w(ax, ay, az, t) -> np.ndarray:
+    m = np.eye(4)
+    m[:3, :3] = _rot(ax, ay, az)
+    m[:3, 3] = t
+    return m.astype(np.float32).reshape(16)
+
+
+def projection_vectors() -> None:
+    """Projection conditioning (src/projection.cpp) on seeded inputs: a
+    37x37 DINO-sized map sampled at a subset of the 64^3 shell from the front
+    camera and from a rotated / translated camera (part of the shell falls
+    outside the image or behind the camera), a dense two-view average, and
+    relative camera matrices."""
+    from oracle import reflib
+    from oracle.oracle import ProjCamera
+    from pixal3d.cpp_b200.workloads import shell_coords
+
+    rng = np.random.default_rng(77)
+    v = {}
+    coords = np.ascontiguousarray(shell_coords()[::8])
+    coords[:, 0] = 0
+    fmap = rng.standard_normal((37, 37, 8)).astype(np.float32)
+    v["coords"], v["fmap"] = coords, fmap
+    front = ProjCamera(0.6, 2.0, 1.0)
+    v["front_feats"], v["front_valid"] = reflib.project_at_coords(fmap, 64, 518, front, coords)
+    # front view from distance 0.3 (inside the shell's extent), turned and
+    # shifted: part of the shell is behind the camera or outside the image
+    m = (_c2w(0.2, 0.0, 0.3, [0.05, 0.0, -0.1]).reshape(4, 4).astype(np.float64) @
+         np.array([[1, 0, 0, 0], [0, 0, -1, -0.3], [0, 1, 0, 0], [0, 0, 0, 1]])).astype(np.float32).reshape(16)
+    v["moved_c2w"] = m
+    moved = ProjCamera(0.9, 2.0, 0.8, m)
+    v["moved_feats"], v["moved_valid"] = reflib.project_at_coords(fmap, 64, 518, moved, coords)
+    a = rng.standard_normal((9, 7, 5)).astype(np.float32)
+    b = rng.standard_normal((9, 7, 5)).astype(np.float32)
+    v["avg_map_a"], v["avg_map_b"] = a, b
+    m2 = _c2w(0.0, 0.4, 0.0, [0.2, -2.2, 0.1])
+    v["avg_c2w"] = m2
+    v["avg_feats"], v["avg_valid"] = reflib.project_average([a, b], 8, 64, [ProjCamera(0.7, 2.2, 1.0),
+                                                                        ProjCamera(0.7, 2.2, 1.0, m2)])
+    c2w = np.stack([_c2w(0.1, 0.2, 0.3, [0.0, -2.0, 0.3]), _c2w(-0.4, 0.9, 0.1, [1.0, -1.5, 0.2]),
+                    _c2w(0.7, -0.3, -1.1, [-0.5, 0.5, -2.0])])
+    d = np.array([2.0, 1.7, 2.4], np.float32)
+    v["rel_c2w"], v["rel_dist"] = c2w, d
+    v["rel_out"] = reflib.relative_matrices(c2w, d)
+    np.savez_compressed(HERE / "projection_vectors.npz", **v)
+    print("wrote projection_vectors.npz", coords.shape[0], "points")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("P3D_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["fixtures", "ref_vectors", "projection"], default=None,
+                    help="regenerate one group only")
     a = ap.parse_args()
     build(a.ref)
-    run_fixtures()
-    ref_vectors()
+    if a.only in (None, "fixtures"):
+        run_fixtures()
+    if a.only in (None, "ref_vectors"):
+        ref_vectors()
+    if a.only in (None, "projection"):
+        projection_vectors()
 
 
 if __name__ == "__main__":
