@@ -458,7 +458,8 @@ int p3d_flow_prepare(p3d_flow *flow, const int32_t *coords, int64_t n, int batch
 /* One forward (slat_flow_forward_f32, src/slat_flow.cpp:161-249):
  * x f32 [n][in], timesteps f32 [batch] (device), ctx bf16 or f32
  * [T][cond] (ctx_dtype: P3D_F32, or the model's operand dtype), proj f32
- * [n][proj_in] or NULL, out f32 [n][out]. */
+ * [n][proj_in] or NULL, out f32 [n][out].  With a concat condition, x is
+ * the caller's [input | concat] rows (concat_sparse_features, :50-75). */
 int p3d_flow_forward(p3d_flow *flow, const float *x, const float *timesteps, const void *ctx_feats,
                      int ctx_dtype, const float *proj, float *out);
 
@@ -481,6 +482,14 @@ typedef struct p3d_sampler_config {
  * the conditional rows, in/out. */
 int p3d_flow_sample(p3d_flow *flow, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
                     const p3d_sampler_config *cfg);
+/* The same with a concat condition (the texture stage's normalized shape
+ * latent, src/slat_flow.cpp:1407-1447 and :171-181): the model input of
+ * every forward, conditional and unconditional, is [state | concat] with
+ * concat f32 [n/2][concat_channels] for the conditional rows; the model's
+ * in_channels = out_channels + concat_channels; x holds the out_channels
+ * state columns.  concat NULL with concat_channels 0 is p3d_flow_sample. */
+int p3d_flow_sample_concat(p3d_flow *flow, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
+                           const float *concat, int concat_channels, const p3d_sampler_config *cfg);
 /* Kernel launches one sampler step issued (forward + update), for reporting. */
 int64_t p3d_flow_launches_per_step(const p3d_flow *flow);
 

@@ -168,6 +168,7 @@ _optional("p3d_flow_destroy", i32, vp)
 _optional("p3d_flow_prepare", i32, vp, vp, i64, i32, i32, i32, i32, C.POINTER(i64))
 _optional("p3d_flow_forward", i32, vp, vp, vp, vp, i32, vp, vp)
 _optional("p3d_flow_sample", i32, vp, vp, vp, i32, vp, C.POINTER(SamplerConfig))
+_optional("p3d_flow_sample_concat", i32, vp, vp, vp, i32, vp, vp, i32, C.POINTER(SamplerConfig))
 _optional("p3d_flow_last_error", C.c_char_p, vp)
 _optional("p3d_flow_launches_per_step", i64, vp)
 

@@ -211,7 +211,7 @@ __global__ void euler_sched_stats_kernel(const float *__restrict__ x, const floa
 __global__ void euler_sched_kernel(float *__restrict__ x, const float *__restrict__ vp, const float *__restrict__ vn,
                                    int64_t n, int C, const int32_t *__restrict__ offsets, int nbatch,
                                    const float *sched, const int *counter, float gr, float sigma_min,
-                                   const double *__restrict__ stats, float *__restrict__ x_model) {
+                                   const double *__restrict__ stats, float *__restrict__ x_model, int ldm) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n * C) return;
     const float *s = sched + 4 * (*counter);
@@ -233,9 +233,11 @@ __global__ void euler_sched_kernel(float *__restrict__ x, const float *__restric
     }
     const float nx = x[i] - dt * pred;
     x[i] = nx;
-    // next forward's input: conditional and unconditional copies
-    x_model[i] = nx;
-    x_model[n * C + i] = nx;
+    // next forward's input: conditional and unconditional copies (rows of
+    // ldm >= C columns; columns [C, ldm) hold the fixed concat condition)
+    const int64_t r = i / C, c = i - r * C;
+    x_model[r * ldm + c] = nx;
+    x_model[(n + r) * ldm + c] = nx;
 }
 
 __global__ void advance_kernel(int *counter) { *counter += 1; }
@@ -869,13 +871,22 @@ extern "C" int p3d_flow_forward(p3d_flow *f, const float *x, const float *timest
 
 extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
                                const p3d_sampler_config *cfg) {
+    return p3d_flow_sample_concat(f, x, ctx_feats, ctx_dtype, proj, nullptr, 0, cfg);
+}
+
+extern "C" int p3d_flow_sample_concat(p3d_flow *f, float *x, const void *ctx_feats, int ctx_dtype, const float *proj,
+                                      const float *concat, int concat_channels, const p3d_sampler_config *cfg) {
     if (!f || !cfg) return P3D_ERR_INVALID;
     p3d_ctx *ctx = f->ctx;
     DeviceGuard dg(ctx->device);
     P3D_REQUIRE(ctx, f->prepared, "p3d_flow_sample: call p3d_flow_prepare first");
     P3D_REQUIRE(ctx, x && ctx_feats, "p3d_flow_sample: null pointer");
     P3D_REQUIRE(ctx, f->batch % 2 == 0, "p3d_flow_sample: batch must be 2 x images (conditional, unconditional)");
-    P3D_REQUIRE(ctx, f->hp.in_channels == f->hp.out_channels, "p3d_flow_sample: in/out channels differ");
+    P3D_REQUIRE(ctx, concat_channels >= 0 && (concat_channels == 0) == (concat == nullptr),
+                "SLat flow concat condition shape or coordinates mismatch");
+    P3D_REQUIRE(ctx, f->hp.in_channels == f->hp.out_channels + concat_channels,
+                concat_channels ? "SLat stage concat condition does not match model input metadata"
+                                : "p3d_flow_sample: in/out channels differ");
     P3D_REQUIRE(ctx, !f->hp.proj_mode || proj, "SLat flow projection context shape mismatch");
     P3D_REQUIRE(ctx, cfg->steps > 0 && cfg->steps < 4096 && cfg->sigma_min >= 0.0f && cfg->sigma_min < 1.0f &&
                          cfg->rescale_t > 0.0f && cfg->guidance_rescale >= 0.0f &&
@@ -884,7 +895,8 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
     const int I = f->batch / 2;
     const int64_t half = f->h_fine_off[I];
     P3D_REQUIRE(ctx, 2 * half == f->n, "p3d_flow_sample: unconditional half must mirror the conditional half");
-    const int ch = f->hp.in_channels;
+    const int ch = f->hp.out_channels;   // sampler state columns
+    const int ldm = f->hp.in_channels;   // model input: [state | concat]
     // t schedule (src/flow_sampler.cpp:268-286), computed in f32 like the reference
     std::vector<float> sched(4 * (cfg->steps + 1), 0.0f);
     const float steps = static_cast<float>(cfg->steps);
@@ -924,11 +936,18 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
                                           f->stream));
             P3D_CUDA(ctx, cudaMemsetAsync(f->proj_model + hp_rows, 0, sizeof(float) * hp_rows, f->stream));
         }
-        // sampler state and model input [x; x]
+        // sampler state and model input [x | concat; x | concat] (the concat
+        // condition is the same for both branches, src/slat_flow.cpp:1427-1441)
         P3D_CUDA(ctx, cudaMemcpyAsync(f->x_state, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
-        P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice, f->stream));
-        P3D_CUDA(ctx, cudaMemcpyAsync(f->x_model + half * ch, x, sizeof(float) * half * ch, cudaMemcpyDeviceToDevice,
-                                      f->stream));
+        for (int b = 0; b < 2; ++b) {
+            float *dst = f->x_model + b * half * ldm;
+            P3D_CUDA(ctx, cudaMemcpy2DAsync(dst, sizeof(float) * ldm, x, sizeof(float) * ch, sizeof(float) * ch, half,
+                                            cudaMemcpyDeviceToDevice, f->stream));
+            if (concat_channels)
+                P3D_CUDA(ctx, cudaMemcpy2DAsync(dst + ch, sizeof(float) * ldm, concat, sizeof(float) * concat_channels,
+                                                sizeof(float) * concat_channels, half, cudaMemcpyDeviceToDevice,
+                                                f->stream));
+        }
         const bool rescale = cfg->guidance_rescale > 0.0f;
         const float gr = cfg->guidance_rescale, sigma = cfg->sigma_min;
         auto one_step = [&]() -> int {
@@ -942,7 +961,7 @@ extern "C" int p3d_flow_sample(p3d_flow *f, float *x, const void *ctx_feats, int
             }
             euler_sched_kernel<<<blocks_for(half * ch, 256), 256, 0, f->stream>>>(
                 f->x_state, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, gr, sigma,
-                rescale ? f->stats : nullptr, f->x_model);
+                rescale ? f->stats : nullptr, f->x_model, ldm);
             P3D_TRY(check_launch(ctx, "euler_sched"));
             advance_kernel<<<1, 1, 0, f->stream>>>(f->counter);
             return check_launch(ctx, "advance");

@@ -134,15 +134,23 @@ class FlowModel:
 
     def sample(self, x: torch.Tensor, ctx_feats: torch.Tensor, steps: int, guidance_strength: float = 1.0,
                guidance_rescale: float = 0.0, sigma_min: float = 1e-5, rescale_t: float = 1.0,
-               guidance_interval=(0.0, 1.0), proj: torch.Tensor | None = None, use_graph: bool = True) -> torch.Tensor:
-        """In-place Euler/CFG integration of x (f32 [n/2, ch], the conditional rows)."""
+               guidance_interval=(0.0, 1.0), proj: torch.Tensor | None = None, use_graph: bool = True,
+               concat: torch.Tensor | None = None) -> torch.Tensor:
+        """In-place Euler/CFG integration of x (f32 [n/2, out_channels], the
+        conditional rows).  concat (f32 [n/2, in - out]): the fixed concat
+        condition appended to the state in every forward."""
         c = _ctx(self.device)
         cfg = L.SamplerConfig(steps=steps, sigma_min=sigma_min, rescale_t=rescale_t,
                               guidance_strength=guidance_strength, guidance_rescale=guidance_rescale,
                               guidance_interval_min=guidance_interval[0], guidance_interval_max=guidance_interval[1],
                               use_graph=int(use_graph))
         dt = {torch.bfloat16: L.P3D_BF16, torch.float16: L.P3D_F16}.get(ctx_feats.dtype, L.P3D_F32)
-        c.check(L.OPTIONAL["p3d_flow_sample"](self.h, _ptr(x), _ptr(ctx_feats), dt, _ptr(proj), C.byref(cfg)))
+        if concat is None:
+            c.check(L.OPTIONAL["p3d_flow_sample"](self.h, _ptr(x), _ptr(ctx_feats), dt, _ptr(proj), C.byref(cfg)))
+        else:
+            concat = concat.contiguous()
+            c.check(L.OPTIONAL["p3d_flow_sample_concat"](self.h, _ptr(x), _ptr(ctx_feats), dt, _ptr(proj),
+                                                         _ptr(concat), concat.shape[1], C.byref(cfg)))
         return x
 
     @property

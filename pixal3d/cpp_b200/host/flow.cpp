@@ -1,8 +1,10 @@
 // flow_euler_sample_f32, slat_flow_forward_f32 and SLatFlowModel on the B200
 // kernels (src/flow_sampler.cpp:245-343, src/slat_flow.cpp:161-249,
 // :1301-1447).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <limits>
 
 #include <map>
 #include <memory>
@@ -223,11 +225,41 @@ bool prepare(p3d_ctx *ctx, p3d_flow *flow, const SparseTensorF32 &input, int cop
               error);
 }
 
+// concat_sparse_features (src/slat_flow.cpp:50-75): rows [left | right]
+// with the same coordinates; a host row copy of the API's host tensors.
+bool concat_features(const SparseTensorF32 &left, const SparseTensorF32 &right, SparseTensorF32 &out,
+                     std::string *error) {
+    if (left.batch_size != right.batch_size || left.spatial_x != right.spatial_x ||
+        left.spatial_y != right.spatial_y || left.spatial_z != right.spatial_z || left.coords != right.coords ||
+        right.channels <= 0 || left.channels > std::numeric_limits<int>::max() - right.channels ||
+        right.feats.size() != right.points() * static_cast<std::size_t>(right.channels))
+        return fail(error, "SLat flow concat condition shape or coordinates mismatch");
+    out = left;
+    out.channels = left.channels + right.channels;
+    const std::size_t n = left.points(), lc = static_cast<std::size_t>(left.channels),
+                      rc = static_cast<std::size_t>(right.channels);
+    out.feats.resize(n * (lc + rc));
+    for (std::size_t p = 0; p < n; ++p) {
+        std::copy(left.feats.begin() + static_cast<std::ptrdiff_t>(p * lc),
+                  left.feats.begin() + static_cast<std::ptrdiff_t>((p + 1) * lc),
+                  out.feats.begin() + static_cast<std::ptrdiff_t>(p * (lc + rc)));
+        std::copy(right.feats.begin() + static_cast<std::ptrdiff_t>(p * rc),
+                  right.feats.begin() + static_cast<std::ptrdiff_t>((p + 1) * rc),
+                  out.feats.begin() + static_cast<std::ptrdiff_t>(p * (lc + rc) + lc));
+    }
+    return true;
+}
+
 bool check_forward_inputs(const SparseTensorF32 &input, std::size_t timestep_count,
                           const VarLenTensorF32 &global_context, const SparseTensorF32 *projection_context,
                           const SLatFlowHParams &h, const SparseTensorF32 *concat_condition, std::string *error) {
-    if (concat_condition) return fail(error, "SLat flow concat conditioning is not supported by the B200 path");
-    if (input.channels != h.in_channels || global_context.channels != h.cond_channels ||
+    if (concat_condition &&
+        (concat_condition->batch_size != input.batch_size || concat_condition->spatial_x != input.spatial_x ||
+         concat_condition->spatial_y != input.spatial_y || concat_condition->spatial_z != input.spatial_z ||
+         concat_condition->coords != input.coords || concat_condition->channels <= 0))
+        return fail(error, "SLat flow concat condition shape or coordinates mismatch");
+    const int in_channels = input.channels + (concat_condition ? concat_condition->channels : 0);
+    if (in_channels != h.in_channels || global_context.channels != h.cond_channels ||
         global_context.batch_size != input.batch_size || timestep_count != static_cast<std::size_t>(input.batch_size))
         return fail(error, "SLat flow input, timestep or context shape mismatch");
     if (h.image_attn_mode == "proj" &&
@@ -420,12 +452,16 @@ bool slat_flow_forward_f32(const SparseTensorF32 &input, const float *timesteps,
     if (!check_forward_inputs(input, timestep_count, global_context, projection_context, hparams, concat_condition,
                               error))
         return false;
+    SparseTensorF32 joined;
+    if (concat_condition && !concat_features(input, *concat_condition, joined, error)) return false;
+    const SparseTensorF32 &model_input = concat_condition ? joined : input;
     if (!device_flow_supported(hparams))
-        return composed_forward(ctx, input, timesteps, global_context, projection_context, hparams, weights, output,
-                                error);
+        return composed_forward(ctx, model_input, timesteps, global_context, projection_context, hparams, weights,
+                                output, error);
     p3d_flow *flow = nullptr;
     if (!create_flow(ctx, hparams, weights, &flow, error)) return false;
-    const bool r = run_forward(ctx, flow, input, timesteps, global_context, projection_context, hparams, output, error);
+    const bool r =
+        run_forward(ctx, flow, model_input, timesteps, global_context, projection_context, hparams, output, error);
     p3d_flow_destroy(flow);
     return r;
 }
@@ -686,11 +722,14 @@ bool SLatFlowModel::forward(const SparseTensorF32 &input, const float *timesteps
     if (!check_forward_inputs(input, timestep_count, global_context, projection_context, impl_->hp, concat_condition,
                               error))
         return false;
+    SparseTensorF32 joined;
+    if (concat_condition && !concat_features(input, *concat_condition, joined, error)) return false;
+    const SparseTensorF32 &model_input = concat_condition ? joined : input;
     if (!impl_->flow)
-        return composed_forward(ctx, input, timesteps, global_context, projection_context, impl_->hp, impl_->host.w,
-                                output, error);
-    return run_forward(ctx, impl_->flow, input, timesteps, global_context, projection_context, impl_->hp, output,
-                       error);
+        return composed_forward(ctx, model_input, timesteps, global_context, projection_context, impl_->hp,
+                                impl_->host.w, output, error);
+    return run_forward(ctx, impl_->flow, model_input, timesteps, global_context, projection_context, impl_->hp,
+                       output, error);
 }
 
 bool SLatFlowModel::sample(const SparseTensorF32 &noise, const FlowEulerSamplerConfig &sampler_config,
@@ -703,7 +742,8 @@ bool SLatFlowModel::sample(const SparseTensorF32 &noise, const FlowEulerSamplerC
     const SLatFlowHParams &h = impl_->hp;
     if (!check_forward_inputs(noise, noise.batch_size, global_context, projection_context, h, concat_condition, error))
         return false;
-    if (sampler_config.record_trajectory || h.in_channels != h.out_channels || !impl_->flow) {
+    const int concat_channels = concat_condition ? concat_condition->channels : 0;
+    if (sampler_config.record_trajectory || h.in_channels != h.out_channels + concat_channels || !impl_->flow) {
         // host-driven loop (trajectory recorded per step), forward on the device
         VarLenTensorF32 zeros = global_context;
         std::fill(zeros.feats.begin(), zeros.feats.end(), 0.0f);
@@ -717,20 +757,20 @@ bool SLatFlowModel::sample(const SparseTensorF32 &noise, const FlowEulerSamplerC
                                 std::string *e) {
             std::fill(ts.begin(), ts.end(), t);
             return forward(state, ts.data(), ts.size(), cond ? global_context : zeros,
-                           projection_context ? (cond ? projection_context : &zproj) : nullptr, v, e);
+                           projection_context ? (cond ? projection_context : &zproj) : nullptr, v, e,
+                           concat_condition);
         };
         return flow_euler_sample_f32(noise, sampler_config, fn, output, error);
     }
     output = FlowEulerSampleF32{};
-    Buffer x, g, coords, proj;
+    Buffer x, g, coords, proj, cat;
     if (!b200::validate_sparse(ctx, noise, nullptr, &x, error) || !valid_config(sampler_config, error)) return false;
+    if (concat_condition && !b200::validate_sparse(ctx, *concat_condition, nullptr, &cat, error)) return false;
     // condition items: [0, I) conditional, [I, 2I) cleared to zeros by the sampler
     const int I = noise.batch_size;
     std::vector<int64_t> coff(2 * static_cast<std::size_t>(I) + 1, 0);
-    for (int b = 0; b < I; ++b) {
-        coff[b + 1] = static_cast<int64_t>(global_context.offsets[b + 1]);
-        coff[I + b + 1] = coff[I] + static_cast<int64_t>(global_context.offsets[b + 1]);
-    }
+    for (int b = 0; b < I; ++b) coff[b + 1] = static_cast<int64_t>(global_context.offsets[b + 1]);
+    for (int b = 0; b < I; ++b) coff[I + b + 1] = coff[I] + static_cast<int64_t>(global_context.offsets[b + 1]);
     std::vector<float> cond2(global_context.feats);
     cond2.resize(global_context.feats.size() * 2, 0.0f);
     if (!b200::upload(ctx, g, cond2.data(), cond2.size() * 4, error)) return false;
@@ -746,8 +786,9 @@ bool SLatFlowModel::sample(const SparseTensorF32 &noise, const FlowEulerSamplerC
     c.guidance_interval_max = sampler_config.guidance_interval_max;
     c.use_graph = 1;
     if (!ok(ctx,
-            p3d_flow_sample(impl_->flow, x.as<float>(), g.get(), P3D_F32,
-                            projection_context ? proj.as<float>() : nullptr, &c),
+            p3d_flow_sample_concat(impl_->flow, x.as<float>(), g.get(), P3D_F32,
+                                   projection_context ? proj.as<float>() : nullptr,
+                                   concat_condition ? cat.as<float>() : nullptr, concat_channels, &c),
             error))
         return false;
     output.samples = noise;

@@ -4,7 +4,7 @@
 // from a file, results written to a file for the Python test to compare
 // with the reference's own outputs.
 //
-//   host_api_check <inputs.bin> <outputs.bin>
+//   host_api_check <inputs.bin> <outputs.bin> [<flow pack.gguf> [<texture pack.gguf>]]
 //
 // File format: records of {u32 name length, name, u8 type (0 f32, 1 i32,
 // 2 i64), u64 count, count values}.
@@ -360,6 +360,44 @@ void flow_gguf(const std::string &path) {
     else put_error("gguf_flow_forward", e);
 }
 
+// The calls of the reference's tests/slat_flow_concat_fixture.cpp: a
+// texture_flow_1024 pack, forward and a 3-step sample with a concat
+// condition and projection context.
+void flow_concat_gguf(const std::string &path) {
+    std::string e;
+    SLatFlowModel model;
+    if (!model.load(path, "texture_flow_1024", true, &e)) {
+        put_error("tx_load", e);
+        return;
+    }
+    const SLatFlowHParams &h = model.hparams();
+    const int base = 12, cc = h.in_channels - base;
+    const SparseTensorF32 x = sparse(I("tx.coords"), F("tx.x"), base, 2, h.resolution, h.resolution, h.resolution);
+    const SparseTensorF32 cat = sparse(I("tx.coords"), F("tx.concat"), cc, 2, h.resolution, h.resolution, h.resolution);
+    const SparseTensorF32 proj =
+        sparse(I("tx.coords"), F("tx.proj"), h.proj_in_channels, 2, h.resolution, h.resolution, h.resolution);
+    const VarLenTensorF32 ctx = varlen(F("tx.ctx"), h.cond_channels, {0, 3, 5});
+    const std::vector<float> ts = {0.17f, -0.23f};
+    SparseTensorF32 o;
+    if (model.forward(x, ts.data(), ts.size(), ctx, &proj, o, &e, &cat)) put("tx_concat_forward", o.feats);
+    else put_error("tx_concat_forward", e);
+    FlowEulerSamplerConfig sc;
+    sc.steps = 3;
+    sc.sigma_min = 0.031f;
+    sc.rescale_t = 2.7f;
+    sc.guidance_strength = 1.0f;
+    sc.record_trajectory = false;
+    FlowEulerSampleF32 r;
+    if (model.sample(x, sc, ctx, &proj, r, &e, &cat)) put("tx_concat_sample", r.samples.feats);
+    else put_error("tx_concat_sample", e);
+    // a concat condition on other coordinates is refused with the reference's message
+    SparseTensorF32 moved = cat;
+    moved.coords[1] += 1;
+    const bool refused = !model.forward(x, ts.data(), ts.size(), ctx, &proj, o, &e, &moved) &&
+                         e == "SLat flow concat condition shape or coordinates mismatch";
+    put("tx_concat_mismatch_refused", std::vector<float>{refused ? 1.f : 0.f});
+}
+
 SLatDecoderBlockWeightsF32 dec_block(int i, bool c2s, int C, int O, int mlp) {
     SLatDecoderBlockWeightsF32 b;
     const std::string p = "dec.b" + std::to_string(i) + ".";
@@ -477,8 +515,8 @@ void sampler() {
 }  // namespace
 
 int main(int argc, char **argv) {
-    if ((argc != 3 && argc != 4) || !read_inputs(argv[1])) {
-        std::cerr << "usage: host_api_check <inputs.bin> <outputs.bin> [<flow pack.gguf>]\n";
+    if (argc < 3 || argc > 5 || !read_inputs(argv[1])) {
+        std::cerr << "usage: host_api_check <inputs.bin> <outputs.bin> [<flow pack.gguf> [<texture pack.gguf>]]\n";
         return 2;
     }
     out_file.open(argv[2], std::ios::binary);
@@ -489,7 +527,8 @@ int main(int argc, char **argv) {
         flow_device();
         decoder();
         sampler();
-        if (argc == 4) flow_gguf(argv[3]);
+        if (argc >= 4) flow_gguf(argv[3]);
+        if (argc >= 5) flow_concat_gguf(argv[4]);
     } catch (const std::exception &ex) {
         std::cerr << "exception: " << ex.what() << "\n";
         return 3;

@@ -138,4 +138,5 @@ def flow_metadata(component: str, hp, resolution: int = 16) -> dict:
             k + "num_blocks": hp.num_blocks, k + "num_heads": hp.num_heads, k + "mlp_ratio": float(hp.mlp_ratio),
             k + "pe_mode": "rope", k + "share_mod": True, k + "qk_rms_norm": bool(hp.qk_rms_norm),
             k + "qk_rms_norm_cross": bool(hp.qk_rms_norm_cross), k + "rope_freq_min": float(hp.rope_freq_min),
-            k + "rope_freq_base": float(hp.rope_freq_base), k + "image_attn_mode": "cross"}
+            k + "rope_freq_base": float(hp.rope_freq_base), k + "image_attn_mode": hp.image_attn_mode,
+            k + "proj_in_channels": int(hp.proj_in_channels)}

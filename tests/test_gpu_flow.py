@@ -121,6 +121,43 @@ def test_flow_sample_cfg(use_graph, g, gr):
     model.close()
 
 
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_flow_sample_concat_and_projection(use_graph):
+    """The texture stage's layout (SLatFlowModel::sample with a concat
+    condition and projection mode, src/slat_flow.cpp:1407-1447): each forward
+    sees [state | concat]; the unconditional branch keeps the concat rows and
+    zeroes the global and projected conditions."""
+    c0 = shell_coords(16, 5.5, 1.0)
+    coords = batched(c0, 2)
+    m = c0.shape[0]
+    hp = O.FlowHParams(in_channels=13, out_channels=8, model_channels=128, cond_channels=64, num_blocks=2,
+                       num_heads=2, proj_in_channels=7, image_attn_mode="proj")
+    w, model = make(hp, seed=7)
+    rng = np.random.default_rng(8)
+    noise = rng.standard_normal((m, 8)).astype(np.float32)
+    concat = rng.standard_normal((m, 5)).astype(np.float32)
+    proj = rng.standard_normal((m, 7)).astype(np.float32)
+    ctx = rng.standard_normal((33, 64)).astype(np.float32)
+    sc = O.SamplerConfig(steps=3, sigma_min=0.031, rescale_t=2.7, guidance_strength=3.0, guidance_rescale=0.0,
+                         guidance_interval_min=0.0, guidance_interval_max=1.0)
+    one = np.array([0, 33], np.int64)
+
+    def ref_model(state, t, cond):
+        xin = np.concatenate([state, concat], axis=1).astype(np.float32)
+        return O.slat_flow_forward(c0, xin, np.array([t], np.float32), one, ctx if cond else np.zeros_like(ctx),
+                                   proj if cond else np.zeros_like(proj), hp, w)
+
+    exp = O.flow_euler_sample(noise, sc, ref_model, c0[:, 0].astype(np.int64), 1)
+    model.prepare(torch.from_numpy(coords).cuda(), 2, (16, 16, 16), np.array([0, 33, 66]))
+    xt = torch.from_numpy(noise.copy()).cuda()
+    ctx2 = torch.from_numpy(np.concatenate([ctx, ctx])).cuda()
+    model.sample(xt, ctx2, steps=3, guidance_strength=3.0, sigma_min=0.031, rescale_t=2.7, use_graph=use_graph,
+                 proj=torch.from_numpy(proj).cuda(), concat=torch.from_numpy(concat).cuda())
+    torch.cuda.synchronize()
+    check(xt.cpu().numpy(), exp, f"sample concat+proj graph={use_graph}")
+    model.close()
+
+
 def test_flow_forward_bf16_operands():
     """The same forward with bf16 operands: reported, with the looser bound
     that bf16 rounding allows (the default operand type is f16)."""

@@ -98,6 +98,12 @@ def _inputs():
     a["dec.h0"] = O.linear(dx, wd["from_latent_w"], wd["from_latent_b"])
     a["fs.coords"] = np.array([[0, 0, 0, 0], [0, 0, 1, 0], [0, 2, 1, 1], [1, 0, 0, 1], [1, 1, 2, 0]], np.int32)
     a["fs.noise"] = FX.seq(15, -0.73, 0.091)
+    # texture stage (the reference's tests/slat_flow_concat_fixture.cpp inputs)
+    a["tx.coords"] = FX.TEN_COORDS.astype(np.int32)
+    a["tx.x"] = FX.seq(120, -0.27, 0.013)
+    a["tx.concat"] = FX.seq(40, 0.07, -0.011)
+    a["tx.proj"] = FX.seq(70, 0.19, -0.017)
+    a["tx.ctx"] = FX.seq(320, -0.11, 0.021)
     return a
 
 
@@ -116,6 +122,28 @@ def _pack_weights():
     return w, G.stored_flow_weights(w, G.GGML_F16)
 
 
+def _texture_hp():
+    """A texture-stage model: 12 noise channels + 4 concat channels in,
+    12 out, projection conditioning with 7 channels."""
+    from oracle import oracle as O
+    return O.FlowHParams(in_channels=16, out_channels=12, model_channels=128, cond_channels=64, num_blocks=2,
+                         num_heads=2, proj_in_channels=7, image_attn_mode="proj")
+
+
+def _texture_weights():
+    from tests._models import random_flow_weights
+    from tests import gguf_pack as G
+    w = random_flow_weights(np.random.default_rng(11), _texture_hp())
+    return w, G.stored_flow_weights(w, G.GGML_F16)
+
+
+def _write_texture_pack(path):
+    from tests import gguf_pack as G
+    w, _ = _texture_weights()
+    G.write_pack(path, G.flow_metadata("texture_flow_1024", _texture_hp(), resolution=16),
+                 G.flow_tensors("tx1024", w, G.GGML_F16))
+
+
 def _write_flow_pack(path):
     from tests import gguf_pack as G
     w, _ = _pack_weights()
@@ -132,8 +160,9 @@ def harness(tmp_path_factory):
     subprocess.run(cmd, check=True, capture_output=True, text=True)
     _write(d / "in.bin", _inputs())
     _write_flow_pack(d / "flow.gguf")
-    r = subprocess.run([str(exe), str(d / "in.bin"), str(d / "out.bin"), str(d / "flow.gguf")], capture_output=True,
-                       text=True, timeout=600)
+    _write_texture_pack(d / "texture.gguf")
+    r = subprocess.run([str(exe), str(d / "in.bin"), str(d / "out.bin"), str(d / "flow.gguf"), str(d / "texture.gguf")],
+                       capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     return _read(d / "out.bin")
 
@@ -243,3 +272,34 @@ def test_flow_gguf_pack_through_host_api(harness):
     one = np.array([0, ctx.shape[0]], np.int64)
     exp = O.slat_flow_forward(c, x, a["bf.timestep"], one, ctx, None, hp, st)
     _close(harness["gguf_flow_forward"], exp.ravel(), "GGUF-loaded forward")
+
+
+def test_texture_stage_concat_and_projection_through_host_api(harness):
+    """The calls of the reference's tests/slat_flow_concat_fixture.cpp on a
+    texture_flow_1024 pack (concat condition + projection mode): forward with
+    [input | concat], then a 3-step sampler run, against the oracle on the
+    pack's stored values."""
+    from oracle import oracle as O
+    hp = _texture_hp()
+    _, st = _texture_weights()
+    a = _inputs()
+    c = a["tx.coords"]
+    x = a["tx.x"].reshape(10, 12)
+    cat = a["tx.concat"].reshape(10, 4)
+    proj = a["tx.proj"].reshape(10, 7)
+    ctx = a["tx.ctx"].reshape(5, 64)
+    offs = np.array([0, 3, 5], np.int64)
+    ts = np.array([0.17, -0.23], np.float32)
+    exp = O.slat_flow_forward(c, np.concatenate([x, cat], 1), ts, offs, ctx, proj, hp, st)
+    _close(harness["tx_concat_forward"], exp.ravel(), "texture forward with concat")
+    sc = O.SamplerConfig(steps=3, sigma_min=0.031, rescale_t=2.7, guidance_strength=1.0, guidance_rescale=0.0,
+                         guidance_interval_min=0.0, guidance_interval_max=1.0)
+
+    def ref_model(state, t, cond):
+        return O.slat_flow_forward(c, np.concatenate([state, cat], 1).astype(np.float32), np.array([t, t], np.float32),
+                                   offs, ctx if cond else np.zeros_like(ctx), proj if cond else np.zeros_like(proj),
+                                   hp, st)
+
+    exp = O.flow_euler_sample(x, sc, ref_model, c[:, 0].astype(np.int64), 2)
+    _close(harness["tx_concat_sample"], exp.ravel(), "texture sample with concat")
+    assert harness["tx_concat_mismatch_refused"][0] == 1
