@@ -274,6 +274,31 @@ int p3d_window_attention(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k
                          int max_window_rows, int64_t n, int heads, int head_dim, float scale, int dtype,
                          void *scratch, size_t scratch_bytes, void *out, int64_t ldo);
 
+/* ---------------------------------------------------- SLat cascade glue */
+
+/* Latent (de)normalization of a SLat stage (normalize_slat_f32,
+ * src/pipeline.cpp:333-357; the denormalization of run_slat_stage_f32,
+ * :418-431): out[i][c] = (x[i][c] - mean[c]) / std[c], or with denormalize
+ * x[i][c] * std[c] + mean[c], f32 with the reference's rounding (bit-exact).
+ * x, out f32 [n][channels] (may alias); mean, std f32 [channels] on the
+ * device.  A non-finite result latches P3D_ERR_NONFINITE. */
+int p3d_slat_normalize(p3d_ctx *ctx, const float *x, int64_t n, int channels, const float *mean, const float *std,
+                       int denormalize, float *out);
+
+/* Shape-decoder coordinates to the 1024 cascade grid
+ * (quantize_slat_coords_f32, src/pipeline.cpp:433-466): each axis v of
+ * coords [n][4] (batch b in [0, batch)) maps to llround((v + 0.5) /
+ * low_resolution * 63) in double; rows are made unique and written in
+ * lexicographic (b, x, y, z) order to out (capacity n rows); *count (device
+ * int64) receives the number of rows.  resolution must be 1024 ("SLat
+ * cascade resolution must be 1024"); a coordinate mapping outside [0, 64)
+ * latches P3D_ERR_INVALID.  ws: p3d_quantize_slat_coords_workspace(batch)
+ * bytes; all pointers 16-byte aligned.  The max_num_tokens guard of the
+ * reference is the caller's check of *count. */
+size_t p3d_quantize_slat_coords_workspace(int batch);
+int p3d_quantize_slat_coords(p3d_ctx *ctx, const int32_t *coords, int64_t n, int batch, int low_resolution,
+                             int resolution, int32_t *out, int64_t *count, void *ws, size_t ws_bytes);
+
 /* ------------------------------------------------- projection conditioning */
 
 /* One camera view of an image feature map (ProjectionView plus the view's

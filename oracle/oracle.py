@@ -1004,3 +1004,60 @@ def relative_calc_matrices(c2w, distances):
         raise ValueError("main-view camera transform matrix is singular")
     f = front_matrix(d0)
     return [matmul4(f, matmul4(inv, m)) for m in c2w]
+
+
+# --------------------------------------------------------------------------
+# SLat cascade glue (src/pipeline.cpp)
+# --------------------------------------------------------------------------
+
+def check_normalization(mean, std, channels):
+    """valid_normalization (src/pipeline.cpp:268-285)."""
+    mean, std = np.asarray(mean, F32), np.asarray(std, F32)
+    if channels <= 0 or mean.shape != (channels,) or std.shape != (channels,):
+        raise ValueError("SLat normalization channel count does not match model output")
+    if not (np.isfinite(mean).all() and np.isfinite(std).all()) or (std == 0).any():
+        raise ValueError("SLat normalization contains a non-finite or zero standard deviation")
+
+
+def normalize_slat(x, mean, std):
+    """normalize_slat_f32 (src/pipeline.cpp:333-358): (x - mean) / std in f32."""
+    x = np.asarray(x, F32)
+    check_normalization(mean, std, x.shape[1])
+    with np.errstate(all="ignore"):
+        y = ((x - np.asarray(mean, F32)).astype(F32) / np.asarray(std, F32)).astype(F32)
+    if not np.isfinite(y).all():
+        raise ValueError("SLat normalization produced a non-finite value")
+    return y
+
+
+def denormalize_slat(x, mean, std):
+    """The latent denormalization of run_slat_stage_f32
+    (src/pipeline.cpp:418-431): x * std + mean in f32 (two roundings)."""
+    x = np.asarray(x, F32)
+    check_normalization(mean, std, x.shape[1])
+    with np.errstate(all="ignore"):
+        y = ((x * np.asarray(std, F32)).astype(F32) + np.asarray(mean, F32)).astype(F32)
+    if not np.isfinite(y).all():
+        raise ValueError("SLat stage denormalization produced a non-finite value")
+    return y
+
+
+def quantize_slat_coords(coords, low_resolution, requested_resolution=1024, max_num_tokens=0):
+    """quantize_slat_coords_f32 + quantize_at_resolution (src/pipeline.cpp:
+    296-329, 437-468): each axis v -> llround((v + 0.5) / low * 63) in double
+    (halves away from zero) on the 64^3 grid of resolution 1024, rows unique
+    in lexicographic (b, x, y, z) order."""
+    if requested_resolution != 1024:
+        raise ValueError("SLat cascade resolution must be 1024")
+    if low_resolution <= 0:
+        raise ValueError("SLat cascade low resolution must be positive")
+    c = np.asarray(coords, np.int64).reshape(-1, 4)
+    grid = 1024 // 16
+    mapped = (c[:, 1:].astype(np.float64) + 0.5) / float(low_resolution) * float(grid - 1)
+    q = np.where(mapped >= 0, np.floor(mapped + 0.5), np.ceil(mapped - 0.5)).astype(np.int64)
+    if ((q < 0) | (q >= grid)).any():
+        raise ValueError("SLat decoder coordinate is outside cascade quantization range")
+    rows = np.unique(np.concatenate([c[:, :1], q], 1), axis=0)
+    if max_num_tokens and rows.shape[0] > max_num_tokens:
+        raise ValueError("quantized SLat coordinate count exceeds max_num_tokens at resolution 1024")
+    return rows.astype(np.int32)

@@ -31,6 +31,21 @@ bool p3dref_reference_neighbor_map(const SparseTensorF32 & input,
 std::uint64_t p3dref_coords_fingerprint(const std::vector<std::int32_t> & coords);
 }  // namespace pixal3d
 
+namespace pixal3d {
+// src/pipeline.cpp glue built from the extracted translation unit (the
+// reference's include/pixal3d/pipeline.h pulls in ggml through ss_flow.h,
+// so its two declarations used here are repeated).
+struct SLatNormalizationF32 {
+    std::vector<float> mean;
+    std::vector<float> std;
+};
+bool normalize_slat_f32(const SparseTensorF32 & input, const SLatNormalizationF32 & normalization,
+                        SparseTensorF32 & output, std::string * error);
+bool quantize_slat_coords_f32(const SparseTensorF32 & upsampled_coords, int low_resolution,
+                              int requested_resolution, std::size_t max_num_tokens,
+                              std::vector<std::int32_t> & coords, int & actual_resolution, std::string * error);
+}  // namespace pixal3d
+
 using namespace pixal3d;
 
 namespace {
@@ -611,6 +626,37 @@ int p3dref_relative_matrices(const float * c2w, const float * distances, int n, 
     if (!compute_relative_calc_matrices(m, d, out, &e)) return fail(e, err, errlen);
     for (int i = 0; i < n; ++i)
         for (int j = 0; j < 16; ++j) relative[16 * i + j] = out[static_cast<size_t>(i)][static_cast<size_t>(j)];
+    return 0;
+}
+
+// normalize_slat_f32 (src/pipeline.cpp:333-358): out [n][c].
+int p3dref_normalize_slat(const int32_t * coords, int64_t n, const float * feats, int c, int batch, int sx, int sy,
+                          int sz, const float * mean, const float * stdv, float * out, char * err, int errlen) {
+    SparseTensorF32 in = make_sparse(coords, n, feats, c, batch, sx, sy, sz);
+    SLatNormalizationF32 norm;
+    norm.mean.assign(mean, mean + c);
+    norm.std.assign(stdv, stdv + c);
+    SparseTensorF32 o;
+    std::string e;
+    if (!normalize_slat_f32(in, norm, o, &e)) return fail(e, err, errlen);
+    copy_out(o.feats, out);
+    return 0;
+}
+
+// quantize_slat_coords_f32 (src/pipeline.cpp:437-468): out [m][4], *m.
+int p3dref_quantize_slat_coords(const int32_t * coords, int64_t n, int batch, int sx, int low_resolution,
+                                int requested_resolution, int64_t max_tokens, int32_t * out, int64_t * m, char * err,
+                                int errlen) {
+    std::vector<float> zeros(static_cast<size_t>(n), 0.0f);
+    SparseTensorF32 in = make_sparse(coords, n, zeros.data(), 1, batch, sx, sx, sx);
+    std::vector<std::int32_t> q;
+    int res = 0;
+    std::string e;
+    if (!quantize_slat_coords_f32(in, low_resolution, requested_resolution, static_cast<std::size_t>(max_tokens), q,
+                                  res, &e))
+        return fail(e, err, errlen);
+    std::memcpy(out, q.data(), q.size() * 4);
+    *m = static_cast<int64_t>(q.size() / 4);
     return 0;
 }
 

@@ -392,3 +392,30 @@ def relative_matrices(c2w, distances):
     err = _err()
     _check(lib().p3dref_relative_matrices(m.ctypes, d.ctypes, m.shape[0], out.ctypes, err, 512), err)
     return out
+
+
+def normalize_slat(coords, x, mean, std, batch=None, shape=None):
+    """normalize_slat_f32 (src/pipeline.cpp:333-358)."""
+    coords, x = _c(coords, np.int32), _c(x, np.float32)
+    batch, shape = _shape(coords, batch, shape)
+    out = np.empty_like(x)
+    err = _err()
+    _check(lib().p3dref_normalize_slat(coords.ctypes, C.c_int64(x.shape[0]), x.ctypes, x.shape[1], batch, *shape,
+                                       _c(mean, np.float32).ctypes, _c(std, np.float32).ctypes, out.ctypes, err, 512),
+           err)
+    return out
+
+
+def quantize_slat_coords(coords, low_resolution, requested_resolution=1024, max_tokens=0, batch=None, spatial=None):
+    """quantize_slat_coords_f32 (src/pipeline.cpp:437-468): int32 [m, 4]."""
+    coords = _c(coords, np.int32)
+    n = coords.shape[0]
+    batch = int(coords[:, 0].max()) + 1 if batch is None else batch
+    spatial = low_resolution if spatial is None else spatial
+    out = np.empty((max(n, 1), 4), np.int32)
+    m = C.c_int64(0)
+    err = _err()
+    _check(lib().p3dref_quantize_slat_coords(coords.ctypes, C.c_int64(n), batch, spatial, low_resolution,
+                                             requested_resolution, C.c_int64(max_tokens), out.ctypes, C.byref(m),
+                                             err, 512), err)
+    return out[:m.value].copy()

@@ -133,6 +133,9 @@ _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp
 _sig("p3d_ape_add", i32, vp, vp, i64, i32, vp)
 _sig("p3d_project_features", i32, vp, C.POINTER(ProjectionView), i32, i32, vp, i64, vp, i64, i32, vp)
 _sig("p3d_projection_relative_matrices", i32, vp, vp, vp, i32, vp)
+_sig("p3d_slat_normalize", i32, vp, vp, i64, i32, vp, vp, i32, vp)
+_sig("p3d_quantize_slat_coords_workspace", sz, i32)
+_sig("p3d_quantize_slat_coords", i32, vp, vp, i64, i32, i32, i32, vp, vp, vp, sz)
 _sig("p3d_batch_offsets", i32, vp, vp, i64, i32, vp)
 _sig("p3d_window_count", i64, i32, i32, i32, i32, i32, i32)
 _sig("p3d_window_partition_workspace", C.c_size_t, i64, i64)

@@ -349,6 +349,33 @@ def projection_relative_matrices(c2w, distances):
     return out
 
 
+def slat_normalize(x: torch.Tensor, mean: torch.Tensor, std: torch.Tensor, denormalize: bool = False,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """(x - mean) / std, or x * std + mean (p3d_slat_normalize), f32 rows."""
+    assert x.dtype == torch.float32 and x.is_contiguous()
+    c = ctx(x.device)
+    if out is None:
+        out = torch.empty_like(x)
+    c.check(L.lib.p3d_slat_normalize(c.h, _p(x), x.shape[0], x.shape[1], _p(mean.contiguous()),
+                                     _p(std.contiguous()), int(denormalize), _p(out)))
+    return out
+
+
+def quantize_slat_coords(coords: torch.Tensor, batch: int, low_resolution: int, resolution: int = 1024) -> torch.Tensor:
+    """Decoder coordinates -> unique sorted coordinates on the 1024 cascade
+    grid (p3d_quantize_slat_coords); returns int32 [m, 4] (reads the count)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    out = torch.empty((max(n, 1), 4), dtype=torch.int32, device=coords.device)
+    count = torch.zeros(1, dtype=torch.int64, device=coords.device)
+    wsb = int(L.lib.p3d_quantize_slat_coords_workspace(batch))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=coords.device)
+    c.check(L.lib.p3d_quantize_slat_coords(c.h, _p(coords.contiguous()), n, batch, low_resolution, resolution,
+                                           _p(out), _p(count), _p(ws), wsb))
+    c.sync_check()
+    return out[:int(count.item())]
+
+
 def layernorm_modulate(x: torch.Tensor, eps: float, gamma=None, beta=None, mod: torch.Tensor | None = None,
                        batch_offsets: torch.Tensor | None = None, out_dtype=torch.bfloat16,
                        out: torch.Tensor | None = None) -> torch.Tensor:

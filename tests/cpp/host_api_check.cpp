@@ -8,6 +8,7 @@
 //
 // File format: records of {u32 name length, name, u8 type (0 f32, 1 i32,
 // 2 i64), u64 count, count values}.
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <fstream>
@@ -17,6 +18,7 @@
 #include <vector>
 
 #include "pixal3d/flow_sampler.h"
+#include "pixal3d/pipeline.h"
 #include "pixal3d/slat_decoder.h"
 #include "pixal3d/slat_flow.h"
 #include "pixal3d/sparse.h"
@@ -390,12 +392,64 @@ void flow_concat_gguf(const std::string &path) {
     FlowEulerSampleF32 r;
     if (model.sample(x, sc, ctx, &proj, r, &e, &cat)) put("tx_concat_sample", r.samples.feats);
     else put_error("tx_concat_sample", e);
+    // the stage wrapper: sample + latent denormalization (run_slat_stage_f32)
+    SLatNormalizationF32 norm;
+    for (int c = 0; c < h.out_channels; ++c) {
+        norm.mean.push_back(0.25f * static_cast<float>(c) - 1.0f);
+        norm.std.push_back(0.5f + 0.125f * static_cast<float>(c));
+    }
+    Pixal3DImageConditionF32 cond{ctx, proj};
+    SLatStageOutputF32 stage;
+    if (run_slat_stage_f32(model, x, cond, sc, norm, stage, &e, &cat)) put("tx_stage_latent", stage.latent.feats);
+    else put_error("tx_stage_latent", e);
     // a concat condition on other coordinates is refused with the reference's message
     SparseTensorF32 moved = cat;
     moved.coords[1] += 1;
     const bool refused = !model.forward(x, ts.data(), ts.size(), ctx, &proj, o, &e, &moved) &&
                          e == "SLat flow concat condition shape or coordinates mismatch";
     put("tx_concat_mismatch_refused", std::vector<float>{refused ? 1.f : 0.f});
+}
+
+// The checks of the reference's tests/pipeline_utils_test.cpp: 1 = as the
+// reference asserts, 0 = not.
+void pipeline_utils() {
+    SparseTensorF32 up;
+    up.batch_size = 1;
+    up.channels = 2;
+    up.spatial_x = up.spatial_y = up.spatial_z = 512;
+    up.coords = {0, 0, 0, 0, 0, 1, 1, 1, 0, 256, 256, 256, 0, 511, 511, 511};
+    up.feats.assign(up.points() * 2, 0.0f);
+    std::vector<std::int32_t> coords;
+    int res = 0;
+    std::string e;
+    const bool q = quantize_slat_coords_f32(up, 512, 1024, 0, coords, res, &e);
+    const std::vector<std::int32_t> expected = {0, 0, 0, 0, 0, 32, 32, 32, 0, 63, 63, 63};
+    std::vector<float> r = {q && res == 1024 && coords == expected ? 1.f : 0.f};
+    e.clear();
+    r.push_back(!quantize_slat_coords_f32(up, 512, 1536, 0, coords, res, &e) && !e.empty() ? 1.f : 0.f);
+    e.clear();
+    r.push_back(!quantize_slat_coords_f32(up, 512, 1024, 2, coords, res, &e) && !e.empty() ? 1.f : 0.f);
+    e.clear();
+    r.push_back(!quantize_slat_coords_f32(up, 512, 1000, 0, coords, res, &e) && !e.empty() ? 1.f : 0.f);
+    SparseTensorF32 d;
+    d.batch_size = 1;
+    d.channels = 2;
+    d.spatial_x = d.spatial_y = d.spatial_z = 2;
+    d.coords = {0, 0, 0, 0, 0, 1, 1, 1};
+    d.feats = {3.0f, -1.0f, 7.0f, 5.0f};
+    SLatNormalizationF32 n;
+    n.mean = {1.0f, 2.0f};
+    n.std = {2.0f, 3.0f};
+    SparseTensorF32 o;
+    const bool nz = normalize_slat_f32(d, n, o, &e);
+    const std::vector<float> en = {1.0f, -1.0f, 3.0f, 1.0f};
+    bool close = nz && o.coords == d.coords && o.feats.size() == en.size();
+    for (std::size_t i = 0; close && i < en.size(); ++i) close = std::fabs(o.feats[i] - en[i]) < 1.0e-6f;
+    r.push_back(close ? 1.f : 0.f);
+    n.std[1] = 0.0f;
+    e.clear();
+    r.push_back(!normalize_slat_f32(d, n, o, &e) && !e.empty() ? 1.f : 0.f);
+    put("pipeline_utils", r);
 }
 
 SLatDecoderBlockWeightsF32 dec_block(int i, bool c2s, int C, int O, int mlp) {
@@ -527,6 +581,7 @@ int main(int argc, char **argv) {
         flow_device();
         decoder();
         sampler();
+        pipeline_utils();
         if (argc >= 4) flow_gguf(argv[3]);
         if (argc >= 5) flow_concat_gguf(argv[4]);
     } catch (const std::exception &ex) {

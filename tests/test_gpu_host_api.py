@@ -302,4 +302,17 @@ def test_texture_stage_concat_and_projection_through_host_api(harness):
 
     exp = O.flow_euler_sample(x, sc, ref_model, c[:, 0].astype(np.int64), 2)
     _close(harness["tx_concat_sample"], exp.ravel(), "texture sample with concat")
+    # run_slat_stage_f32: the same sampling, then latent * std + mean
+    mean = (0.25 * np.arange(12) - 1.0).astype(np.float32)
+    std = (0.5 + 0.125 * np.arange(12)).astype(np.float32)
+    got = harness["tx_stage_latent"].reshape(10, 12)
+    np.testing.assert_array_equal(got, O.denormalize_slat(harness["tx_concat_sample"].reshape(10, 12), mean, std))
+    _close(got.ravel(), O.denormalize_slat(exp, mean, std).ravel(), "texture stage latent")
     assert harness["tx_concat_mismatch_refused"][0] == 1
+
+
+def test_pipeline_utils_reference_checks(harness):
+    """tests/pipeline_utils_test.cpp's assertions through this library's
+    pipeline.h: quantization known answer and refusals, normalization known
+    answer and the zero-std refusal."""
+    np.testing.assert_array_equal(harness["pipeline_utils"], np.ones(6, np.float32))
