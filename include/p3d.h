@@ -234,6 +234,20 @@ int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const i
                     int out_dtype, int epilogue, const float *gate, int64_t gate_ld,
                     const int32_t *batch_offsets, int nbatch);
 
+/* The same conv with the taps of each 256-row tile given: bit t of
+ * tile_taps[b] set when some row of rows [256 b, 256 b + 256) has a
+ * neighbour at tap t (p3d_conv_tile_taps).  The CTA-pair kernel (cout a
+ * multiple of 256) skips the other taps, whose gathered rows are all zero,
+ * so the result equals p3d_subm_conv3d's bit for bit; other shapes ignore
+ * tile_taps.  Rows ordered so that tiles share their missing taps (for a
+ * surface, by neighbour pattern) skip the most.  tile_taps NULL = every tap. */
+int p3d_subm_conv3d_taps(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const int32_t *nbr, const void *w,
+                         int ab_dtype, const float *bias, int64_t cout, void *out, int64_t ldo, int out_dtype,
+                         int epilogue, const float *gate, int64_t gate_ld, const int32_t *batch_offsets, int nbatch,
+                         const uint32_t *tile_taps);
+/* tile_taps [ceil(n / 256)] of a neighbour map [27][n] (missing = n). */
+int p3d_conv_tile_taps(p3d_ctx *ctx, const int32_t *nbr, int64_t n, uint32_t *tile_taps);
+
 /* Varlen flash attention on tcgen05 tensor cores, head_dim 64, 16-bit in/out
  * (dtype), f32 softmax/accumulation.  rows_q / rows_k: total rows of the q and
  * k/v views (cu_q[nseq], cu_k[nseq]); q/k/v/out rows 16-byte aligned.

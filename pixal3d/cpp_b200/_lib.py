@@ -128,6 +128,8 @@ _sig("p3d_c2s_topology", i32, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp)
 _sig("p3d_c2s_gather", i32, vp, vp, i64, vp, vp, i64, i32, i32, i32, vp)
 _sig("p3d_linear", i32, vp, vp, i64, vp, i32, vp, i64, i64, i64, vp, i64, i32, i32, vp, i64, vp, i32)
 _sig("p3d_subm_conv3d", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i32, i32, vp, i64, vp, i32)
+_sig("p3d_subm_conv3d_taps", i32, vp, vp, i64, i64, vp, vp, i32, vp, i64, vp, i64, i32, i32, vp, i64, vp, i32, vp)
+_sig("p3d_conv_tile_taps", i32, vp, vp, i64, vp)
 _sig("p3d_varlen_attention", i32, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, i64, i64, i64, i32, i32, f32,
      i32)
 _sig("p3d_ape_add", i32, vp, vp, i64, i32, vp)

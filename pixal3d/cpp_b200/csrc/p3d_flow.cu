@@ -16,7 +16,9 @@
 //     one step (forward + update) is captured once as a CUDA graph and
 //     replayed for every remaining step.
 // Residual stream h is f32; GEMM operands f16 (or bf16); accumulation f32.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <unordered_map>
 #include <vector>
 
@@ -133,22 +135,55 @@ __global__ void add_mod_kernel(const float *bm, const float *tmod, int batch, in
 
 // f32 [n, in] -> 16-bit [n, in_pad] (zero padded).
 template <typename T>
-__global__ void pad16_kernel(const float *x, int64_t n, int in, int in_pad, T *out) {
+__global__ void pad16_kernel(const float *x, int64_t n, int in, int in_pad, T *out, const int32_t *rows) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n * in_pad) return;
     const int64_t r = i / in_pad;
     const int c = static_cast<int>(i - r * in_pad);
-    out[i] = from_f32<T>(c < in ? x[r * in + c] : 0.0f);
+    const int64_t src = rows ? rows[r] : r;  // rows: gather x[rows[r]] into row r
+    out[i] = from_f32<T>(c < in ? x[src * in + c] : 0.0f);
 }
 
-int pad16(p3d_ctx *ctx, const float *x, int64_t n, int in, int in_pad, void *out, int dtype) {
+int pad16(p3d_ctx *ctx, const float *x, int64_t n, int in, int in_pad, void *out, int dtype,
+          const int32_t *rows = nullptr) {
     if (n * in_pad == 0) return P3D_OK;
     const unsigned grid = blocks_for(n * in_pad, 256);
     if (dtype == P3D_BF16)
-        pad16_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__nv_bfloat16 *>(out));
+        pad16_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__nv_bfloat16 *>(out),
+                                                                   rows);
     else
-        pad16_kernel<__half><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__half *>(out));
+        pad16_kernel<__half><<<grid, 256, 0, ctx->stream>>>(x, n, in, in_pad, static_cast<__half *>(out), rows);
     return check_launch(ctx, "pad16");
+}
+
+// Neighbour pattern of each row: bit t set when nbr[t][row] is a point.
+__global__ void row_taps_kernel(const int32_t *__restrict__ nbr, int64_t n, uint32_t *__restrict__ taps) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (row >= n) return;
+    uint32_t m = 0;
+    for (int t = 0; t < 27; ++t) {
+        const int32_t s = nbr[static_cast<int64_t>(t) * n + row];
+        if (s >= 0 && s < n) m |= 1u << t;
+    }
+    taps[row] = m;
+}
+
+// out[rows[i]][c] = y[i][c]: fine rows back to the caller's order.
+__global__ void scatter_rows_kernel(const float *__restrict__ y, const int32_t *__restrict__ rows, int64_t n, int C,
+                                    float *__restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * C) return;
+    const int64_t r = i / C;
+    out[static_cast<int64_t>(rows[r]) * C + (i - r * C)] = y[i];
+}
+
+// P3D_CONV_SORT=0 keeps the fine level in the caller's row order.
+bool conv_sort_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("P3D_CONV_SORT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 // Sinusoidal absolute 3D PE added to h (no reference; benchmark config 1/2):
@@ -294,6 +329,11 @@ struct p3d_flow {
     int64_t n = 0, nt = 0, T = 0, max_fine = 0, max_trunk = 0, max_ctx = 0;
     int32_t *coords = nullptr, *trunk_coords = nullptr, *fine_off = nullptr, *trunk_off = nullptr, *ctx_off = nullptr;
     int32_t *nbr = nullptr, *parent = nullptr, *child = nullptr;
+    // fine level in neighbour-pattern order: fine row i is the caller's row
+    // perm[i] (null: caller order); conv taps per 256-row tile
+    int32_t *perm = nullptr;
+    uint32_t *row_taps = nullptr, *fine_taps = nullptr;
+    float *out_tmp = nullptr;
     // workspaces
     float *h = nullptr, *hf = nullptr, *ftmp = nullptr, *tfreq = nullptr, *temb = nullptr, *temb2 = nullptr,
           *tmod = nullptr, *mods = nullptr, *x_model = nullptr, *vel = nullptr, *sched = nullptr, *ts = nullptr;
@@ -404,7 +444,7 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
     P3D_TRY(small_linear(ctx, f->temb, B, C, f->t_w2, f->t_b2, C, f->temb2, 0, 0));
     P3D_TRY(small_linear(ctx, f->temb2, B, C, f->mod_w, f->mod_b, 6 * C, f->tmod, 2, 0));
     // input linear
-    P3D_TRY(pad16(ctx, x, n, hp.in_channels, f->in_pad, f->x_in, dt));
+    P3D_TRY(pad16(ctx, x, n, hp.in_channels, f->in_pad, f->x_in, dt, io ? f->perm : nullptr));
     float *hin = io ? f->hf : f->h;
     P3D_TRY(p3d_linear(ctx, f->x_in, f->in_pad, f->input_w, dt, f->input_b, n, C, f->in_pad, hin, C, P3D_F32, P3D_EPI_NONE,
                        nullptr, 0, nullptr, 0));
@@ -412,12 +452,12 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         for (const DevRes &r : f->io_in) {
             P3D_TRY(p3d_group_norm_silu(ctx, f->hf, n, C, hp.groups, 1e-5f, r.gn1_w, r.gn1_b, f->fine_off, B, 1,
                                         f->stats, f->fbf, dt));
-            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
-                                    P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_subm_conv3d_taps(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
+                                         P3D_EPI_NONE, nullptr, 0, nullptr, 0, f->fine_taps));
             P3D_TRY(p3d_group_norm_silu(ctx, f->ftmp, n, C, hp.groups, 1e-5f, r.gn2_w, r.gn2_b, f->fine_off, B, 1,
                                         f->stats, f->fbf, dt));
-            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
-                                    P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_subm_conv3d_taps(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
+                                         P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0, f->fine_taps));
         }
         P3D_TRY(p3d_downsample_mean(ctx, f->hf, nt, C, 2, f->child, P3D_F32, f->h));
     }
@@ -495,20 +535,26 @@ int forward_impl(p3d_flow *f, const float *x, const float *ts, int ts_stride, co
         for (const DevRes &r : f->io_out) {
             P3D_TRY(p3d_group_norm_silu(ctx, f->hf, n, C, hp.groups, 1e-5f, r.gn1_w, r.gn1_b, f->fine_off, B, 1,
                                         f->stats, f->fbf, dt));
-            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
-                                    P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_subm_conv3d_taps(ctx, f->fbf, n, C, f->nbr, r.conv1_w, dt, r.conv1_b, C, f->ftmp, C, P3D_F32,
+                                         P3D_EPI_NONE, nullptr, 0, nullptr, 0, f->fine_taps));
             P3D_TRY(p3d_group_norm_silu(ctx, f->ftmp, n, C, hp.groups, 1e-5f, r.gn2_w, r.gn2_b, f->fine_off, B, 1,
                                         f->stats, f->fbf, dt));
-            P3D_TRY(p3d_subm_conv3d(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
-                                    P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0));
+            P3D_TRY(p3d_subm_conv3d_taps(ctx, f->fbf, n, C, f->nbr, r.conv2_w, dt, r.conv2_b, C, f->hf, C, P3D_F32,
+                                         P3D_EPI_RESIDUAL, nullptr, 0, nullptr, 0, f->fine_taps));
         }
         hout = f->hf;
     }
     // final LayerNorm (eps 1e-5, src/slat_flow.cpp:244-248) + output linear
     uint16_t *xfin = io ? f->fbf : f->xn;
     P3D_TRY(p3d_layernorm_modulate(ctx, hout, n, C, 1e-5f, nullptr, nullptr, nullptr, 0, nullptr, 0, xfin, dt));
-    P3D_TRY(p3d_linear(ctx, xfin, C, f->output_w, dt, f->output_b, n, hp.out_channels, C, out, hp.out_channels, P3D_F32,
+    float *y = (io && f->perm) ? f->out_tmp : out;
+    P3D_TRY(p3d_linear(ctx, xfin, C, f->output_w, dt, f->output_b, n, hp.out_channels, C, y, hp.out_channels, P3D_F32,
                        P3D_EPI_NONE, nullptr, 0, nullptr, 0));
+    if (y != out) {
+        scatter_rows_kernel<<<blocks_for(n * hp.out_channels, 256), 256, 0, ctx->stream>>>(y, f->perm, n,
+                                                                                          hp.out_channels, out);
+        P3D_TRY(check_launch(ctx, "scatter_rows"));
+    }
     return P3D_OK;
 }
 
@@ -524,7 +570,9 @@ struct StreamSwap {
 void p3d_flow::reset_topology() {
     prepared = false;
     n = nt = T = max_fine = max_trunk = max_ctx = 0;
-    coords = trunk_coords = fine_off = trunk_off = ctx_off = nbr = parent = child = nullptr;
+    coords = trunk_coords = fine_off = trunk_off = ctx_off = nbr = parent = child = perm = nullptr;
+    row_taps = fine_taps = nullptr;
+    out_tmp = nullptr;
     h = hf = ftmp = tfreq = temb = temb2 = tmod = mods = x_model = vel = sched = ts = x_state = proj_model = nullptr;
     xn = qkv = attn = mlp = kv = cq = ctx_bf = proj_bf = x_in = fbf = nullptr;
     stats = nullptr;
@@ -739,6 +787,42 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         const size_t wsb = p3d_neighbor_map27_workspace(n);
         P3D_TRY(f->alloc(&f->hash_ws, static_cast<int64_t>((wsb + 3) / 4)));
         P3D_TRY(p3d_neighbor_map27_ws(ctx, f->coords, n, f->hash_ws, wsb, f->nbr));
+        if (conv_sort_enabled()) {
+            // Order the fine rows of each batch item by neighbour pattern
+            // (stable), so a 256-row conv tile shares its missing taps and
+            // the conv skips them.  The fine level runs in this order; the
+            // input rows are gathered and the output rows scattered back.
+            P3D_TRY(f->alloc(&f->row_taps, n));
+            row_taps_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(f->nbr, n, f->row_taps);
+            P3D_TRY(check_launch(ctx, "row_taps"));
+            std::vector<uint32_t> hm(static_cast<size_t>(n));
+            P3D_CUDA(ctx, cudaMemcpyAsync(hm.data(), f->row_taps, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost,
+                                          ctx->stream));
+            P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+            std::vector<int32_t> order(static_cast<size_t>(n));
+            for (int64_t i = 0; i < n; ++i) order[i] = static_cast<int32_t>(i);
+            auto key = [&](int32_t i) {
+                return (static_cast<uint64_t>(static_cast<uint32_t>(hc[static_cast<size_t>(i) * 4])) << 32) | hm[i];
+            };
+            std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return key(a) < key(b); });
+            bool identity = true;
+            for (int64_t i = 0; i < n && identity; ++i) identity = order[i] == i;
+            if (!identity) {
+                std::vector<int32_t> hcp(static_cast<size_t>(n) * 4);
+                for (int64_t i = 0; i < n; ++i)
+                    for (int k = 0; k < 4; ++k) hcp[i * 4 + k] = hc[static_cast<size_t>(order[i]) * 4 + k];
+                P3D_CUDA(ctx, cudaMemcpyAsync(f->coords, hcp.data(), sizeof(int32_t) * n * 4, cudaMemcpyHostToDevice,
+                                              ctx->stream));
+                P3D_TRY(f->alloc(&f->perm, n));
+                P3D_CUDA(ctx, cudaMemcpyAsync(f->perm, order.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice,
+                                              ctx->stream));
+                P3D_TRY(f->alloc(&f->out_tmp, n * hp.out_channels));
+                P3D_TRY(p3d_neighbor_map27_ws(ctx, f->coords, n, f->hash_ws, wsb, f->nbr));
+                P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // host vectors above go out of scope
+            }
+        }
+        P3D_TRY(f->alloc(&f->fine_taps, (n + 255) / 256));
+        P3D_TRY(p3d_conv_tile_taps(ctx, f->nbr, n, f->fine_taps));
         const int64_t gints = p3d_downsample_grid_ints(batch, sx, sy, sz, 2);
         P3D_TRY(f->alloc(&f->trunk_coords, n * 4));
         P3D_TRY(f->alloc(&f->parent, n));

@@ -76,6 +76,10 @@ struct GemmParams {
     // 1: the epilogue stages 32 x 32 boxes in shared memory and writes them
     // with TMA through tmap_o (store, or reduce-add for the residual).
     int tma_out;
+    // Gather (pair kernel): per 256-row tile, bit t set when some row of the
+    // tile has a neighbour at tap t; other taps are skipped (their A rows
+    // are all zero).  Null: every tap.
+    const uint32_t *tile_taps;
 };
 
 // TMA-store epilogue staging: each of the 4 epilogue warps owns two 4 KB
@@ -805,6 +809,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
     const int64_t num_tiles = m_tiles * n_tiles;
     const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
     const int num_kb = GATHER ? 27 * kblocks_per_tap : kblocks_per_tap;
+    // taps of a pair tile (the centre tap always: every row has itself)
+    auto tile_taps = [&](int64_t tile) -> uint32_t {
+        if (!GATHER || TMAG || !p.tile_taps) return 0x7FFFFFFu;
+        return (__ldg(p.tile_taps + tile / n_tiles) | (1u << 13)) & 0x7FFFFFFu;
+    };
+    auto tile_kb = [&](int64_t tile) -> int { return GATHER ? __popc(tile_taps(tile)) * kblocks_per_tap : num_kb; };
 
     if (threadIdx.x == 0) {
         // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
@@ -890,11 +900,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
             const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
             const int64_t n0 = (tile % n_tiles) * PAIR_N;
             int32_t cur_src = 0, next_src = 0;
+            // taps still to visit after `tap`; next_tap = 27 when none
+            uint32_t rem = tile_taps(tile);
+            int tap = 0, next_tap = 27;
             if (GATHER) {
-                cur_src = gather_src(p, grow, m0, 0);
-                next_src = gather_src(p, grow, m0, 1);
+                tap = __ffs(rem) - 1;
+                rem &= rem - 1;
+                next_tap = rem ? __ffs(rem) - 1 : 27;
+                cur_src = gather_src(p, grow, m0, tap);
+                next_src = gather_src(p, grow, m0, next_tap);
             }
-            for (int kb = 0; kb < num_kb; ++kb) {
+            const int nkb = tile_kb(tile);
+            for (int kb = 0; kb < nkb; ++kb) {
                 if (GATHER) {
                     if (!warp_wait<true>(&empty_bar[stage], phase ^ 1, p.fault)) {
                         ok = false;
@@ -908,12 +925,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
                 }
                 uint8_t *sa = smem_a + stage * C::A_BYTES;
                 uint8_t *sb = smem_b + stage * C::B_BYTES;
-                const int tap = GATHER ? kb / kblocks_per_tap : 0;
                 const int kc = GATHER ? (kb % kblocks_per_tap) * BK : kb * BK;
                 if (GATHER) {
-                    if (kc == 0 && tap > 0) {
+                    if (kc == 0 && kb > 0) {
+                        tap = next_tap;
+                        rem &= rem - 1;
+                        next_tap = rem ? __ffs(rem) - 1 : 27;
                         cur_src = next_src;
-                        next_src = gather_src(p, grow, m0, tap + 1);
+                        next_src = gather_src(p, grow, m0, next_tap);
                     }
                     gather_stage_a16(p, sa, pw, lane, cur_src, kc);
                 }
@@ -951,7 +970,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const int nkb = tile_kb(tile);
+                for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait_cluster(&full_bar[stage], phase, p.fault)) {
                         ok = false;
                         break;
@@ -995,7 +1015,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
             uint32_t phase = 0;
             bool ok = true;
             for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const int nkb = tile_kb(tile);
+                for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait(&full_bar[stage], phase, p.fault)) {
                         ok = false;
                         break;
@@ -1337,10 +1358,55 @@ int linear_impl(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_
 }
 }  // namespace
 
+namespace p3d {
+namespace {
+// Bit t of tile_taps[b]: some row of rows [256 b, 256 b + 256) has a
+// neighbour at tap t (nbr[t][row] in [0, n)).  One block per tile.
+__global__ void __launch_bounds__(256) conv_tile_taps_kernel(const int32_t *__restrict__ nbr, int64_t n,
+                                                             uint32_t *__restrict__ taps) {
+    __shared__ uint32_t warp_or[8];
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    uint32_t m = 0;
+    if (row < n) {
+#pragma unroll
+        for (int t = 0; t < 27; ++t) {
+            const int32_t s = __ldg(nbr + static_cast<int64_t>(t) * n + row);
+            if (s >= 0 && s < n) m |= 1u << t;
+        }
+    }
+    m = __reduce_or_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0) warp_or[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t r = 0;
+        for (int i = 0; i < 8; ++i) r |= warp_or[i];
+        taps[blockIdx.x] = r;
+    }
+}
+}  // namespace
+}  // namespace p3d
+
+extern "C" int p3d_conv_tile_taps(p3d_ctx *ctx, const int32_t *nbr, int64_t n, uint32_t *tile_taps) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, nbr && tile_taps && n >= 0 && n < (int64_t(1) << 31), "p3d_conv_tile_taps: bad argument");
+    if (n == 0) return P3D_OK;
+    DeviceGuard guard(ctx->device);
+    conv_tile_taps_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(nbr, n, tile_taps);
+    return check_launch(ctx, "conv_tile_taps");
+}
+
 extern "C" int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const int32_t *nbr,
                                const void *w, int ab_dtype, const float *bias, int64_t cout, void *out, int64_t ldo,
                                int out_dtype, int epilogue, const float *gate, int64_t gate_ld,
                                const int32_t *batch_offsets, int nbatch) {
+    return p3d_subm_conv3d_taps(ctx, x, n, cin, nbr, w, ab_dtype, bias, cout, out, ldo, out_dtype, epilogue, gate,
+                                gate_ld, batch_offsets, nbatch, nullptr);
+}
+
+extern "C" int p3d_subm_conv3d_taps(p3d_ctx *ctx, const void *x, int64_t n, int64_t cin, const int32_t *nbr,
+                                    const void *w, int ab_dtype, const float *bias, int64_t cout, void *out,
+                                    int64_t ldo, int out_dtype, int epilogue, const float *gate, int64_t gate_ld,
+                                    const int32_t *batch_offsets, int nbatch, const uint32_t *tile_taps) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && nbr && w && out, "p3d_subm_conv3d: null pointer");
     P3D_REQUIRE(ctx, n >= 0 && cout > 0, "p3d_subm_conv3d: bad shape");
@@ -1372,5 +1438,6 @@ extern "C" int p3d_subm_conv3d(p3d_ctx *ctx, const void *x, int64_t n, int64_t c
     p.out_dtype = out_dtype;
     p.epi = epilogue;
     p.fault = ctx->fault;
+    p.tile_taps = tile_taps;
     return run_gemm(ctx, nullptr, cin, w, ab_dtype, p);
 }

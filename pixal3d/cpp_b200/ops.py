@@ -225,9 +225,11 @@ def rope_table(coords: torch.Tensor, head_dim: int = 64, freq_min: float = 1.0,
 def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32,
                 epilogue: int = L.EPI_NONE, gate: torch.Tensor | None = None,
-                batch_offsets: torch.Tensor | None = None) -> torch.Tensor:
+                batch_offsets: torch.Tensor | None = None, tile_taps: torch.Tensor | None = None) -> torch.Tensor:
     """Gather-GEMM submanifold conv (sparse_submanifold_conv3d, src/sparse.cpp:999-1055).
-    x [n, cin], w [27, cout, cin], both bf16 or both f16."""
+    x [n, cin], w [27, cout, cin], both bf16 or both f16.  tile_taps
+    (conv_tile_taps of nbr) lets the kernel skip taps no row of a 256-row
+    tile uses; the result is the same."""
     assert x.dtype in HALF and w.dtype == x.dtype and x.is_contiguous() and w.is_contiguous()
     c = ctx(x.device)
     n, cin = x.shape
@@ -236,9 +238,18 @@ def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch
         out = torch.empty((n, cout), dtype=out_dtype, device=x.device)
     gate_ld = gate.stride(0) if gate is not None else 0
     nb = batch_offsets.shape[0] - 1 if batch_offsets is not None else 0
-    c.check(L.lib.p3d_subm_conv3d(c.h, _p(x), n, cin, _p(nbr), _p(w), _dt(x), _p(bias), cout, _p(out), _rows(out), _dt(out),
-                                  epilogue, _p(gate), gate_ld, _p(batch_offsets), nb))
+    c.check(L.lib.p3d_subm_conv3d_taps(c.h, _p(x), n, cin, _p(nbr), _p(w), _dt(x), _p(bias), cout, _p(out), _rows(out),
+                                       _dt(out), epilogue, _p(gate), gate_ld, _p(batch_offsets), nb, _p(tile_taps)))
     return out
+
+
+def conv_tile_taps(nbr: torch.Tensor) -> torch.Tensor:
+    """Per 256-row tile, the taps some row of the tile uses (p3d_conv_tile_taps)."""
+    c = ctx(nbr.device)
+    n = nbr.shape[1]
+    taps = torch.empty(max((n + 255) // 256, 1), dtype=torch.int32, device=nbr.device)
+    c.check(L.lib.p3d_conv_tile_taps(c.h, _p(nbr), n, _p(taps)))
+    return taps
 
 
 def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: torch.Tensor, cu_k: torch.Tensor,

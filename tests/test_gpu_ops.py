@@ -336,6 +336,40 @@ def test_subm_conv3d_pair_tiles(cin, cout, npts):
     check(out.cpu().numpy(), res + tight, max_abs=1e-3, rel_l2=1e-4, what="pair conv residual")
 
 
+def test_subm_conv3d_tile_taps_skip_is_exact():
+    """Rows ordered by neighbour pattern (as the flow's fine level runs):
+    the pair kernel skipping the taps no row of a 256-row tile uses gives the
+    same bits as the full 27-tap loop, plain and with the residual epilogue."""
+    c = shell_coords(40, 14.0, 1.3)
+    nb = O.neighbor_map27(c)
+    mask = np.zeros(c.shape[0], np.int64)
+    for t in range(27):
+        mask |= (nb[t] < c.shape[0]).astype(np.int64) << t
+    c = np.ascontiguousarray(c[np.argsort(mask, kind="stable")])
+    x, w, b = _conv_case(c, 128, 512, 3)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    taps = o.conv_tile_taps(nbr)
+    tb = taps.cpu().numpy().astype(np.uint32)
+    full = (1 << 27) - 1
+    assert (tb != full).sum() > 0  # some tiles skip taps
+    a = o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out_dtype=torch.float32)
+    s = o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out_dtype=torch.float32, tile_taps=taps)
+    assert torch.equal(a, s)
+    res = dev(np.random.default_rng(1).standard_normal((c.shape[0], 512)).astype(np.float32))
+    r1, r2 = res.clone(), res.clone()
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=r1, epilogue=L().EPI_RESIDUAL)
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=r2, epilogue=L().EPI_RESIDUAL, tile_taps=taps)
+    assert torch.equal(r1, r2)
+    # tile taps against the map: OR of each 256-row tile's neighbour patterns
+    nbs = O.neighbor_map27(c)
+    pat = np.zeros(c.shape[0], np.int64)
+    for t in range(27):
+        pat |= (nbs[t] < c.shape[0]).astype(np.int64) << t
+    exp = [int(np.bitwise_or.reduce(pat[i:i + 256])) for i in range(0, c.shape[0], 256)]
+    np.testing.assert_array_equal(tb.astype(np.int64), exp)
+
+
 def test_linear_pair_kernel_subprocess():
     """The CTA-pair kernel on dense linears (selected by P3D_GEMM_PAIR_DENSE=1,
     read once per process, hence a child process): M below one CTA's 128 rows
