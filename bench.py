@@ -186,22 +186,29 @@ def algorithmic_flops(n_img: int, n_trunk_img: int, pairs_img: int) -> dict:
 def time_conv_kernel(torch, ops, coords_dev, reps=10):
     """Average device time of the dominant kernel (gather-GEMM sparse conv,
     C=1024, the config-2 fine level, batch 2) measured with CUDA events on
-    the launching stream."""
+    the launching stream, as the flow runs it: rows of each batch item in
+    neighbour-pattern order, taps no row of a 256-row tile uses skipped."""
     n = coords_dev.shape[0]
     nbr = ops.neighbor_map27(coords_dev)
+    bits = torch.arange(27, device=nbr.device, dtype=torch.int64)
+    pattern = ((nbr < n).to(torch.int64) << bits[:, None]).sum(0)
+    key = (coords_dev[:, 0].to(torch.int64) << 32) | pattern
+    order = torch.sort(key, stable=True).indices
+    nbr = ops.neighbor_map27(coords_dev[order].contiguous())
+    taps = ops.conv_tile_taps(nbr)
     pairs = int((nbr < n).sum().item())
     x = torch.randn((n, C), device="cuda").to(torch.float16)
     w = (torch.randn((27, C, C), device="cuda") / math.sqrt(27 * C)).to(torch.float16)
     b = torch.zeros(C, device="cuda")
     out = torch.empty((n, C), device="cuda")
     for _ in range(2):
-        ops.subm_conv3d(x, nbr, w, b, out=out)
+        ops.subm_conv3d(x, nbr, w, b, out=out, tile_taps=taps)
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(s)
     for _ in range(reps):
-        ops.subm_conv3d(x, nbr, w, b, out=out)
+        ops.subm_conv3d(x, nbr, w, b, out=out, tile_taps=taps)
     e1.record(s)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps

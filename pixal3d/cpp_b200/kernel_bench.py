@@ -5,6 +5,7 @@ events around a CUDA-graph replay of --reps calls).
 
 Kernels (config-2 shapes unless noted):
   conv1024   gather-GEMM sparse conv 1024->1024 on the 64^3 shell, batch 2
+  conv1024t  the same with rows in neighbour-pattern order and tile tap skipping
   conv64     config-0 conv 64->64 on the shell (21,766 voxels)
   qkv        trunk qkv linear, 8,184 x 1024 -> 3072
   mlp0       trunk MLP up-projection with GELU, 8,184 x 1024 -> 4096
@@ -69,18 +70,25 @@ def run(kernel: str, reps: int) -> dict:
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     h = torch.float16
-    if kernel in ("conv1024", "conv64"):
+    if kernel in ("conv1024", "conv1024t", "conv64"):
         cc = shell_coords()
-        ch = 1024 if kernel == "conv1024" else 64
+        ch = 64 if kernel == "conv64" else 1024
         coords = torch.from_numpy(batched(cc, 2) if ch == 1024 else cc).to(dev)
         n = coords.shape[0]
         nbr = ops.neighbor_map27(coords)
+        taps = None
+        if kernel == "conv1024t":
+            # as the flow's fine level runs: rows in neighbour-pattern order, tile taps
+            bits = torch.arange(27, device=dev, dtype=torch.int64)
+            key = (coords[:, 0].to(torch.int64) << 32) | ((nbr < n).to(torch.int64) << bits[:, None]).sum(0)
+            nbr = ops.neighbor_map27(coords[torch.sort(key, stable=True).indices].contiguous())
+            taps = ops.conv_tile_taps(nbr)
         pairs = int((nbr < n).sum().item())
         x = torch.randn((n, ch), device=dev, generator=g).to(h)
         w = (torch.randn((27, ch, ch), device=dev, generator=g) / math.sqrt(27 * ch)).to(h)
         b = torch.zeros(ch, device=dev)
         out = torch.empty((n, ch), device=dev)
-        ms = _time(lambda: ops.subm_conv3d(x, nbr, w, b, out=out), reps)
+        ms = _time(lambda: ops.subm_conv3d(x, nbr, w, b, out=out, tile_taps=taps), reps)
         flops = 2.0 * pairs * ch * ch
         bytes_ = n * ch * 2 + 27 * ch * ch * 2 + 27 * n * 4 + n * ch * 4
         return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6,
