@@ -214,7 +214,7 @@ int p3d_linear(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_d
  * [0, norm_cols) are RMS-normalised per 64-column head with gamma[col]
  * (sparse_multihead_rms_norm, src/sparse.cpp:919-954), and columns
  * [0, rope_cols) are rotated by the interleaved 3D RoPE with
- * rope_table[row][32] = (cos, sin) from p3d_rope_table
+ * rope_table[pair][row] = (cos, sin), 32 pairs x m rows, from p3d_rope_table
  * (sparse_rotary_position_embedding, src/sparse.cpp:861-917).  Normalises
  * the f32 accumulators before rounding to out_dtype.  n, norm_cols and
  * rope_cols must be multiples of 64. */
@@ -383,8 +383,9 @@ int p3d_qk_rmsnorm_rope(p3d_ctx *ctx, void *x, int64_t n, int64_t ld, int heads,
                         const float *gamma, const int32_t *coords, float freq_min, float freq_base,
                         int dtype);
 /* Per-point RoPE cos/sin table for p3d_linear_headnorm
- * (src/sparse.cpp:881-906): table[i][p] = (cos, sin) of pair p of point i,
- * head_dim/2 pairs; pairs past 3*floor(head_dim/6) get (1, 0). */
+ * (src/sparse.cpp:881-906), pair-major: table[p][i] = (cos, sin) of pair p
+ * of point i (float2 [head_dim/2][n]); pairs past 3*floor(head_dim/6) get
+ * (1, 0). */
 int p3d_rope_table(p3d_ctx *ctx, const int32_t *coords, int64_t n, int head_dim, float freq_min,
                    float freq_base, float *table);
 

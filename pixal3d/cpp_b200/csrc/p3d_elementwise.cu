@@ -227,14 +227,14 @@ __global__ void qk_rms_rope_kernel(T *__restrict__ x, int64_t n, int64_t ld, int
     }
 }
 
-// One thread per (point, pair): the cos/sin that qk_rms_rope_kernel computes
-// on the fly, stored once per coordinate set.
+// One thread per (pair, point): the cos/sin that qk_rms_rope_kernel computes
+// on the fly, stored once per coordinate set, pair-major (table[pr][row]).
 __global__ void rope_table_kernel(const int4 *__restrict__ coords, int64_t n, int pairs, float fmin, float fbase,
                                   float2 *__restrict__ table) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n * pairs) return;
-    const int64_t row = i / pairs;
-    const int pr = static_cast<int>(i - row * pairs);
+    const int pr = static_cast<int>(i / n);
+    const int64_t row = i - static_cast<int64_t>(pr) * n;
     const int fd = pairs / 3;
     float cs = 1.0f, sn = 0.0f;
     if (pr < 3 * fd) {

@@ -69,7 +69,8 @@ struct GemmParams {
     int *fault;
     // Per-head RMS norm + RoPE epilogue (head_dim 64): columns [0, norm_cols)
     // are normalised per 64-column head with gamma[col]; columns
-    // [0, rope_cols) are then rotated with rope[row][pair] = (cos, sin).
+    // [0, rope_cols) are then rotated with rope[pair][row] = (cos, sin)
+    // (pair-major: a warp's 32 rows read one contiguous 256-byte run).
     int64_t norm_cols, rope_cols;
     const float *norm_gamma;
     const float2 *rope;
@@ -234,10 +235,9 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc
                     for (int i = 0; i < 64; ++i) v[i] = v[i] * inv * __ldg(p.norm_gamma + col0 + i);
                 }
                 if (col0 < p.rope_cols) {
-                    const float2 *cs2 = p.rope + row * 32;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const float2 r = __ldg(cs2 + i);
+                        const float2 r = __ldg(p.rope + static_cast<int64_t>(i) * p.M + row);
                         const float e = v[2 * i], o = v[2 * i + 1];
                         v[2 * i] = e * r.x - o * r.y;
                         v[2 * i + 1] = e * r.y + o * r.x;
@@ -398,14 +398,12 @@ __device__ __forceinline__ bool prep_chunk(const GemmParams &p, int64_t row, int
 
 // Rotate the 16 (even, odd) pairs of v by (cos, sin) = (r[i/2].x, .y) for
 // even i and (r[i/2].z, .w) for odd i.
-__device__ __forceinline__ void rope_rotate16(float (&v)[32], const float4 (&r)[8]) {
+__device__ __forceinline__ void rope_rotate16(float (&v)[32], const float2 (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const float c = (i & 1) ? r[i >> 1].z : r[i >> 1].x;
-        const float sn = (i & 1) ? r[i >> 1].w : r[i >> 1].y;
         const float e = v[2 * i], o = v[2 * i + 1];
-        v[2 * i] = e * c - o * sn;
-        v[2 * i + 1] = e * sn + o * c;
+        v[2 * i] = e * r[i].x - o * r[i].y;
+        v[2 * i + 1] = e * r[i].y + o * r[i].x;
     }
 }
 
@@ -434,7 +432,7 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
             tmem_ld32(tacc + cs + 32, b);
             const bool rope = col0 < p.rope_cols;
             const bool norm = col0 < p.norm_cols;
-            const float4 *rp = reinterpret_cast<const float4 *>(p.rope + (row < p.M ? row : 0) * 32);
+            const float2 *rp = p.rope + (row < p.M ? row : 0);  // pair j at rp[j * M]
             tmem_ld_wait_regs(a);
             tmem_ld_wait_regs(b);
             if (p.bias) {
@@ -464,10 +462,10 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
                     mul_vec32(a, p.norm_gamma + col0 + 32 * half, 32);
                 }
                 if (rope) {
-                    float4 r4[8];
+                    float2 r2[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) r4[i] = __ldg(rp + 8 * half + i);
-                    rope_rotate16(a, r4);
+                    for (int i = 0; i < 16; ++i) r2[i] = __ldg(rp + static_cast<int64_t>(16 * half + i) * p.M);
+                    rope_rotate16(a, r2);
                 }
                 stage_row(p.out_dtype, buf, lane, a, f32 ? 0 : half);
                 if (f32) issue_box(p, tmo, buf, lane, col0 + 32 * half, row0, slot);

@@ -214,10 +214,11 @@ def linear_headnorm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None,
 
 def rope_table(coords: torch.Tensor, head_dim: int = 64, freq_min: float = 1.0,
                freq_base: float = 10000.0) -> torch.Tensor:
-    """[n, head_dim/2, 2] f32 (cos, sin) per point and rotation pair."""
+    """[head_dim/2, n, 2] f32 (cos, sin) per rotation pair and point
+    (pair-major, the layout p3d_linear_headnorm reads)."""
     c = ctx(coords.device)
     n = coords.shape[0]
-    t = torch.empty((n, head_dim // 2, 2), dtype=torch.float32, device=coords.device)
+    t = torch.empty((head_dim // 2, n, 2), dtype=torch.float32, device=coords.device)
     c.check(L.lib.p3d_rope_table(c.h, _p(coords), n, head_dim, freq_min, freq_base, _p(t)))
     return t
 

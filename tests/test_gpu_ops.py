@@ -635,7 +635,7 @@ def test_qk_rmsnorm_rope_f16():
 
 def test_rope_table():
     c = batched(shell_coords(32, 11.0, 1.0), 2)
-    t = ops().rope_table(dev(c), 64, 1.0, 10000.0).cpu().numpy()
+    t = ops().rope_table(dev(c), 64, 1.0, 10000.0).cpu().numpy().transpose(1, 0, 2)  # pair-major -> [n, pairs, 2]
     cos, sin = O.rope_tables(c, 64, 1.0, 10000.0)
     check(t[..., 0], cos, max_abs=2e-5, rel_l2=1e-5, what="rope cos")
     check(t[..., 1], sin, max_abs=2e-5, rel_l2=1e-5, what="rope sin")
