@@ -396,8 +396,7 @@ __device__ __forceinline__ bool prep_chunk(const GemmParams &p, int64_t row, int
     return true;
 }
 
-// Rotate the 16 (even, odd) pairs of v by (cos, sin) = (r[i/2].x, .y) for
-// even i and (r[i/2].z, .w) for odd i.
+// Rotate the 16 (even, odd) pairs of v: pair i by (cos, sin) = (r[i].x, r[i].y).
 __device__ __forceinline__ void rope_rotate16(float (&v)[32], const float2 (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
