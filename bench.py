@@ -45,6 +45,28 @@ RES, RADIUS, HALF_WIDTH = 64, 24.0, 1.5
 C, HEADS, BLOCKS, CTX_TOKENS, CH = 1024, 16, 24, 1029, 8
 
 
+class _stdout_to_stderr:
+    """Within the block, writes to file descriptor 1 (C and Python) land on
+    stderr; C stdio buffers are flushed before descriptor 1 is restored."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        try:
+            import ctypes
+            ctypes.CDLL(None).fflush(None)
+        except OSError:
+            pass
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -326,11 +348,16 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        # NCCL's own log lines (e.g. "NCCL version ..." under NCCL_DEBUG) go to
-        # stderr, so rank 0's stdout carries only the JSON result line.
+        # NCCL prints its version line ("NCCL version ...") to the process's
+        # stdout at communicator creation under NCCL_DEBUG=VERSION/WARN, where
+        # NCCL_DEBUG_FILE is not used.  Point file descriptor 1 at stderr while
+        # the communicator is created (eagerly here, plus a barrier), so rank
+        # 0's stdout carries only the JSON result line.
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
     from pixal3d.cpp_b200 import dist as D
     from pixal3d.cpp_b200 import ops
     from pixal3d.cpp_b200.flow import FlowModel, HParams
