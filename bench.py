@@ -11,10 +11,19 @@ forward (conditional + zeros condition, batched) + the Euler/CFG update.
 Weights random-init (seeded), condition tokens and noise N(0,1) (seeded).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --workload cfg4 [--gpus N] [--steps 25]
 
 N > 1: launched by torchrun, one rank per GPU; every rank samples its own
 image (weak scaling); NCCL broadcasts the condition tokens before timing and
 gathers the results after it.  Rank 0 prints ONE JSON line.
+
+--workload cfg4: 64 independent images with ragged
+shells (radius ~ U(12, 30), half-width ~ U(1, 2.5); 4,256 to 55,719 voxels),
+each with its own 1,029 x 1,024 condition, assigned to ranks by greedy LPT on
+voxel count and packed per rank into varlen CFG batches; every image runs
+the full config-2 sampler (--steps Euler steps, default 25).  Reports
+images/s end to end (host inputs copied in, latents copied out), the
+per-step latency and the measured load imbalance.
 """
 from __future__ import annotations
 
@@ -70,7 +79,8 @@ class _stdout_to_stderr:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--workload", choices=["cfg2", "cfg4"], default="cfg2")
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (cfg4: sampler steps per image)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--blocks", type=int, default=BLOCKS, help=argparse.SUPPRESS)
@@ -264,8 +274,54 @@ def time_conv_cfg0(torch, ops, reps=50):
         if i >= 3:
             times.append(e0.elapsed_time(e1))
     ms = statistics.median(times)
+    # Back-to-back launches replayed from one CUDA graph (one ~11 MB conv is
+    # dominated by launch and fill latency when timed alone).  The launches
+    # rotate over 16 copies of (x, neighbour map, weights, out), 176 MB in
+    # all, more than the 126 MB L2, so each launch reads its inputs from HBM.
+    copies = 16
+    sets = [(x.clone(), nbr.clone(), w.clone(), torch.empty_like(out)) for _ in range(copies)]
+    graph_reps = 3 * copies
+    for xs, ns, ws, os_ in sets:
+        ops.subm_conv3d(xs, ns, ws, b, out=os_)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(graph_reps):
+            xs, ns, ws, os_ = sets[i % copies]
+            ops.subm_conv3d(xs, ns, ws, b, out=os_)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_graph = e0.elapsed_time(e1) / graph_reps
+    del g, sets
     bytes_ = n * 64 * 2 + 27 * 64 * 64 * 2 + 27 * n * 4 + n * 64 * 4
-    return ms, bytes_, 2.0 * pairs * 64 * 64
+    return ms, bytes_, 2.0 * pairs * 64 * 64, ms_graph
+
+
+def cpu_conv_cfg0(reps: int = 5):
+    """The reference's sparse_submanifold_conv3d (oracle/_ref, compiled from
+    the reference sources) on the config-0 shell, 64 -> 64, all host threads:
+    median seconds of `reps` runs, and the thread count."""
+    import numpy as np
+    from oracle import reflib
+    from pixal3d.cpp_b200.workloads import shell_coords
+    threads = os.cpu_count() or 1
+    reflib.set_threads(threads)
+    c = shell_coords()
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((c.shape[0], 64)).astype(np.float32)
+    w = (rng.standard_normal((27, 64, 64)) / math.sqrt(27 * 64)).astype(np.float32)
+    b = np.zeros(64, np.float32)
+    times = []
+    for _ in range(reps + 1):
+        t0 = time.perf_counter()
+        reflib.subm_conv3d(c, x, w, b, 1, (RES, RES, RES))
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times[1:]), threads
 
 
 def cpu_baseline_sample(target_seconds: float = 20.0):
@@ -337,11 +393,8 @@ def cpu_baseline_sample(target_seconds: float = 20.0):
                   "sample_seconds": round(sum(times) + t_slab, 1)}
 
 
-def run_ours(args):
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-
+def init_ranks(torch, dist):
+    """(world, rank, local rank); one process per GPU, NCCL when world > 1."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -358,6 +411,15 @@ def run_ours(args):
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device("cuda", local))
             dist.barrier()
+    return world, rank, local
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = init_ranks(torch, dist)
     from pixal3d.cpp_b200 import dist as D
     from pixal3d.cpp_b200 import ops
     from pixal3d.cpp_b200.flow import FlowModel, HParams
@@ -429,7 +491,7 @@ def run_ours(args):
         if TRAFFIC_FILE.exists():
             mt = re.search(r"traffic_bytes_per_launch\s*=\s*(\d+)", TRAFFIC_FILE.read_text())
             traffic = int(mt.group(1)) if mt else None
-        c0_ms, c0_bytes, c0_flops = time_conv_cfg0(torch, ops)
+        c0_ms, c0_bytes, c0_flops, c0_graph_ms = time_conv_cfg0(torch, ops)
         hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         result = {
             "metric": METRIC, "value": round(value, 3), "unit": "steps/s", "n_gpus": world, "steps": args.steps,
@@ -451,11 +513,16 @@ def run_ours(args):
                          "peak_kind": f"{peak_kind} bf16 burst (f16 dense rate is identical)",
                          "unit": "TFLOP/s", "frac": round(conv_tflops / peak_t, 4), "traffic": traffic,
                          "avg_launch_ms": round(conv_ms, 4), "flops_per_launch": conv_flops},
-            "sparse_conv_cfg0": {"ms": round(c0_ms, 4), "algorithmic_bytes": c0_bytes,
-                                 "achieved_gbs": round(c0_bytes / (c0_ms / 1000.0) / 1e9, 1), "peak_gbs": hbm,
-                                 "frac_hbm": round(c0_bytes / (c0_ms / 1000.0) / 1e9 / hbm, 4),
-                                 "tflops": round(c0_flops / (c0_ms / 1000.0) / 1e12, 2),
-                                 "l2": "flushed (256 MB write) before each launch"},
+            "sparse_conv_cfg0": {"ms_graph": round(c0_graph_ms, 4), "algorithmic_bytes": c0_bytes,
+                                 "achieved_gbs": round(c0_bytes / (c0_graph_ms / 1000.0) / 1e9, 1), "peak_gbs": hbm,
+                                 "frac_hbm": round(c0_bytes / (c0_graph_ms / 1000.0) / 1e9 / hbm, 4),
+                                 "tflops": round(c0_flops / (c0_graph_ms / 1000.0) / 1e12, 2),
+                                 "timing": "ms_graph: 48 back-to-back launches replayed from one CUDA graph, "
+                                           "rotating over 16 input/output copies (176 MB > L2, so inputs come "
+                                           "from HBM); ms_single_flushed: one launch after a 256 MB L2-flush "
+                                           "write, median of 50",
+                                 "ms_single_flushed": round(c0_ms, 4),
+                                 "frac_hbm_single_flushed": round(c0_bytes / (c0_ms / 1000.0) / 1e9 / hbm, 4)},
         }
     # e2e: the public sampler call with HOST buffers (pinned), copies inside
     e2e = None
@@ -464,6 +531,13 @@ def run_ours(args):
     if rank == 0:
         result["e2e"] = e2e
         if world == 1 and not args.no_cpu_baseline:
+            try:
+                cs, thr = cpu_conv_cfg0()
+                result["sparse_conv_cfg0"]["cpu_reference"] = {
+                    "ms": round(cs * 1000.0, 2), "cores": thr, "kind": "reference",
+                    "sample": "sparse_submanifold_conv3d 64->64 on the full config-0 shell, measured (median of 5)"}
+            except Exception as ex:  # reported, not fatal
+                result["sparse_conv_cfg0"]["cpu_reference"] = {"error": str(ex)[:200]}
             try:
                 step_s, det = cpu_baseline_sample()
                 result["cpu_baseline"] = {"value": round(1.0 / step_s, 8), "unit": "steps/s",
@@ -520,6 +594,126 @@ def run_e2e(torch, model, img, cond, args, dev, world, rank):
                         "K sampler steps, D2H latents"}
 
 
+# ------------------------------------------------------- config 4 (images/s)
+
+CFG4_IMAGES = 64
+CFG4_PACK_VOXELS = 400_000  # voxels of one varlen CFG batch (x2 rows with the unconditional copies)
+
+
+def run_cfg4(args):
+    """BASELINE config 4 on this rank's LPT share of the 64 images."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = init_ranks(torch, dist)
+    from pixal3d.cpp_b200 import dist as D
+    from pixal3d.cpp_b200 import ops
+    from pixal3d.cpp_b200.flow import FlowModel, HParams
+    from pixal3d.cpp_b200.workloads import image_shells, pack_cfg, split_packs
+
+    dev = torch.device("cuda", local)
+    shells = image_shells(CFG4_IMAGES, seed=0)
+    sizes = [int(c.shape[0]) for c in shells]
+    plan = D.lpt_assign(sizes, world)
+    packs = split_packs(plan[rank], sizes, CFG4_PACK_VOXELS)
+    hp = HParams(in_channels=CH, out_channels=CH, model_channels=C, cond_channels=C, num_blocks=BLOCKS,
+                 num_heads=HEADS, mlp_ratio=4.0, io_resblocks=2, groups=32, operand_dtype="f16")
+    w = make_weights(torch, dev, seed=1234)  # same seed on every rank: one model
+    model = FlowModel(hp, w, device=local)
+    del w
+    torch.cuda.empty_cache()
+
+    # Host inputs of this rank's images, pinned: each image's own condition
+    # tokens and initial noise, generated from the image index (no broadcast).
+    host = []
+    for pk in packs:
+        coords, offs = pack_cfg([shells[i] for i in pk])
+        conds = [np.random.default_rng(10_000 + i).standard_normal((CTX_TOKENS, C)).astype(np.float16) for i in pk]
+        noise = [np.random.default_rng(20_000 + i).standard_normal((sizes[i], CH)).astype(np.float32) for i in pk]
+        ctx = np.concatenate(conds + [np.zeros((CTX_TOKENS * len(pk), C), np.float16)])
+        host.append({
+            "coords": torch.from_numpy(coords).pin_memory(),
+            "x": torch.from_numpy(np.concatenate(noise)).pin_memory(),
+            "ctx": torch.from_numpy(ctx.view(np.int16)).pin_memory(),
+            "ctx_offsets": [CTX_TOKENS * j for j in range(2 * len(pk) + 1)],
+            "out": torch.empty((int(offs[-1]), CH)).pin_memory(),
+            "images": len(pk),
+        })
+
+    def run_pack(h, steps):
+        d_coords = h["coords"].to(dev, non_blocking=True)
+        d_x = h["x"].to(dev, non_blocking=True)
+        d_ctx = h["ctx"].to(dev, non_blocking=True).view(torch.float16)
+        model.prepare(d_coords, 2 * h["images"], (RES, RES, RES), h["ctx_offsets"])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        model.sample(d_x, d_ctx, steps=steps, guidance_strength=3.0)
+        e1.record()
+        h["out"].copy_(d_x, non_blocking=True)
+        return e0, e1
+
+    # warm-up: the first pack, one step (kernel loading, graph capture)
+    if host:
+        run_pack(host[0], max(1, min(args.warmup, 2)))
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.ctx(local).launches
+    t0.record()
+    sample_events = [run_pack(h, args.steps) for h in host]
+    t1.record()
+    torch.cuda.synchronize()
+    launches = ops.ctx(local).launches - launches0
+    clk = clocks.stop()
+    ms_rank = t0.elapsed_time(t1)
+    sample_ms = [a.elapsed_time(b) for a, b in sample_events]
+    if world > 1:
+        dist.barrier()
+    ms_max = D.max_over_ranks(ms_rank, dev)
+    ms_all = [ms_rank]
+    if world > 1:
+        tt = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
+        got = [torch.zeros_like(tt) for _ in range(world)]
+        dist.all_gather(got, tt)
+        ms_all = [float(g.item()) for g in got]
+    finite = all(bool(torch.isfinite(h["out"]).all()) for h in host)
+    outs = torch.cat([h["out"] for h in host]).to(dev) if host else torch.zeros((0, CH), device=dev)
+    D.gather_rows(outs, dst=0)  # latents to rank 0 (outside the timed region)
+    if rank == 0:
+        h2d = sum(h["coords"].numel() * 4 + h["x"].numel() * 4 + h["ctx"].numel() * 2 for h in host)
+        value = CFG4_IMAGES / (ms_max / 1000.0)
+        result = {
+            "metric": "SLat flow images/s, config 4 (64 ragged images, 25-step CFG sampler each)",
+            "value": round(value, 3), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_total": round(ms_max, 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 operands, f32 accumulate/residual",
+            "data": "synthetic: seeded ragged sphere shells, per-image N(0,1) noise and condition tokens, "
+                    "random-init weights",
+            "config": {"workload": "config4: 64 images, LPT over ranks, varlen CFG packs per rank",
+                       "voxels_total": sum(sizes), "voxels_min": min(sizes), "voxels_max": max(sizes),
+                       "pack_voxels_max": CFG4_PACK_VOXELS, "parallelism": f"dp{world} (images)"},
+            "per_step_ms_rank0": round(sum(sample_ms) / max(1, len(sample_ms) * args.steps), 3),
+            "packs_rank0": len(host), "rank_ms": [round(v, 1) for v in ms_all],
+            "imbalance_measured": round(max(ms_all) / (sum(ms_all) / len(ms_all)), 4),
+            "imbalance_planned_voxels": round(D.imbalance(plan, sizes), 4),
+            "latents_finite_rank0": finite, "gpu_launches_rank0": int(launches), "clocks": clk,
+            "e2e": {"value": round(value, 3), "unit": "images/s", "h2d_bytes_rank0": int(h2d),
+                    "includes": "per pack: H2D coords/noise/conditions from pinned memory, topology prepare, "
+                                "25 sampler steps (one captured step graph per pack shape), D2H latents"},
+        }
+        print(json.dumps(result), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -557,6 +751,16 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.steps is None:
+        args.steps = 25 if args.workload == "cfg4" else 20
+    if args.workload == "cfg4":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "cfg4",
+                              "unavailable": "config 4 has no reference arm: 64 images x 25 steps of the CPU path "
+                                             "would take days (the per-step figure is the config-2 reference arm)"}))
+            return
+        run_cfg4(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

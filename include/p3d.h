@@ -94,14 +94,29 @@ int p3d_copy_to_host(p3d_ctx *ctx, void *dst, const void *src, size_t bytes);
 /* Wait for ctx's stream, then report (and clear) a latched device fault. */
 int p3d_ctx_synchronize(p3d_ctx *ctx);
 
+/* No reference counterpart: a check of the failure path that every
+ * pipeline wait of this library takes.  One device thread waits, through the
+ * same bounded-wait routine the kernels use, on an mbarrier phase; with
+ * complete != 0 another warp completes it, with complete == 0 nothing does
+ * and the wait gives up after limit_ns (at most 5 s).  Synchronizes, writes
+ * out_host[0] = 1 if the wait succeeded (else 0) and out_host[1] = the
+ * wait's duration in ns, and returns p3d_ctx_check's status: P3D_ERR_TIMEOUT
+ * after an expired wait (the flag is then cleared and ctx stays usable). */
+int p3d_wait_selftest(p3d_ctx *ctx, int complete, int64_t limit_ns, int64_t *out_host);
+
 /* ------------------------------------------------------ coordinates/hash */
 
 /* Table slots for n keys (power of two >= 2n).  Keys are uint64, values
  * int32; the caller allocates both arrays of this length. */
 int64_t p3d_coord_hash_capacity(int64_t n);
 
-/* Insert every row of coords into an open-addressing table (warp-cooperative
- * linear probing in HBM, bounded probes).  Replaces the
+/* Insert every row of coords into an open-addressing table in HBM
+ * (warp-cooperative bucketed linear probing: 8 lanes of a warp per key read
+ * a window of 8 slots per step; bounded probes).  Keys pack 16 bits per
+ * field, so batch must lie in [0, 65536) and x, y, z in [-32768, 32768): a
+ * row outside that range latches P3D_ERR_INVALID instead of aliasing
+ * another key, and p3d_neighbor_map27 reports neighbours outside it as
+ * missing.  capacity: a power of two >= max(n, 64).  Replaces the
  * std::unordered_map<Coord,size_t,CoordHash> builds in
  * src/sparse.cpp:1017-1022 and src/slat_decoder.cpp:630-635.  A duplicate
  * coordinate latches P3D_ERR_DUPLICATE (SparseTensorF32::valid,
@@ -131,7 +146,8 @@ int p3d_neighbor_map27_ws(p3d_ctx *ctx, const int32_t *coords, int64_t n, void *
  * >= 0x7F7F7F7F7F7F7F7F when the tensor is valid.  This is the error the
  * reference's sequential scan reports.  feats may be NULL (coordinates
  * only).  ws: p3d_sparse_validate_workspace(n) bytes, 256-byte aligned
- * (unused when coords is NULL). */
+ * (unused when coords is NULL).  With coords, batch above 65536 or an extent
+ * above 32768 is P3D_ERR_UNSUPPORTED (the hash key's field range). */
 size_t p3d_sparse_validate_workspace(int64_t n);
 int p3d_sparse_validate(p3d_ctx *ctx, const int32_t *coords, int64_t n, const float *feats, int channels,
                         int batch, int sx, int sy, int sz, void *ws, size_t ws_bytes, int64_t *first_bad);
@@ -145,9 +161,11 @@ int p3d_sparse_validate(p3d_ctx *ctx, const int32_t *coords, int64_t n, const fl
  * loads the library holds until the process exits; the call makes no
  * cudaMalloc/cudaFree and no allocating library call.
  *   - n above P3D_NBR_STATIC_MAX_POINTS is rejected with P3D_ERR_INVALID.
- *   - The first call on a device looks up the array's address there
- *     (cudaGetSymbolAddress, with ctx's device current); make that first
- *     call before any stream capture.
+ *   - Every call looks up the array's address on ctx's device
+ *     (cudaGetSymbolAddress, with that device current), so the address is
+ *     never stale, even after a device reset.  The first call on a device
+ *     also loads the library's device code there: make that first call
+ *     before any stream capture.
  *   - Every call shares the one array and clears the slots it uses; calls
  *     that overlap on the GPU (other streams, contexts or threads on the
  *     same device) race on it and must be serialised by the caller. */

@@ -35,12 +35,24 @@ F32 = np.float32
 # Coordinates, hashing, neighbour maps
 # --------------------------------------------------------------------------
 
-def pack_keys(coords: np.ndarray) -> np.ndarray:
-    """Pack (b,x,y,z) into one int64 whose integer order is the lexicographic
-    order of the tuple.  Fields must be in [0, 2^15) for b and [-2^15, 2^15)
-    offset-shifted for x/y/z (neighbour probes may reach -1)."""
-    c = coords.astype(np.int64)
-    return (c[:, 0] << 48) | ((c[:, 1] + 32768) << 32) | ((c[:, 2] + 32768) << 16) | (c[:, 3] + 32768)
+def _fits16(c: np.ndarray, margin: int = 0) -> bool:
+    return c.size == 0 or bool(c[:, 0].min() >= 0 and c[:, 0].max() < 2 ** 15 and
+                               c[:, 1:].min() - margin >= -2 ** 15 and c[:, 1:].max() + margin < 2 ** 15)
+
+
+def pack_keys(coords: np.ndarray, wide: bool | None = None) -> np.ndarray:
+    """Keys whose order is the lexicographic order of the (b,x,y,z) rows and
+    which are equal exactly when the rows are (the reference's CoordHash
+    compares full int32 fields, src/sparse.cpp:34-42).  While every field
+    fits 16 bits (b in [0, 2^15), x/y/z in [-2^15, 2^15)) the key is one int64;
+    otherwise (or with wide=True) it is a 32-byte big-endian record of the
+    four fields, slower but exact for any int64 values."""
+    c = np.asarray(coords).astype(np.int64)
+    if wide is None:
+        wide = not _fits16(c)
+    if not wide:
+        return (c[:, 0] << 48) | ((c[:, 1] + 32768) << 32) | ((c[:, 2] + 32768) << 16) | (c[:, 3] + 32768)
+    return np.ascontiguousarray((c + 2 ** 62).astype(">u8")).view("V32").ravel()
 
 
 def neighbor_map27(coords: np.ndarray) -> np.ndarray:
@@ -51,17 +63,19 @@ def neighbor_map27(coords: np.ndarray) -> np.ndarray:
     holding (b, x+kd-1, y+kh-1, z+kw-1), else the sentinel N.
     """
     n = coords.shape[0]
-    keys = pack_keys(coords)
+    c = np.asarray(coords).astype(np.int64)
+    wide = not _fits16(c, margin=1)  # one key form for the points and all probes
+    keys = pack_keys(c, wide)
     order = np.argsort(keys, kind="stable")
     sk = keys[order]
     out = np.full((27, n), n, dtype=np.int32)
     for k in range(27):
         kd, kh, kw = k // 9, (k // 3) % 3, k % 3
-        probe = coords.astype(np.int64).copy()
+        probe = c.copy()
         probe[:, 1] += kd - 1
         probe[:, 2] += kh - 1
         probe[:, 3] += kw - 1
-        pk = pack_keys(probe)
+        pk = pack_keys(probe, wide)
         pos = np.searchsorted(sk, pk)
         pos_c = np.minimum(pos, n - 1)
         hit = (pos < n) & (sk[pos_c] == pk)
@@ -213,9 +227,13 @@ def rope(coords, x, heads, head_dim, fmin=1.0, fbase=10000.0):
     return out.reshape(n, heads * head_dim).astype(F32)
 
 
-def _softmax_attend(q, k, v, scale):
+def _softmax_attend(q, k, v, scale, chunk=4096):
     # q [Lq, hd], k [Lk, hd], v [Lk, vd]: two-pass softmax as
-    # src/sparse.cpp:754-778.
+    # src/sparse.cpp:754-778.  Rows are independent; long query sets run in
+    # chunks of `chunk` rows so the score block stays small.
+    if q.shape[0] > chunk:
+        return np.concatenate([_softmax_attend(q[i:i + chunk], k, v, scale, chunk)
+                               for i in range(0, q.shape[0], chunk)])
     s = (q @ k.T) * F32(scale)
     s = s - s.max(axis=1, keepdims=True)
     p = np.exp(s)

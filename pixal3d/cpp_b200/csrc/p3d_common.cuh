@@ -115,17 +115,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: true when the phase completed, false on timeout (fault latched).
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *fault) {
+// Bounded wait: true when the phase completed, false once limit_ns passed
+// without it (P3D_ERR_TIMEOUT latched in *fault).  Every pipeline wait of the
+// library goes through this routine with kWaitLimitNs; p3d_wait_selftest
+// drives it to expiry with a short limit.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, int *fault, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit_ns) {
             latch_fault(fault, P3D_ERR_TIMEOUT);
             return false;
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *fault) {
+    return mbar_wait_for(bar, parity, fault, kWaitLimitNs);
 }
 // Arrive on `bar` when all cp.async issued so far by this thread complete.
 __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {

@@ -13,6 +13,15 @@ namespace {
 constexpr uint64_t kEmpty = ~0ull;
 constexpr int kMaxProbes = 1 << 16;
 
+// A key holds 16 bits per field: batch in [0, 65536), x/y/z in [-32768,
+// 32768).  Coordinates outside that range would alias another key, so the
+// hash build refuses them (P3D_ERR_INVALID) and lookups of such a neighbour
+// report it missing.
+__device__ __forceinline__ bool key_packable(int b, int x, int y, int z) {
+    return static_cast<unsigned>(b) < 65536u && static_cast<unsigned>(x + 32768) < 65536u &&
+           static_cast<unsigned>(y + 32768) < 65536u && static_cast<unsigned>(z + 32768) < 65536u;
+}
+
 __device__ __forceinline__ uint64_t pack_key(int b, int x, int y, int z) {
     return (static_cast<uint64_t>(static_cast<uint32_t>(b) & 0xFFFFu) << 48) |
            (static_cast<uint64_t>(static_cast<uint32_t>(x + 32768) & 0xFFFFu) << 32) |
@@ -39,28 +48,64 @@ __global__ void fill_i32_kernel(int32_t *p, int64_t n, int32_t v) {
     if (i < n) p[i] = v;
 }
 
-// One thread per row; linear probing with CAS; bounded probe count.
+// Bucketed linear probing, warp-cooperative: the table is read in windows of
+// kTile = 8 consecutive slots (64 bytes of keys), starting at the key's home
+// window and moving to the next window while the current one is full.  An
+// 8-lane tile of a warp handles one key: each lane reads one slot of the
+// window, ballots tell the tile where the key and the empty slots are, and
+// the lowest empty slot is claimed by CAS.  A key therefore sits behind no
+// empty slot of its probe sequence, so a scalar scan from the home window
+// (hash_find) and the cooperative scan (tile_find) agree.
+constexpr int kTile = 8;
+constexpr int kMaxWindows = kMaxProbes / kTile;
+
+__device__ __forceinline__ uint64_t home_slot(uint64_t key, uint64_t mask) {
+    return (mix64(key) & mask) & ~static_cast<uint64_t>(kTile - 1);
+}
+
+// Thread t of the grid is lane (t % 8) of the tile of key t / 8 (a tile never
+// straddles a warp; the grid has 8 n threads, so whole tiles exit together).
 __global__ void hash_insert_kernel(const int4 *__restrict__ coords, int64_t n, uint64_t *keys, int32_t *vals,
                                    uint64_t mask, int *fault) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kTile;
     if (i >= n) return;
+    const int lane = threadIdx.x & 31, l = lane & (kTile - 1);
+    const unsigned tmask = 0xFFu << (lane & ~(kTile - 1));
     const int4 c = coords[i];
-    const uint64_t key = pack_key(c.x, c.y, c.z, c.w);
-    uint64_t slot = mix64(key) & mask;
-    for (int probe = 0; probe < kMaxProbes; ++probe) {
-        const unsigned long long prev =
-            atomicCAS(reinterpret_cast<unsigned long long *>(keys + slot), kEmpty, static_cast<unsigned long long>(key));
-        if (prev == kEmpty) {
-            vals[slot] = static_cast<int32_t>(i);
-            return;
-        }
-        if (prev == key) {
-            latch_fault(fault, P3D_ERR_DUPLICATE);
-            return;
-        }
-        slot = (slot + 1) & mask;
+    if (!key_packable(c.x, c.y, c.z, c.w)) {
+        if (l == 0) latch_fault(fault, P3D_ERR_INVALID);
+        return;
     }
-    latch_fault(fault, P3D_ERR_HASH_FULL);
+    const uint64_t key = pack_key(c.x, c.y, c.z, c.w);
+    uint64_t base = home_slot(key, mask);
+    for (int w = 0; w < kMaxWindows; ++w) {
+        const uint64_t slot = base + l;
+        const uint64_t k = *reinterpret_cast<volatile const uint64_t *>(keys + slot);
+        if (__ballot_sync(tmask, k == key)) {
+            if (l == 0) latch_fault(fault, P3D_ERR_DUPLICATE);
+            return;
+        }
+        unsigned empty = __ballot_sync(tmask, k == kEmpty);
+        while (empty) {
+            const int leader = __ffs(empty) - 1;
+            unsigned long long prev = 0;
+            if (lane == leader)
+                prev = atomicCAS(reinterpret_cast<unsigned long long *>(keys + slot), kEmpty,
+                                 static_cast<unsigned long long>(key));
+            prev = __shfl_sync(tmask, prev, leader);
+            if (prev == kEmpty) {
+                if (lane == leader) vals[slot] = static_cast<int32_t>(i);
+                return;
+            }
+            if (prev == key) {
+                if (lane == leader) latch_fault(fault, P3D_ERR_DUPLICATE);
+                return;
+            }
+            empty &= ~(1u << leader);  // taken by another key meanwhile: next empty slot of the window
+        }
+        base = (base + kTile) & mask;
+    }
+    if (l == 0) latch_fault(fault, P3D_ERR_HASH_FULL);
 }
 
 // Validation insert: every row inserts its key; the slot's value ends as the
@@ -70,8 +115,9 @@ __global__ void validate_insert_kernel(const int4 *__restrict__ coords, int64_t 
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int4 c = coords[i];
+    if (!key_packable(c.x, c.y, c.z, c.w)) return;  // outside every accepted shape: reported as a bounds error
     const uint64_t key = pack_key(c.x, c.y, c.z, c.w);
-    uint64_t slot = mix64(key) & mask;
+    uint64_t slot = home_slot(key, mask);
     for (int probe = 0; probe < kMaxProbes; ++probe) {
         const unsigned long long prev =
             atomicCAS(reinterpret_cast<unsigned long long *>(keys + slot), kEmpty, static_cast<unsigned long long>(key));
@@ -86,7 +132,7 @@ __global__ void validate_insert_kernel(const int4 *__restrict__ coords, int64_t 
 
 __device__ __forceinline__ int32_t hash_find(const uint64_t *__restrict__ keys, const int32_t *__restrict__ vals,
                                              uint64_t mask, uint64_t key, int32_t miss) {
-    uint64_t slot = mix64(key) & mask;
+    uint64_t slot = home_slot(key, mask);
     for (int probe = 0; probe < kMaxProbes; ++probe) {
         const uint64_t k = __ldg(reinterpret_cast<const unsigned long long *>(keys + slot));
         if (k == key) return __ldg(vals + slot);
@@ -96,17 +142,39 @@ __device__ __forceinline__ int32_t hash_find(const uint64_t *__restrict__ keys, 
     return miss;
 }
 
-// Thread per (tap, point): nbr[tap*n + p] = row of (b, x+kd-1, y+kh-1, z+kw-1) or n.
+// Cooperative lookup by the 8-lane tile of the calling lane (all lanes of
+// the tile pass the same key); every lane returns the row or `miss`.
+__device__ __forceinline__ int32_t tile_find(const uint64_t *__restrict__ keys, const int32_t *__restrict__ vals,
+                                             uint64_t mask, uint64_t key, int32_t miss, unsigned tmask, int l) {
+    uint64_t base = home_slot(key, mask);
+    for (int w = 0; w < kMaxWindows; ++w) {
+        const uint64_t k = __ldg(reinterpret_cast<const unsigned long long *>(keys + base + l));
+        const unsigned hit = __ballot_sync(tmask, k == key);
+        if (hit) {
+            const int32_t v = k == key ? __ldg(vals + base + l) : 0;
+            return __shfl_sync(tmask, v, __ffs(hit) - 1);
+        }
+        if (__ballot_sync(tmask, k == kEmpty)) return miss;
+        base = (base + kTile) & mask;
+    }
+    return miss;
+}
+
+// Tile per (tap, point): nbr[tap*n + p] = row of (b, x+kd-1, y+kh-1, z+kw-1) or n.
 __global__ void neighbor_map_kernel(const int4 *__restrict__ coords, int64_t n, const uint64_t *__restrict__ keys,
                                     const int32_t *__restrict__ vals, uint64_t mask, int32_t *__restrict__ nbr) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kTile;
     if (i >= 27 * n) return;
+    const int lane = threadIdx.x & 31, l = lane & (kTile - 1);
+    const unsigned tmask = 0xFFu << (lane & ~(kTile - 1));
     const int tap = static_cast<int>(i / n);
     const int64_t p = i - static_cast<int64_t>(tap) * n;
     const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
     const int4 c = __ldg(coords + p);
-    nbr[i] = hash_find(keys, vals, mask, pack_key(c.x, c.y + kd - 1, c.z + kh - 1, c.w + kw - 1),
-                       static_cast<int32_t>(n));
+    const int x = c.y + kd - 1, y = c.z + kh - 1, z = c.w + kw - 1;
+    int32_t r = static_cast<int32_t>(n);
+    if (key_packable(c.x, x, y, z)) r = tile_find(keys, vals, mask, pack_key(c.x, x, y, z), r, tmask, l);
+    if (l == 0) nbr[i] = r;
 }
 
 // ------------------------------------------------------------------ scans
@@ -369,13 +437,13 @@ extern "C" int p3d_coord_hash_build(p3d_ctx *ctx, const int32_t *coords, int64_t
                                     int64_t capacity) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, coords && keys && vals, "p3d_coord_hash_build: null pointer");
-    P3D_REQUIRE(ctx, capacity > 0 && (capacity & (capacity - 1)) == 0 && capacity >= n,
-                "p3d_coord_hash_build: capacity must be a power of two >= n");
+    P3D_REQUIRE(ctx, capacity >= 64 && (capacity & (capacity - 1)) == 0 && capacity >= n,
+                "p3d_coord_hash_build: capacity must be a power of two >= max(n, 64)");
     P3D_REQUIRE(ctx, n < (int64_t(1) << 31), "p3d_coord_hash_build: too many points");
     fill_u64_kernel<<<blocks_for(capacity, 256), 256, 0, ctx->stream>>>(keys, capacity, kEmpty);
     int rc = check_launch(ctx, "fill_u64");
     if (rc || n == 0) return rc;
-    hash_insert_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(reinterpret_cast<const int4 *>(coords), n, keys,
+    hash_insert_kernel<<<blocks_for(n * kTile, 256), 256, 0, ctx->stream>>>(reinterpret_cast<const int4 *>(coords), n, keys,
                                                                     vals, static_cast<uint64_t>(capacity - 1),
                                                                     ctx->fault);
     return check_launch(ctx, "hash_insert");
@@ -387,8 +455,9 @@ extern "C" int p3d_neighbor_map27(p3d_ctx *ctx, const int32_t *coords, int64_t n
     P3D_REQUIRE(ctx, coords && keys && vals && nbr_out, "p3d_neighbor_map27: null pointer");
     P3D_REQUIRE(ctx, capacity > 0 && (capacity & (capacity - 1)) == 0, "p3d_neighbor_map27: bad capacity");
     P3D_REQUIRE(ctx, n < (int64_t(1) << 31) / 27, "p3d_neighbor_map27: too many points");
+    P3D_REQUIRE(ctx, capacity >= 64, "p3d_neighbor_map27: capacity below 64 slots");
     if (n == 0) return P3D_OK;
-    neighbor_map_kernel<<<blocks_for(27 * n, 256), 256, 0, ctx->stream>>>(
+    neighbor_map_kernel<<<blocks_for(27 * n * kTile, 256), 256, 0, ctx->stream>>>(
         reinterpret_cast<const int4 *>(coords), n, keys, vals, static_cast<uint64_t>(capacity - 1), nbr_out);
     return check_launch(ctx, "neighbor_map");
 }
@@ -442,6 +511,10 @@ extern "C" int p3d_sparse_validate(p3d_ctx *ctx, const int32_t *coords, int64_t 
     P3D_CUDA(ctx, cudaMemsetAsync(first, 0x7F, sizeof(int64_t), ctx->stream));  // 0x7F7F... = no error
     if (n == 0) return P3D_OK;
     if (coords) {
+        // every coordinate inside the shape then packs into a 16-bit-per-field key
+        if (batch > 65536 || sx > 32768 || sy > 32768 || sz > 32768)
+            return set_error(ctx, P3D_ERR_UNSUPPORTED,
+                             "p3d_sparse_validate: batch above 65536 or a spatial extent above 32768");
         P3D_REQUIRE(ctx, ws && (reinterpret_cast<uintptr_t>(ws) & 255) == 0 &&
                              ws_bytes >= p3d_sparse_validate_workspace(n),
                     "p3d_sparse_validate: workspace too small or not 256-byte aligned");

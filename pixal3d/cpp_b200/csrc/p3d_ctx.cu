@@ -96,6 +96,49 @@ extern "C" int p3d_ctx_check(p3d_ctx *ctx) {
     return P3D_OK;
 }
 
+namespace p3d {
+namespace {
+// One thread waits, through the pipelines' bounded-wait routine, on phase 0 of
+// an mbarrier of arrival count 1.  With `complete`, a thread of another warp
+// makes that arrival (the wait succeeds); without it nothing does, so the wait
+// runs out after limit_ns, latches P3D_ERR_TIMEOUT and the kernel returns.
+// out[0] = 1 when the wait succeeded, out[1] = its duration in ns.
+__global__ void wait_selftest_kernel(int complete, uint64_t limit_ns, int *fault, int64_t *out) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 32 && complete) mbar_arrive(&bar);
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer();
+        const bool ok = mbar_wait_for(&bar, 0, fault, limit_ns);
+        out[0] = ok ? 1 : 0;
+        out[1] = static_cast<int64_t>(globaltimer() - t0);
+    }
+}
+}  // namespace
+}  // namespace p3d
+
+extern "C" int p3d_wait_selftest(p3d_ctx *ctx, int complete, int64_t limit_ns, int64_t *out_host) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, out_host && limit_ns > 0 && limit_ns <= 5000000000ll,
+                "p3d_wait_selftest: limit must be in (0, 5 s] and out non-null");
+    DeviceGuard dg(ctx->device);
+    int64_t *d = nullptr;
+    P3D_CUDA(ctx, cudaMalloc(&d, 2 * sizeof(int64_t)));
+    wait_selftest_kernel<<<1, 64, 0, ctx->stream>>>(complete, static_cast<uint64_t>(limit_ns), ctx->fault, d);
+    int rc = check_launch(ctx, "wait_selftest");
+    if (rc == P3D_OK) {
+        cudaError_t e = cudaMemcpyAsync(out_host, d, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        rc = e == cudaSuccess ? p3d_ctx_check(ctx) : set_error(ctx, P3D_ERR_CUDA, cudaGetErrorString(e));
+    }
+    cudaFree(d);
+    return rc;
+}
+
 extern "C" int p3d_convert(p3d_ctx *ctx, const void *x, int x_dtype, int64_t count, void *out, int out_dtype) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, x && out, "p3d_convert: null pointer");

@@ -50,6 +50,8 @@ constexpr int kThreads = 9 * 32;
 constexpr int kThreadsG = 13 * 32;
 constexpr int kGatherThreads = 256;
 constexpr int kMmaWarp = 8;
+// (tile, tap) steps by which the 1-CTA gather loads its row sources ahead.
+constexpr int kSrcAhead = 8;
 
 struct GemmParams {
     const uint16_t *x;  // gather variant: base of x [n][cin] (16-bit elements)
@@ -610,14 +612,25 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
+        // Gather sources run kSrcAhead (tile, tap) steps ahead of their use,
+        // across tile boundaries: with a small cin one tap is one stage, and a
+        // source loaded only one tap ahead would stall every stage on it.
+        int32_t ring[kSrcAhead];
+        int64_t q_next = 0;  // next (tile, tap) step to load: local tile q / 27, tap q % 27
+        auto src_at = [&](int64_t q) -> int32_t {
+            const int64_t tl = blockIdx.x + (q / 27) * gridDim.x;
+            if (tl >= num_tiles) return -1;
+            return gather_src(p, grow, (tl / n_tiles) * BM, static_cast<int>(q % 27));
+        };
+        if (GATHER) {
+#pragma unroll
+            for (int j = 0; j < kSrcAhead; ++j) ring[j] = src_at(q_next++);
+        }
         for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
             const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
-            int32_t cur_src = 0, next_src = 0;
-            if (GATHER) {
-                cur_src = gather_src(p, grow, m0, 0);
-                next_src = gather_src(p, grow, m0, 1);
-            }
+            (void)m0;
+            int32_t cur_src = GATHER ? ring[0] : 0;
             for (int kb = 0; kb < num_kb; ++kb) {
                 if (GATHER) {
                     if (!warp_wait<false>(&empty_bar[stage], phase ^ 1, p.fault)) {
@@ -635,9 +648,11 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
                 if (GATHER) {
                     const int tap = kb / kblocks_per_tap;
                     const int kc = (kb % kblocks_per_tap) * BK;
-                    if (kc == 0 && tap > 0) {
-                        cur_src = next_src;
-                        next_src = gather_src(p, grow, m0, tap + 1);
+                    if (kc == 0) {
+                        cur_src = ring[0];
+#pragma unroll
+                        for (int j = 0; j + 1 < kSrcAhead; ++j) ring[j] = ring[j + 1];
+                        ring[kSrcAhead - 1] = src_at(q_next++);
                     }
                     gather_stage_a16(p, sa, pw, lane, cur_src, kc);
                     if (warp == 0 && lane == 0) {

@@ -3,11 +3,12 @@
 //
 // The table (keys then values, the layout p3d_neighbor_map27_ws carves out
 // of caller scratch) lives in g_nbr_table, which every GPU that loads the
-// library holds until the process exits.  Its device address is looked up
-// once per device with cudaGetSymbolAddress, by the first call on that
-// device, with that device current.
-#include <mutex>
-
+// library holds until the process exits.  Host code cannot use the symbol
+// itself as a device address, so every call asks the runtime for the
+// array's address on ctx's device (cudaGetSymbolAddress, with that device
+// current).  Nothing is cached: after a device reset the next call gets the
+// address in the new context.  The first call on a device also loads the
+// module there, which is why that call must come before any stream capture.
 #include "p3d_common.cuh"
 
 namespace {
@@ -18,31 +19,22 @@ namespace {
 constexpr int64_t kSlots = int64_t(1) << 20;
 constexpr int64_t kMaxPoints = kSlots / 2;
 static_assert(kMaxPoints == P3D_NBR_STATIC_MAX_POINTS, "static table size and header limit disagree");
-constexpr int kMaxDevices = 64;
 
 // [kSlots] uint64 keys, then [kSlots] int32 values (kSlots/2 uint64 words).
 static __device__ __align__(256) uint64_t g_nbr_table[kSlots + kSlots / 2];
 
-std::mutex g_setup_mutex;
-void *g_table_ptr[kMaxDevices] = {};
-
-// Device address of g_nbr_table on ctx->device; looked up on first use.
+// Device address of g_nbr_table on ctx->device.
 int table_address(p3d_ctx *ctx, void **out) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_table_ptr[ctx->device]) {
-        int prev = -1;
-        P3D_CUDA(ctx, cudaGetDevice(&prev));
-        if (prev != ctx->device) P3D_CUDA(ctx, cudaSetDevice(ctx->device));
-        void *ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_nbr_table);
-        if (prev != ctx->device) cudaSetDevice(prev);
-        if (e != cudaSuccess)
-            return p3d::set_error(ctx, P3D_ERR_CUDA,
-                                  std::string("p3d_neighbor_map27_static: cudaGetSymbolAddress: ") +
-                                      cudaGetErrorString(e));
-        g_table_ptr[ctx->device] = ptr;
-    }
-    *out = g_table_ptr[ctx->device];
+    int prev = -1;
+    P3D_CUDA(ctx, cudaGetDevice(&prev));
+    if (prev != ctx->device) P3D_CUDA(ctx, cudaSetDevice(ctx->device));
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_nbr_table);
+    if (prev != ctx->device) cudaSetDevice(prev);
+    if (e != cudaSuccess)
+        return p3d::set_error(ctx, P3D_ERR_CUDA,
+                              std::string("p3d_neighbor_map27_static: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    *out = ptr;
     return P3D_OK;
 }
 
@@ -57,7 +49,6 @@ extern "C" int p3d_neighbor_map27_static(p3d_ctx *ctx, const int32_t *coords, in
                               "p3d_neighbor_map27_static: " + std::to_string(n) +
                                   " points exceed the static table's maximum of " + std::to_string(kMaxPoints) +
                                   " (use p3d_neighbor_map27_ws with caller scratch)");
-    P3D_REQUIRE(ctx, ctx->device >= 0 && ctx->device < kMaxDevices, "p3d_neighbor_map27_static: device index");
     void *table = nullptr;
     int rc = table_address(ctx, &table);
     if (rc) return rc;

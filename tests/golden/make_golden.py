@@ -2,7 +2,7 @@
 
 Run where the reference checkout is mounted (it is not on the GPU box):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <Pixal3D.cpp checkout>   (or $P3D_REFERENCE)
 
 1. Builds the reference CPU path and its deterministic numeric fixtures with
    oracle/Makefile (sources compiled where they lie; outputs in oracle/_ref/).
@@ -11,6 +11,15 @@ Run where the reference checkout is mounted (it is not on the GPU box):
 3. Calls the compiled reference through oracle/reflib.py on small seeded
    inputs and stores inputs + outputs in ref_vectors.npz (sparse path) and
    projection_vectors.npz (projection conditioning).
+
+    python tests/golden/make_golden.py --only configs
+
+4. Runs the numpy oracle (oracle/oracle.py, pinned to the reference by
+   tests/test_oracle_pin.py) on the BASELINE configurations at full size
+   (tests/_configs.py: config-1 block at N=21,766, one config-2 forward at
+   N=2 x 21,766 with 24 blocks) and stores the outputs with fingerprints of
+   the seeded inputs in cfg1_block.npz and cfg2_forward.npz.  Needs no
+   reference checkout; takes a few minutes of CPU.
 """
 from __future__ import annotations
 
@@ -151,12 +160,34 @@ def projection_vectors() -> None:
     print("wrote projection_vectors.npz", coords.shape[0], "points")
 
 
+def config_goldens() -> None:
+    import time
+
+    from oracle import oracle as O
+    from tests import _configs as K
+    for name, make in (("cfg1_block", K.cfg1), ("cfg2_forward", K.cfg2)):
+        coords, x, ts, offs, ctx, hp, w = make()
+        t0 = time.perf_counter()
+        out = O.slat_flow_forward(coords, x, ts, offs, ctx, None, hp, w)
+        dt = time.perf_counter() - t0
+        np.savez_compressed(HERE / f"{name}.npz", out=out.astype(np.float32),
+                            inputs_fp=K.fingerprint(coords, x, ts, ctx), weights_fp=K.weights_fingerprint(w),
+                            oracle_seconds=np.float64(dt))
+        print(f"wrote {name}.npz: out {out.shape}, oracle {dt:.1f} s")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("P3D_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["fixtures", "ref_vectors", "projection"], default=None,
+    ap.add_argument("--ref", default=os.environ.get("P3D_REFERENCE"),
+                    help="Pixal3D.cpp checkout (default $P3D_REFERENCE)")
+    ap.add_argument("--only", choices=["fixtures", "ref_vectors", "projection", "configs"], default=None,
                     help="regenerate one group only")
     a = ap.parse_args()
+    if a.only == "configs":
+        config_goldens()
+        return
+    if not a.ref:
+        ap.error("no reference checkout: pass --ref <path> or set P3D_REFERENCE")
     build(a.ref)
     if a.only in (None, "fixtures"):
         run_fixtures()
@@ -164,6 +195,8 @@ def main() -> None:
         ref_vectors()
     if a.only in (None, "projection"):
         projection_vectors()
+    if a.only is None:
+        config_goldens()
 
 
 if __name__ == "__main__":

@@ -105,6 +105,25 @@ def test_neighbor_map_edge_cases():
     assert e.value.status == L().P3D_ERR_DUPLICATE
 
 
+def test_neighbor_map_key_range():
+    """The hash key holds 16 bits per field.  At the edges of that range the
+    map still equals the (full-width) oracle: the x+1 probe of x = 32767 is
+    missing, not an alias of x = -32768.  A coordinate outside the range is
+    refused (P3D_ERR_INVALID) rather than aliased."""
+    o = ops()
+    edge = np.array([[0, -32768, 0, 0], [0, -32767, 0, 0], [0, 32766, 5, 5], [0, 32767, 0, 0],
+                     [65535, 0, 32767, -32768]], np.int32)
+    got = o.neighbor_map27(dev(edge)).cpu().numpy()
+    o.ctx().sync_check()
+    np.testing.assert_array_equal(got, O.neighbor_map27(edge))
+    assert got[2 * 9 + 4, 3] == edge.shape[0]  # (x+1) of x = 32767
+    for bad in ([[0, 32768, 0, 0]], [[65536, 0, 0, 0]], [[-1, 0, 0, 0]], [[0, 0, -32769, 0]]):
+        o.neighbor_map27(dev(np.array(bad, np.int32)))
+        with pytest.raises(L().P3DError) as e:
+            o.ctx().sync_check()
+        assert e.value.status == L().P3D_ERR_INVALID, bad
+
+
 def test_sparse_validate_matches_reference_order():
     """Device validity probe == the reference's sequential scan (first failing
     row and check) on crafted cases and on the config-0 shell with failures
