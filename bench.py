@@ -79,7 +79,7 @@ class _stdout_to_stderr:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--workload", choices=["cfg2", "cfg4"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4"], default="cfg2")
     ap.add_argument("--steps", type=int, default=None, help="timed steps (cfg4: sampler steps per image)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -221,11 +221,7 @@ def time_conv_kernel(torch, ops, coords_dev, reps=10):
     the launching stream, as the flow runs it: rows of each batch item in
     neighbour-pattern order, taps no row of a 256-row tile uses skipped."""
     n = coords_dev.shape[0]
-    nbr = ops.neighbor_map27(coords_dev)
-    bits = torch.arange(27, device=nbr.device, dtype=torch.int64)
-    pattern = ((nbr < n).to(torch.int64) << bits[:, None]).sum(0)
-    key = (coords_dev[:, 0].to(torch.int64) << 32) | pattern
-    order = torch.sort(key, stable=True).indices
+    order = ops.conv_row_order(coords_dev, ops.neighbor_map27(coords_dev), 2).long()
     nbr = ops.neighbor_map27(coords_dev[order].contiguous())
     taps = ops.conv_tile_taps(nbr)
     pairs = int((nbr < n).sum().item())
@@ -594,6 +590,130 @@ def run_e2e(torch, model, img, cond, args, dev, world, rank):
                         "K sampler steps, D2H latents"}
 
 
+# ------------------------------------------------------- config 1 (one block)
+
+def cfg1_flops(n: int) -> dict:
+    """Algorithmic FLOPs of one config-1 block at n tokens (batch 1)."""
+    lin = 2 * n * C * C * (3 + 1 + 1 + 1 + 4 + 4)
+    kv = 2 * CTX_TOKENS * C * 2 * C
+    self_attn = 4 * n * n * C
+    cross = 4 * n * CTX_TOKENS * C
+    return {"block": lin + kv + self_attn + cross, "linear": lin + kv, "self_attention": self_attn,
+            "cross_attention": cross}
+
+
+def run_cfg1(args):
+    """One config-1 sparse transformer block (N = 21,766 tokens of 1,024
+    channels, 16 heads, sinusoidal absolute PE, 1,029 condition tokens,
+    t = 0.5) through the flow forward (identity input linear, final LayerNorm
+    and a 1024 -> 8 output linear around the block): ms per forward."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = init_ranks(torch, dist)
+    from pixal3d.cpp_b200 import dist as D
+    from pixal3d.cpp_b200 import ops
+    from pixal3d.cpp_b200.flow import FlowModel, HParams
+    from pixal3d.cpp_b200.workloads import shell_coords
+    global BLOCKS_RUN
+    BLOCKS_RUN = 1
+    dev = torch.device("cuda", local)
+    coords = torch.from_numpy(shell_coords()).to(dev)
+    n = coords.shape[0]
+    w = make_weights(torch, dev, seed=1234)
+    w["input_weight"] = torch.eye(C, device=dev)
+    w["input_bias"] = torch.zeros(C, device=dev)
+    hp = HParams(in_channels=C, out_channels=CH, model_channels=C, cond_channels=C, num_blocks=1, num_heads=HEADS,
+                 mlp_ratio=4.0, pe_mode="ape", operand_dtype="f16")
+    model = FlowModel(hp, w, device=local)
+    del w
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    x = torch.randn((n, C), device=dev, generator=g)
+    cond = torch.randn((CTX_TOKENS, C), device=dev, generator=g).to(torch.float16)
+    ts = torch.full((1,), 500.0, device=dev)
+    model.prepare(coords, 1, (RES, RES, RES), [0, CTX_TOKENS])
+    out = torch.empty((n, CH), device=dev)
+    for _ in range(max(args.warmup, 1)):
+        model.forward(x, ts, cond, out=out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.ctx(local).launches
+    e0.record()
+    for _ in range(args.steps):
+        model.forward(x, ts, cond, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ops.ctx(local).launches - launches0
+    ms = D.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    fl = cfg1_flops(n)
+    peaks, kind = load_peaks()
+    if rank == 0:
+        tf = fl["block"] / (ms / 1000.0) / 1e12
+        print(json.dumps({
+            "metric": "config-1 sparse transformer block forward (N=21,766, C=1024)", "value": round(ms, 3),
+            "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "weak", "dtype": "f16 operands, f32 accumulate/residual",
+            "data": "synthetic: config-0 shell coords, N(0,1) tokens and condition, random-init weights",
+            "config": {"workload": "config1: one block, batch 1, N=21,766, 16 heads x 64, APE, 1,029 condition "
+                                   "tokens; identity input linear, final LayerNorm and 1024->8 output linear",
+                       "parallelism": f"replicas x{world}"},
+            "block_tflop": round(fl["block"] / 1e12, 4), "achieved_tflops": round(tf, 1),
+            "frac_of_bf16_burst": round(tf / peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), 4),
+            "gpu_launches": int(launches), "flops_split_tflop": {k: round(v / 1e12, 4) for k, v in fl.items()}}),
+            flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_cfg1(args):
+    """The reference's sparse_transformer_cross_block_f32 (oracle/_ref,
+    compiled from the reference sources) once at the config-1 shape on all
+    host threads.  Its self-attention is a serial loop, so one run takes on
+    the order of 15-20 minutes."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import numpy as np
+    from oracle import reflib, oracle as O
+    from pixal3d.cpp_b200.workloads import shell_coords
+    if not reflib.available():
+        print(json.dumps({"impl": "reference", "workload": "cfg1", "unavailable": "oracle/_ref not built"}))
+        return
+    threads = os.cpu_count() or 1
+    reflib.set_threads(threads)
+    rng = np.random.default_rng(0)
+    coords = shell_coords()
+    n = coords.shape[0]
+    cfg = O.BlockConfig(channels=C, num_heads=HEADS, mlp_hidden=4 * C, context_channels=C)
+    w = {"modulation": (rng.standard_normal(6 * C) * 0.1).astype(np.float32)}
+    for f, shp in [("self_to_qkv_weight", (3 * C, C)), ("self_to_out_weight", (C, C)), ("cross_to_q_weight", (C, C)),
+                   ("cross_to_kv_weight", (2 * C, C)), ("cross_to_out_weight", (C, C)), ("mlp0_weight", (4 * C, C)),
+                   ("mlp2_weight", (C, 4 * C))]:
+        w[f] = (rng.standard_normal(shp) * 0.02).astype(np.float32)
+        w[f.replace("weight", "bias")] = np.zeros(shp[0], np.float32)
+    for f in ("self_q_gamma", "self_k_gamma", "norm2_weight", "cross_q_gamma", "cross_k_gamma"):
+        w[f] = np.ones(C, np.float32)
+    w["norm2_bias"] = np.zeros(C, np.float32)
+    x = rng.standard_normal((n, C)).astype(np.float32)
+    ctx = rng.standard_normal((CTX_TOKENS, C)).astype(np.float32)
+    tmod = (rng.standard_normal((1, 6 * C)) * 0.1).astype(np.float32)
+    t0 = time.perf_counter()
+    out = reflib.transformer_block(coords, x, tmod, np.array([0, CTX_TOKENS], np.int64), ctx, None, cfg, w, 1,
+                                   (RES, RES, RES))
+    sec = time.perf_counter() - t0
+    fl = cfg1_flops(n)
+    print(json.dumps({"impl": "reference", "metric": "config-1 sparse transformer block forward (N=21,766, C=1024)",
+                      "value": round(sec * 1000.0, 1), "unit": "ms", "higher_is_better": False, "dtype": "f32",
+                      "cpu_baseline": {"value": round(sec * 1000.0, 1), "unit": "ms", "cores": threads,
+                                       "kind": "reference", "sample": "one full config-1 block, measured once"},
+                      "achieved_gflops": round(fl["block"] / sec / 1e9, 2), "finite": bool(np.isfinite(out).all()),
+                      "e2e": {"value": round(sec * 1000.0, 1), "unit": "ms", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
 # ------------------------------------------------------- config 4 (images/s)
 
 CFG4_IMAGES = 64
@@ -753,6 +873,9 @@ def main():
     args = parse()
     if args.steps is None:
         args.steps = 25 if args.workload == "cfg4" else 20
+    if args.workload == "cfg1":
+        (run_reference_cfg1 if args.impl == "reference" else run_cfg1)(args)
+        return
     if args.workload == "cfg4":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "workload": "cfg4",

@@ -5,6 +5,8 @@
 // All of it is integer-exact: the neighbour map, the downsampled coordinate
 // order and the subdivided coordinate order are bit-identical to the
 // reference (src/slat_decoder.cpp:670-714, src/sparse.cpp:536-702).
+#include <cub/device/device_radix_sort.cuh>
+
 #include "p3d_common.cuh"
 
 namespace p3d {
@@ -422,10 +424,72 @@ __global__ void batch_offsets_kernel(const int4 *__restrict__ coords, int64_t n,
     off[b] = static_cast<int32_t>(b == batch ? n : lo);
 }
 
+// Sort key of a fine-level row: (batch, neighbour pattern), pattern bit t
+// set when nbr[t][row] is a point.
+__global__ void row_pattern_key_kernel(const int4 *__restrict__ coords, const int32_t *__restrict__ nbr, int64_t n,
+                                       uint64_t *__restrict__ keys, int32_t *__restrict__ idx) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t m = 0;
+    for (int t = 0; t < 27; ++t) {
+        const int32_t s = __ldg(nbr + static_cast<int64_t>(t) * n + i);
+        if (s >= 0 && s < n) m |= 1u << t;
+    }
+    keys[i] = (static_cast<uint64_t>(static_cast<uint32_t>(__ldg(&coords[i].x))) << 27) | m;
+    idx[i] = static_cast<int32_t>(i);
+}
+
+int row_order_end_bit(int batch) {
+    int bits = 1;
+    while ((int64_t(1) << bits) < batch) ++bits;
+    return 27 + bits;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+size_t row_order_temp_bytes(int64_t n, int batch) {
+    size_t temp = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, temp, static_cast<const uint64_t *>(nullptr),
+                                    static_cast<uint64_t *>(nullptr), static_cast<const int32_t *>(nullptr),
+                                    static_cast<int32_t *>(nullptr), static_cast<int>(n), 0, row_order_end_bit(batch));
+    return temp;
+}
+
 }  // namespace
 }  // namespace p3d
 
 using namespace p3d;
+
+extern "C" size_t p3d_conv_row_order_workspace(int64_t n, int batch) {
+    if (n < 0 || batch <= 0 || n >= (int64_t(1) << 31)) return 0;
+    return align256(sizeof(uint64_t) * n) * 2 + align256(sizeof(int32_t) * n) + align256(row_order_temp_bytes(n, batch)) +
+           256;
+}
+
+extern "C" int p3d_conv_row_order(p3d_ctx *ctx, const int32_t *coords, const int32_t *nbr, int64_t n, int batch,
+                                  void *ws, size_t ws_bytes, int32_t *perm) {
+    if (!ctx) return P3D_ERR_INVALID;
+    P3D_REQUIRE(ctx, coords && nbr && perm && ws && batch > 0 && n >= 0 && n < (int64_t(1) << 31),
+                "p3d_conv_row_order: bad argument");
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(coords) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+                "p3d_conv_row_order: coords must be 16-byte and ws 256-byte aligned");
+    P3D_REQUIRE(ctx, ws_bytes >= p3d_conv_row_order_workspace(n, batch), "p3d_conv_row_order: workspace too small");
+    if (n == 0) return P3D_OK;
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    uint64_t *keys_in = reinterpret_cast<uint64_t *>(w);
+    uint64_t *keys_out = reinterpret_cast<uint64_t *>(w + align256(sizeof(uint64_t) * n));
+    int32_t *idx = reinterpret_cast<int32_t *>(w + 2 * align256(sizeof(uint64_t) * n));
+    void *temp = w + 2 * align256(sizeof(uint64_t) * n) + align256(sizeof(int32_t) * n);
+    size_t temp_bytes = row_order_temp_bytes(n, batch);
+    row_pattern_key_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(reinterpret_cast<const int4 *>(coords), nbr, n,
+                                                                        keys_in, idx);
+    int rc = check_launch(ctx, "row_pattern_key");
+    if (rc) return rc;
+    const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx, perm,
+                                                          static_cast<int>(n), 0, row_order_end_bit(batch), ctx->stream);
+    if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("p3d_conv_row_order: ") + cudaGetErrorString(e));
+    return check_launch(ctx, "row_order_sort");
+}
 
 extern "C" int64_t p3d_coord_hash_capacity(int64_t n) {
     int64_t cap = 64;

@@ -156,16 +156,42 @@ int pad16(p3d_ctx *ctx, const float *x, int64_t n, int in, int in_pad, void *out
     return check_launch(ctx, "pad16");
 }
 
-// Neighbour pattern of each row: bit t set when nbr[t][row] is a point.
-__global__ void row_taps_kernel(const int32_t *__restrict__ nbr, int64_t n, uint32_t *__restrict__ taps) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (row >= n) return;
-    uint32_t m = 0;
-    for (int t = 0; t < 27; ++t) {
-        const int32_t s = nbr[static_cast<int64_t>(t) * n + row];
-        if (s >= 0 && s < n) m |= 1u << t;
+// Prepare-time checks and offsets, written into one int32 summary so that
+// prepare reads everything it needs back with a single copy:
+//   [0] batch-order fault (1 when some row's batch is outside [0, batch) or
+//       decreases), [1] the context's device fault flag,
+//   [2, 2 + B]  fine-level batch offsets, [3 + B, 3 + 2B] trunk offsets,
+//   [4 + 2B] trunk rows.
+__global__ void check_batch_kernel(const int4 *__restrict__ coords, int64_t n, int batch, int32_t *summary) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int b = coords[i].x;
+    if (b < 0 || b >= batch || (i > 0 && coords[i - 1].x > b)) summary[0] = 1;
+}
+
+// off[b] = first row of batch item b among the *m rows (sorted by batch);
+// off[batch] = *m, also written to *m_out.
+__global__ void offsets_dev_kernel(const int4 *__restrict__ coords, const int64_t *m, int batch, int32_t *off,
+                                   int32_t *m_out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b > batch) return;
+    const int64_t n = *m;
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (coords[mid].x < b) lo = mid + 1; else hi = mid;
     }
-    taps[row] = m;
+    off[b] = static_cast<int32_t>(b == batch ? n : lo);
+    if (b == batch && m_out) *m_out = static_cast<int32_t>(n);
+}
+
+__global__ void copy_fault_kernel(const int *fault, int32_t *dst) { *dst = *fault; }
+
+// coords_out[i] = coords_in[perm[i]]
+__global__ void gather_coords_kernel(const int4 *__restrict__ in, const int32_t *__restrict__ perm, int64_t n,
+                                     int4 *__restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = in[perm[i]];
 }
 
 // out[rows[i]][c] = y[i][c]: fine rows back to the caller's order.
@@ -175,15 +201,6 @@ __global__ void scatter_rows_kernel(const float *__restrict__ y, const int32_t *
     if (i >= n * C) return;
     const int64_t r = i / C;
     out[static_cast<int64_t>(rows[r]) * C + (i - r * C)] = y[i];
-}
-
-// P3D_CONV_SORT=0 keeps the fine level in the caller's row order.
-bool conv_sort_enabled() {
-    static const bool on = [] {
-        const char *e = std::getenv("P3D_CONV_SORT");
-        return !(e && e[0] == '0');
-    }();
-    return on;
 }
 
 // Sinusoidal absolute 3D PE added to h (no reference; benchmark config 1/2):
@@ -332,7 +349,9 @@ struct p3d_flow {
     // fine level in neighbour-pattern order: fine row i is the caller's row
     // perm[i] (null: caller order); conv taps per 256-row tile
     int32_t *perm = nullptr;
-    uint32_t *row_taps = nullptr, *fine_taps = nullptr;
+    uint32_t *fine_taps = nullptr;
+    int32_t *summary = nullptr;  // prepare's device-side checks and offsets (check_batch_kernel)
+    int32_t *order_ws = nullptr;  // p3d_conv_row_order scratch (pooled)
     float *out_tmp = nullptr;
     // workspaces
     float *h = nullptr, *hf = nullptr, *ftmp = nullptr, *tfreq = nullptr, *temb = nullptr, *temb2 = nullptr,
@@ -571,7 +590,8 @@ void p3d_flow::reset_topology() {
     prepared = false;
     n = nt = T = max_fine = max_trunk = max_ctx = 0;
     coords = trunk_coords = fine_off = trunk_off = ctx_off = nbr = parent = child = perm = nullptr;
-    row_taps = fine_taps = nullptr;
+    fine_taps = nullptr;
+    summary = order_ws = nullptr;
     out_tmp = nullptr;
     h = hf = ftmp = tfreq = temb = temb2 = tmod = mods = x_model = vel = sched = ts = x_state = proj_model = nullptr;
     xn = qkv = attn = mlp = kv = cq = ctx_bf = proj_bf = x_in = fbf = nullptr;
@@ -748,21 +768,9 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     const int C = f->C;
     f->batch = batch;
     f->n = n;
-    // host copies of coords -> batch offsets (rows contiguous by batch)
-    std::vector<int32_t> hc(static_cast<size_t>(n) * 4);
-    P3D_CUDA(ctx, cudaMemcpyAsync(hc.data(), coords, sizeof(int32_t) * hc.size(), cudaMemcpyDeviceToHost, ctx->stream));
-    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    std::vector<int32_t> off(batch + 1, 0);
-    for (int64_t i = 0; i < n; ++i) {
-        const int b = hc[i * 4];
-        if (b < 0 || b >= batch || (i > 0 && hc[(i - 1) * 4] > b))
-            return set_error(ctx, P3D_ERR_INVALID, "sparse coordinates must be contiguous by batch");
-        off[b + 1]++;
-    }
-    for (int b = 0; b < batch; ++b) {
-        off[b + 1] += off[b];
-        f->max_fine = std::max<int64_t>(f->max_fine, off[b + 1] - off[b]);
-    }
+    // Topology on the device; one copy of `summary` brings back what the host
+    // needs (the batch check, the fault flag, batch offsets, trunk size): one
+    // synchronisation per prepare.
     std::vector<int32_t> coff(batch + 1);
     for (int b = 0; b <= batch; ++b) coff[b] = static_cast<int32_t>(ctx_offsets_host[b]);
     for (int b = 0; b < batch; ++b) {
@@ -770,59 +778,42 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         f->max_ctx = std::max<int64_t>(f->max_ctx, coff[b + 1] - coff[b]);
     }
     f->T = coff[batch];
-    f->h_fine_off = off;
     f->h_ctx_off = coff;
-    P3D_TRY(f->alloc(&f->coords, n * 4));
-    P3D_CUDA(ctx, cudaMemcpyAsync(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(coords) & 15) == 0, "p3d_flow_prepare: coords must be 16-byte aligned");
+    const int64_t nsum = 2 * static_cast<int64_t>(batch) + 5;
+    P3D_TRY(f->alloc(&f->summary, nsum));
+    P3D_CUDA(ctx, cudaMemsetAsync(f->summary, 0, sizeof(int32_t) * nsum, ctx->stream));
+    const int4 *cin = reinterpret_cast<const int4 *>(coords);
+    check_batch_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(cin, n, batch, f->summary);
+    P3D_TRY(check_launch(ctx, "check_batch"));
     P3D_TRY(f->alloc(&f->fine_off, batch + 1));
-    P3D_CUDA(ctx, cudaMemcpyAsync(f->fine_off, off.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
-                                  ctx->stream));
+    P3D_TRY(p3d_batch_offsets(ctx, coords, n, batch, f->fine_off));
     P3D_TRY(f->alloc(&f->ctx_off, batch + 1));
     P3D_CUDA(ctx, cudaMemcpyAsync(f->ctx_off, coff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
                                   ctx->stream));
+    P3D_TRY(f->alloc(&f->coords, n * 4));
     const bool io = hp.io_resblocks > 0;
     if (io) {
-        // fine-level neighbour map and 2x downsample topology
+        // Fine level: rows of each batch item stably sorted by neighbour
+        // pattern (device radix sort), so a 256-row conv tile shares its
+        // missing taps and the conv skips them; the input rows are gathered
+        // through perm and the output rows scattered back.
         P3D_TRY(f->alloc(&f->nbr, 27 * n));
         const size_t wsb = p3d_neighbor_map27_workspace(n);
         P3D_TRY(f->alloc(&f->hash_ws, static_cast<int64_t>((wsb + 3) / 4)));
+        P3D_TRY(p3d_neighbor_map27_ws(ctx, coords, n, f->hash_ws, wsb, f->nbr));
+        const size_t owb = p3d_conv_row_order_workspace(n, batch);
+        P3D_TRY(f->alloc(&f->order_ws, static_cast<int64_t>((owb + 3) / 4)));
+        P3D_TRY(f->alloc(&f->perm, n));
+        P3D_TRY(p3d_conv_row_order(ctx, coords, f->nbr, n, batch, f->order_ws, owb, f->perm));
+        gather_coords_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(cin, f->perm, n,
+                                                                          reinterpret_cast<int4 *>(f->coords));
+        P3D_TRY(check_launch(ctx, "gather_coords"));
+        P3D_TRY(f->alloc(&f->out_tmp, n * hp.out_channels));
         P3D_TRY(p3d_neighbor_map27_ws(ctx, f->coords, n, f->hash_ws, wsb, f->nbr));
-        if (conv_sort_enabled()) {
-            // Order the fine rows of each batch item by neighbour pattern
-            // (stable), so a 256-row conv tile shares its missing taps and
-            // the conv skips them.  The fine level runs in this order; the
-            // input rows are gathered and the output rows scattered back.
-            P3D_TRY(f->alloc(&f->row_taps, n));
-            row_taps_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(f->nbr, n, f->row_taps);
-            P3D_TRY(check_launch(ctx, "row_taps"));
-            std::vector<uint32_t> hm(static_cast<size_t>(n));
-            P3D_CUDA(ctx, cudaMemcpyAsync(hm.data(), f->row_taps, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost,
-                                          ctx->stream));
-            P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-            std::vector<int32_t> order(static_cast<size_t>(n));
-            for (int64_t i = 0; i < n; ++i) order[i] = static_cast<int32_t>(i);
-            auto key = [&](int32_t i) {
-                return (static_cast<uint64_t>(static_cast<uint32_t>(hc[static_cast<size_t>(i) * 4])) << 32) | hm[i];
-            };
-            std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return key(a) < key(b); });
-            bool identity = true;
-            for (int64_t i = 0; i < n && identity; ++i) identity = order[i] == i;
-            if (!identity) {
-                std::vector<int32_t> hcp(static_cast<size_t>(n) * 4);
-                for (int64_t i = 0; i < n; ++i)
-                    for (int k = 0; k < 4; ++k) hcp[i * 4 + k] = hc[static_cast<size_t>(order[i]) * 4 + k];
-                P3D_CUDA(ctx, cudaMemcpyAsync(f->coords, hcp.data(), sizeof(int32_t) * n * 4, cudaMemcpyHostToDevice,
-                                              ctx->stream));
-                P3D_TRY(f->alloc(&f->perm, n));
-                P3D_CUDA(ctx, cudaMemcpyAsync(f->perm, order.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice,
-                                              ctx->stream));
-                P3D_TRY(f->alloc(&f->out_tmp, n * hp.out_channels));
-                P3D_TRY(p3d_neighbor_map27_ws(ctx, f->coords, n, f->hash_ws, wsb, f->nbr));
-                P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // host vectors above go out of scope
-            }
-        }
         P3D_TRY(f->alloc(&f->fine_taps, (n + 255) / 256));
         P3D_TRY(p3d_conv_tile_taps(ctx, f->nbr, n, f->fine_taps));
+        // 2x downsample topology and the trunk's batch offsets
         const int64_t gints = p3d_downsample_grid_ints(batch, sx, sy, sz, 2);
         P3D_TRY(f->alloc(&f->trunk_coords, n * 4));
         P3D_TRY(f->alloc(&f->parent, n));
@@ -831,25 +822,32 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         P3D_TRY(f->alloc(&f->down_m, 1));
         P3D_TRY(p3d_downsample_topology(ctx, f->coords, n, batch, sx, sy, sz, 2, f->down_grid, f->trunk_coords,
                                         f->parent, f->child, f->down_m));
-        int64_t m = 0;
-        P3D_CUDA(ctx, cudaMemcpyAsync(&m, f->down_m, sizeof(int64_t), cudaMemcpyDeviceToHost, ctx->stream));
-        P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-        P3D_TRY(p3d_ctx_check(ctx));
-        f->nt = m;
-        std::vector<int32_t> tc(static_cast<size_t>(m) * 4);
-        P3D_CUDA(ctx, cudaMemcpyAsync(tc.data(), f->trunk_coords, sizeof(int32_t) * tc.size(), cudaMemcpyDeviceToHost,
-                                      ctx->stream));
-        P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-        std::vector<int32_t> toff(batch + 1, 0);
-        for (int64_t i = 0; i < m; ++i) toff[tc[i * 4] + 1]++;
-        for (int b = 0; b < batch; ++b) {
-            toff[b + 1] += toff[b];
-            f->max_trunk = std::max<int64_t>(f->max_trunk, toff[b + 1] - toff[b]);
-        }
         P3D_TRY(f->alloc(&f->trunk_off, batch + 1));
-        P3D_CUDA(ctx, cudaMemcpyAsync(f->trunk_off, toff.data(), sizeof(int32_t) * (batch + 1), cudaMemcpyHostToDevice,
-                                      ctx->stream));
-        f->h_trunk_off = toff;
+        offsets_dev_kernel<<<blocks_for(batch + 1, 128), 128, 0, ctx->stream>>>(
+            reinterpret_cast<const int4 *>(f->trunk_coords), f->down_m, batch, f->trunk_off, f->summary + 4 + 2 * batch);
+        P3D_TRY(check_launch(ctx, "trunk_offsets"));
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->summary + 3 + batch, f->trunk_off, sizeof(int32_t) * (batch + 1),
+                                      cudaMemcpyDeviceToDevice, ctx->stream));
+    } else {
+        P3D_CUDA(ctx, cudaMemcpyAsync(f->coords, coords, sizeof(int32_t) * n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    P3D_CUDA(ctx, cudaMemcpyAsync(f->summary + 2, f->fine_off, sizeof(int32_t) * (batch + 1), cudaMemcpyDeviceToDevice,
+                                  ctx->stream));
+    copy_fault_kernel<<<1, 1, 0, ctx->stream>>>(ctx->fault, f->summary + 1);
+    P3D_TRY(check_launch(ctx, "copy_fault"));
+    std::vector<int32_t> sum(static_cast<size_t>(nsum));
+    P3D_CUDA(ctx, cudaMemcpyAsync(sum.data(), f->summary, sizeof(int32_t) * nsum, cudaMemcpyDeviceToHost, ctx->stream));
+    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // the one synchronisation of prepare
+    if (sum[1]) return p3d_ctx_check(ctx);  // a topology kernel latched a fault (duplicate, hash, key range)
+    if (sum[0]) return set_error(ctx, P3D_ERR_INVALID, "sparse coordinates must be contiguous by batch");
+    std::vector<int32_t> off(sum.begin() + 2, sum.begin() + 3 + batch);
+    for (int b = 0; b < batch; ++b) f->max_fine = std::max<int64_t>(f->max_fine, off[b + 1] - off[b]);
+    f->h_fine_off = off;
+    if (io) {
+        f->nt = sum[4 + 2 * batch];
+        f->h_trunk_off.assign(sum.begin() + 3 + batch, sum.begin() + 4 + 2 * batch);
+        for (int b = 0; b < batch; ++b)
+            f->max_trunk = std::max<int64_t>(f->max_trunk, f->h_trunk_off[b + 1] - f->h_trunk_off[b]);
         P3D_TRY(f->alloc(&f->hf, n * C));
         P3D_TRY(f->alloc(&f->ftmp, n * C));
         P3D_TRY(f->alloc(&f->fbf, n * C));
@@ -889,9 +887,8 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
         P3D_TRY(f->alloc(&f->rope, nt * 64));
         P3D_TRY(p3d_rope_table(ctx, f->trunk_coords, nt, 64, hp.rope_freq_min, hp.rope_freq_base, f->rope));
     }
-    // The host copies above were issued on ctx->stream; the flow's own stream
-    // must not run ahead of them.
-    P3D_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    // Work issued here runs on ctx->stream; sampling orders the flow's own
+    // stream after it with an event, and forward runs on ctx->stream.
     std::vector<int64_t> shape = {n, f->nt, f->T, batch, f->max_fine, f->max_trunk, f->max_ctx};
     shape.insert(shape.end(), off.begin(), off.end());
     shape.insert(shape.end(), coff.begin(), coff.end());

@@ -50,8 +50,6 @@ constexpr int kThreads = 9 * 32;
 constexpr int kThreadsG = 13 * 32;
 constexpr int kGatherThreads = 256;
 constexpr int kMmaWarp = 8;
-// (tile, tap) steps by which the 1-CTA gather loads its row sources ahead.
-constexpr int kSrcAhead = 8;
 
 struct GemmParams {
     const uint16_t *x;  // gather variant: base of x [n][cin] (16-bit elements)
@@ -505,14 +503,19 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
     }
 }
 
-// Source row of tile row m0 + (t & 127) for tap `tap` (sentinel or out of
-// range -> -1, i.e. zero fill).  Loaded one tap ahead of its use so the
-// gather's issue never waits on this load.
+// Source row of tile row m0 + t for tap `tap`, as stored in the neighbour map
+// (the sentinel M, or any value outside [0, M), means zero fill; a row past
+// the end reads as -1).  The value is returned unchecked: checking it here
+// would make the caller wait for the load, while it is loaded ahead of use
+// and range-checked where the gather consumes it.
 __device__ __forceinline__ int32_t gather_src(const GemmParams &p, int t, int64_t m0, int tap) {
     const int64_t row = m0 + t;
     if (tap >= 27 || row >= p.M) return -1;
-    const int32_t s = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
-    return (s >= p.M || s < 0) ? -1 : s;
+    return __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
+}
+
+__device__ __forceinline__ bool src_valid(const GemmParams &p, int32_t s) {
+    return s >= 0 && static_cast<int64_t>(s) < p.M;
 }
 
 // Residual epilogues read-modify-write the f32 output: pull this lane's row
@@ -537,8 +540,9 @@ __device__ __forceinline__ void gather_stage_a16(const GemmParams &p, uint8_t *s
         const int rr = i * 4 + (lane >> 3);
         const int r = 16 * pw + rr;
         const int32_t src = __shfl_sync(0xffffffffu, my_src, rr);
-        const uint16_t *g = p.x + (src >= 0 ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
-        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, src >= 0 ? 16u : 0u);
+        const bool ok = src_valid(p, src);
+        const uint16_t *g = p.x + (ok ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
+        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, ok ? 16u : 0u);
     }
 }
 
@@ -581,7 +585,7 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full_bar[s], GATHER ? (kGatherThreads + 1) : 1);
+            mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -590,7 +594,7 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
-        if (!GATHER) prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
     if (warp == kMmaWarp) {
@@ -604,71 +608,120 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
 
     if (warp < 4 || (GATHER && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
-        // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) gathers tile
-        // rows [16 pw, 16 pw + 16); lane l < 16 holds row 16 pw + l's source
-        const int t = warp < 4 ? threadIdx.x : 0;  // dense: thread 0 issues the TMA loads
+        // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) issues the steps
+        // s with s % 8 == pw; dense: thread 0 issues every TMA load
+        const int t = warp < 4 ? threadIdx.x : 0;
         const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
-        const int grow = 16 * pw + (lane & 15);
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        // Gather sources run kSrcAhead (tile, tap) steps ahead of their use,
-        // across tile boundaries: with a small cin one tap is one stage, and a
-        // source loaded only one tap ahead would stall every stage on it.
-        int32_t ring[kSrcAhead];
-        int64_t q_next = 0;  // next (tile, tap) step to load: local tile q / 27, tap q % 27
-        auto src_at = [&](int64_t q) -> int32_t {
-            const int64_t tl = blockIdx.x + (q / 27) * gridDim.x;
-            if (tl >= num_tiles) return -1;
-            return gather_src(p, grow, (tl / n_tiles) * BM, static_cast<int>(q % 27));
-        };
-        if (GATHER) {
+        bool return_early = false;  // gather: a producer warp without a stage slot
+        if constexpr (GATHER) {
+            // One producer warp per stage slot: step s = (local tile, tap, K
+            // block) goes to producer warp s % STAGES (warps past STAGES stay
+            // idle), so the fixed cost of a step (the empty wait, the barrier
+            // arrive, the index bookkeeping) of STAGES steps overlaps; with
+            // cin = 64 a step is one 128 x 64 x 64 MMA, far shorter than that
+            // cost.  Each warp owns one slot and walks its rounds in order,
+            // so its parity waits never alias an older phase.  Lane l gathers tile rows
+            // [4 l, 4 l + 4) with one TMA tile::gather4 from x; a source
+            // index outside [0, M) (the sentinel M, or -1 past the last row)
+            // reads TMA's zero fill.  Row indices are loaded two of this
+            // warp's steps (2 * STAGES steps) ahead into two fixed registers.
+            const int64_t local_tiles =
+                blockIdx.x < num_tiles ? (num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+            const int64_t total = local_tiles * num_kb;
+            static_assert(STAGES <= 8, "one producer warp per stage slot");
+            if (pw >= STAGES) return_early = true;
+            struct Pos {
+                int64_t lt;  // local tile
+                int w;       // step within the tile: tap * kblocks_per_tap + K block
+                int64_t m0, n0;
+            };
+            auto place = [&](Pos &ps) {
+                const int64_t tile = blockIdx.x + ps.lt * gridDim.x;
+                ps.m0 = (tile / n_tiles) * BM;
+                ps.n0 = (tile % n_tiles) * BN;
+            };
+            auto advance = [&](Pos &ps) {  // by STAGES steps (num_kb >= 27 > STAGES: at most one wrap)
+                ps.w += STAGES;
+                if (ps.w >= num_kb) {
+                    ps.w -= num_kb;
+                    ++ps.lt;
+                    place(ps);
+                }
+            };
+            auto load4 = [&](const Pos &ps) -> int4 {
+                int r[4];
+                const int64_t tap = ps.w / kblocks_per_tap;
 #pragma unroll
-            for (int j = 0; j < kSrcAhead; ++j) ring[j] = src_at(q_next++);
-        }
-        for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int64_t m0 = (tile / n_tiles) * BM;
-            const int64_t n0 = (tile % n_tiles) * BN;
-            (void)m0;
-            int32_t cur_src = GATHER ? ring[0] : 0;
-            for (int kb = 0; kb < num_kb; ++kb) {
-                if (GATHER) {
-                    if (!warp_wait<false>(&empty_bar[stage], phase ^ 1, p.fault)) {
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t row = ps.m0 + 4 * lane + j;
+                    r[j] = (ps.lt < local_tiles && row < p.M) ? __ldg(p.nbr + tap * p.M + row) : -1;
+                }
+                return make_int4(r[0], r[1], r[2], r[3]);
+            };
+            Pos pc{0, pw, 0, 0};
+            place(pc);
+            Pos pa = pc;
+            const int4 first0 = load4(pa);
+            advance(pa);
+            const int4 first1 = load4(pa);
+            advance(pa);
+            int4 ring0 = first0, ring1 = first1;
+            for (int64_t s0 = pw; s0 < total && ok && !return_early; s0 += 2 * STAGES) {
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int64_t st = s0 + STAGES * u;
+                    if (st >= total || !ok) break;
+                    int4 src;
+                    if (u == 0) {
+                        src = ring0;
+                        ring0 = load4(pa);
+                    } else {
+                        src = ring1;
+                        ring1 = load4(pa);
+                    }
+                    advance(pa);
+                    const int stg = static_cast<int>(st % STAGES);
+                    const uint32_t ph = static_cast<uint32_t>((st / STAGES) & 1);
+                    if (!warp_wait<false>(&empty_bar[stg], ph ^ 1, p.fault)) {
                         ok = false;
                         break;
                     }
-                } else if (t == 0) {
-                    if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.fault)) {
-                        ok = false;
-                        break;
-                    }
+                    uint8_t *sa = smem_a + stg * C::A_BYTES;
+                    uint8_t *sb = smem_b + stg * C::B_BYTES;
+                    const int tap = pc.w / kblocks_per_tap;
+                    const int kc = (pc.w - tap * kblocks_per_tap) * BK;
+                    if (lane == 0) mbar_arrive_expect_tx(&full_bar[stg], C::A_BYTES + C::B_BYTES);
+                    __syncwarp();
+                    tma_gather4(sa + lane * 4 * 128, &tmap_a, &full_bar[stg], kc, src.x, src.y, src.z, src.w);
+                    // Tap t's weights are rows [t*N, (t+1)*N) of the stacked [27*N, K] map.
+                    if (lane == 0)
+                        tma_load_2d(sb, &tmap_b, &full_bar[stg], kc, static_cast<int>(tap * p.N + pc.n0));
+                    advance(pc);
                 }
-                uint8_t *sa = smem_a + stage * C::A_BYTES;
-                uint8_t *sb = smem_b + stage * C::B_BYTES;
-                if (GATHER) {
-                    const int tap = kb / kblocks_per_tap;
-                    const int kc = (kb % kblocks_per_tap) * BK;
-                    if (kc == 0) {
-                        cur_src = ring[0];
-#pragma unroll
-                        for (int j = 0; j + 1 < kSrcAhead; ++j) ring[j] = ring[j + 1];
-                        ring[kSrcAhead - 1] = src_at(q_next++);
+            }
+        } else {
+            for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int64_t m0 = (tile / n_tiles) * BM;
+                const int64_t n0 = (tile % n_tiles) * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (t == 0) {
+                        if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.fault)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t *sa = smem_a + stage * C::A_BYTES;
+                        uint8_t *sb = smem_b + stage * C::B_BYTES;
+                        mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
+                        tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, static_cast<int>(m0));
+                        tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, static_cast<int>(n0));
                     }
-                    gather_stage_a16(p, sa, pw, lane, cur_src, kc);
-                    if (warp == 0 && lane == 0) {
-                        mbar_arrive_expect_tx(&full_bar[stage], C::B_BYTES);
-                        // Tap t's weights are rows [t*N, (t+1)*N) of the stacked [27*N, K] map.
-                        tma_load_2d(sb, &tmap_b, &full_bar[stage], kc, static_cast<int>(tap * p.N + n0));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
                     }
-                    cp_async_mbar_arrive_noinc(&full_bar[stage]);
-                } else if (t == 0) {
-                    mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
-                    tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, static_cast<int>(m0));
-                    tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, static_cast<int>(n0));
-                }
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
                 }
             }
         }
@@ -695,7 +748,6 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    if (GATHER) fence_proxy_async_smem();
                     const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
@@ -772,25 +824,8 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
 // even CTA's `tempty` barrier (count 8).  No TMA multicast.  All waits are
 // bounded; the pair meets at cluster barriers before the first remote
 // arrival and before freeing TMEM.
-// Source rows m0 + 4*lane .. +3 of tap `tap` for the TMA row gather (sentinel
-// or out of range -> row M, read as zeros).
-__device__ __forceinline__ int4 gather_src4(const GemmParams &p, int lane, int64_t m0, int tap) {
-    int r[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int64_t row = m0 + 4 * lane + j;
-        int32_t s = static_cast<int32_t>(p.M);
-        if (tap < 27 && row < p.M) {
-            s = __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
-            if (s >= p.M || s < 0) s = static_cast<int32_t>(p.M);
-        }
-        r[j] = s;
-    }
-    return make_int4(r[0], r[1], r[2], r[3]);
-}
-
-template <int NSUB, bool GATHER, bool TMAG = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? kThreadsG : kThreads, 1)
+template <int NSUB, bool GATHER>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
     gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
     using C = Cfg2<NSUB>;
@@ -823,7 +858,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
     const int num_kb = GATHER ? 27 * kblocks_per_tap : kblocks_per_tap;
     // taps of a pair tile (the centre tap always: every row has itself)
     auto tile_taps = [&](int64_t tile) -> uint32_t {
-        if (!GATHER || TMAG || !p.tile_taps) return 0x7FFFFFFu;
+        if (!GATHER || !p.tile_taps) return 0x7FFFFFFu;
         return (__ldg(p.tile_taps + tile / n_tiles) | (1u << 13)) & 0x7FFFFFFu;
     };
     auto tile_kb = [&](int64_t tile) -> int { return GATHER ? __popc(tile_taps(tile)) * kblocks_per_tap : num_kb; };
@@ -832,7 +867,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
         // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
         // the odd CTA's forwarded gather completion); odd CTA (gather): its
         // 128 row-gather threads, forwarded by its warp 8.
-        const uint32_t full_count = (GATHER && !TMAG) ? (rank == 0 ? kGatherThreads + 2 : kGatherThreads) : 1;
+        const uint32_t full_count = GATHER ? (rank == 0 ? kGatherThreads + 2 : kGatherThreads) : 1;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full_bar[s], full_count);
             mbar_init(&empty_bar[s], 1);
@@ -843,7 +878,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
-        if (!GATHER || TMAG) prefetch_tmap(&tmap_a);
+        if (!GATHER) prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
     if (warp == kMmaWarp) {
@@ -855,50 +890,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (GATHER && TMAG && warp < 4) {
-        // ---------------------------------------- producer, TMA row gather
-        // Warp 0 only: lane l gathers rows 4l..4l+3 of the A stage with one
-        // tile::gather4 (box 64 columns x 1 row); both CTAs' A and B bytes
-        // complete on the even CTA's `full` barrier.
-        if (warp == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-                const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
-                const int64_t n0 = (tile % n_tiles) * PAIR_N;
-                int4 cur = gather_src4(p, lane, m0, 0), next = gather_src4(p, lane, m0, 1);
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!warp_wait<true>(&empty_bar[stage], phase ^ 1, p.fault)) {
-                        ok = false;
-                        break;
-                    }
-                    const int tap = kb / kblocks_per_tap;
-                    const int kc = (kb % kblocks_per_tap) * BK;
-                    if (kc == 0 && tap > 0) {
-                        cur = next;
-                        next = gather_src4(p, lane, m0, tap + 1);
-                    }
-                    uint8_t *sa = smem_a + stage * C::A_BYTES;
-                    uint8_t *sb = smem_b + stage * C::B_BYTES;
-                    const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-                    if (lane == 0 && rank == 0)
-                        mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
-                    tma_gather4_pair(sa + lane * 4 * 128, &tmap_a, fb, kc, cur.x, cur.y, cur.z, cur.w);
-                    if (lane == 0) {
-#pragma unroll
-                        for (int j = 0; j < NSUB; ++j)
-                            tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
-                                             static_cast<int>(tap * p.N + n0 + j * 256 + rank * 128));
-                    }
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
-            }
-        }
-    } else if (warp < 4 || (GATHER && !TMAG && warp > kMmaWarp)) {
+    if (warp < 4 || (GATHER && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
         // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) gathers tile
         // rows [16 pw, 16 pw + 16); lane l < 16 holds row 16 pw + l's source
@@ -989,7 +981,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
                         break;
                     }
                     tc_fence_after();
-                    if (GATHER && !TMAG) fence_proxy_async_smem();
+                    if (GATHER) fence_proxy_async_smem();
                     const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
@@ -1021,7 +1013,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__((GATHER && !TMAG) ? 
                 umma_commit2(smem_u32(done_bar));
                 mbar_wait(done_bar, 0, p.fault);
             }
-        } else if (GATHER && !TMAG && lane == 0) {
+        } else if (GATHER && lane == 0) {
             // ------------ odd CTA: forward its row-gather completion to rank 0
             int stage = 0;
             uint32_t phase = 0;
@@ -1119,13 +1111,13 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
-template <int NSUB, bool GATHER, bool TMAG = false>
+template <int NSUB, bool GATHER>
 int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &to,
                  const GemmParams &p) {
     using C = Cfg2<NSUB>;
     static bool attr_set = false;
     if (!attr_set) {
-        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm2_tc_kernel<NSUB, GATHER, TMAG>,
+        P3D_CUDA(ctx, cudaFuncSetAttribute(gemm2_tc_kernel<NSUB, GATHER>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set = true;
     }
@@ -1135,16 +1127,16 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
     if (max_pairs == 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (ctx->num_sms / 2), 1, 1);
-        cfg.blockDim = dim3((GATHER && !TMAG) ? kThreadsG : kThreads, 1, 1);
+        cfg.blockDim = dim3(GATHER ? kThreadsG : kThreads, 1, 1);
         cfg.dynamicSmemBytes = C::SMEM;
         cfg.stream = ctx->stream;
         int n = 0;
-        P3D_CUDA(ctx, cudaOccupancyMaxActiveClusters(&n, gemm2_tc_kernel<NSUB, GATHER, TMAG>, &cfg));
+        P3D_CUDA(ctx, cudaOccupancyMaxActiveClusters(&n, gemm2_tc_kernel<NSUB, GATHER>, &cfg));
         max_pairs = std::max(1, std::min(n, ctx->num_sms / 2));
     }
     const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
-    gemm2_tc_kernel<NSUB, GATHER, TMAG><<<2 * pairs, (GATHER && !TMAG) ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(
+    gemm2_tc_kernel<NSUB, GATHER><<<2 * pairs, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(
         ta, tb, to, p);
     return check_launch(ctx, "gemm2_tc_kernel");
 }
@@ -1153,34 +1145,6 @@ int pick_bn(int64_t n) {
     if (n <= 64) return 64;
     if (n <= 128) return 128;
     return 256;
-}
-
-// Pair kernels on (default) unless P3D_GEMM_PAIR=0 selects the 1-CTA kernels.
-bool pair_enabled() {
-    static const bool on = [] {
-        const char *e = std::getenv("P3D_GEMM_PAIR");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
-
-// P3D_GEMM_PAIR_DENSE=1 also routes dense linears with N % 256 == 0 to the pair kernel.
-bool pair_dense() {
-    static const bool on = [] {
-        const char *e = std::getenv("P3D_GEMM_PAIR_DENSE");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-
-// P3D_CONV_GATHER=tma gathers the conv's A rows with TMA tile::gather4
-// (counted on the even CTA's barrier, no forwarding) instead of cp.async.
-bool conv_tma_gather() {
-    static const bool on = [] {
-        const char *e = std::getenv("P3D_CONV_GATHER");
-        return e && std::string(e) == "tma";
-    }();
-    return on;
 }
 
 // P3D_GEMM_TMA_STORE=0 selects the direct-store epilogue (lane = row,
@@ -1243,28 +1207,23 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
     // streams the most B bytes per output tile; for the dense linears
     // (K <= 4096) it measured no faster than the 1-CTA kernel on B200
     // (qkv 8184x3072x1024: 69.0 vs 69.0 us; MLP-up 99.5 vs 96.6 us).
-    if (pair_enabled() && p.N % 256 == 0 && (gather || pair_dense())) {
-        // Gather: two N = 256 MMAs per pair tile when N allows (long K loops
-        // hide the unbuffered epilogue); dense: one, double-buffered.
-        const int nsub = (gather && p.N % 512 == 0) ? 2 : 1;
+    if (gather && p.N % 256 == 0) {
+        // Two N = 256 MMAs per pair tile when N allows (the long K loop of a
+        // conv hides the unbuffered epilogue).
+        const int nsub = p.N % 512 == 0 ? 2 : 1;
         int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, 128);
         if (rc) return rc;
-        if (!gather && (rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM))) return rc;
         p.idesc = idesc_f32acc(2 * BM, 256, bf16);
-        if (gather && conv_tma_gather()) {
-            // A rows by TMA tile::gather4 from x [M][K] (box 64 x 1 row)
-            if ((rc = make_tmap_16bit_2d(ctx, &ta, p.x, ab_dtype, p.M, p.K, p.ldx, 1))) return rc;
-            return nsub == 2 ? launch_gemm2<2, true, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true, true>(ctx, ta, tb, to, p);
-        }
-        if (gather) ta = tb;
-        if (gather) return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true>(ctx, ta, tb, to, p);
-        return launch_gemm2<1, false>(ctx, ta, tb, to, p);
+        ta = tb;
+        return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true>(ctx, ta, tb, to, p);
     }
     const int bn = pick_bn(p.N);
     int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, bn);
     if (rc) return rc;
-    if (!gather && (rc = make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM))) return rc;
-    if (gather) ta = tb;
+    // dense: A tiles of 128 rows; gather: A rows by tile::gather4 (box 64 x 1 row)
+    if ((rc = gather ? make_tmap_16bit_2d(ctx, &ta, p.x, ab_dtype, p.M, p.K, p.ldx, 1)
+                     : make_tmap_16bit_2d(ctx, &ta, x, ab_dtype, p.M, p.K, ldx, BM)))
+        return rc;
     p.idesc = idesc_f32acc(BM, bn, bf16);
     if (gather) {
         if (bn == 64) return launch_gemm<64, true>(ctx, ta, tb, to, p);

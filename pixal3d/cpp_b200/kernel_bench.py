@@ -79,9 +79,8 @@ def run(kernel: str, reps: int) -> dict:
         taps = None
         if kernel == "conv1024t":
             # as the flow's fine level runs: rows in neighbour-pattern order, tile taps
-            bits = torch.arange(27, device=dev, dtype=torch.int64)
-            key = (coords[:, 0].to(torch.int64) << 32) | ((nbr < n).to(torch.int64) << bits[:, None]).sum(0)
-            nbr = ops.neighbor_map27(coords[torch.sort(key, stable=True).indices].contiguous())
+            order = ops.conv_row_order(coords, nbr, 2).long()
+            nbr = ops.neighbor_map27(coords[order].contiguous())
             taps = ops.conv_tile_taps(nbr)
         pairs = int((nbr < n).sum().item())
         x = torch.randn((n, ch), device=dev, generator=g).to(h)

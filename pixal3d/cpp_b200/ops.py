@@ -244,6 +244,19 @@ def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch
     return out
 
 
+def conv_row_order(coords: torch.Tensor, nbr: torch.Tensor, batch: int) -> torch.Tensor:
+    """perm [n] int32: rows stably sorted by (batch, neighbour pattern), the
+    order in which the flow runs its fine-level convs (p3d_conv_row_order)."""
+    c = ctx(coords.device)
+    n = coords.shape[0]
+    ws_bytes = int(L.lib.p3d_conv_row_order_workspace(n, batch))
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=coords.device)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    perm = torch.empty(n, dtype=torch.int32, device=coords.device)
+    c.check(L.lib.p3d_conv_row_order(c.h, _p(coords), _p(nbr), n, batch, C.c_void_p(base), ws_bytes, _p(perm)))
+    return perm
+
+
 def conv_tile_taps(nbr: torch.Tensor) -> torch.Tensor:
     """Per 256-row tile, the taps some row of the tile uses (p3d_conv_tile_taps)."""
     c = ctx(nbr.device)

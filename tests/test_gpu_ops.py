@@ -389,34 +389,6 @@ def test_subm_conv3d_tile_taps_skip_is_exact():
     np.testing.assert_array_equal(tb.astype(np.int64), exp)
 
 
-def test_linear_pair_kernel_subprocess():
-    """The CTA-pair kernel on dense linears (selected by P3D_GEMM_PAIR_DENSE=1,
-    read once per process, hence a child process): M below one CTA's 128 rows
-    (the odd CTA loads only zero-filled rows) and ragged last pairs."""
-    import subprocess
-    import sys
-    import os
-    code = r"""
-import math, numpy as np, torch
-from pixal3d.cpp_b200 import ops
-def h(a): return torch.from_numpy(np.ascontiguousarray(a.astype(np.float32))).cuda().half()
-def r16(a): return a.astype(np.float32).astype(np.float16).astype(np.float32)
-rng = np.random.default_rng(12)
-for m, n, k in ((100, 512, 128), (1000, 768, 256), (4133, 1024, 1024)):
-    x = rng.standard_normal((m, k)).astype(np.float32)
-    w = (rng.standard_normal((n, k)) / math.sqrt(k)).astype(np.float32)
-    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
-    y = ops.linear(h(x), h(w), torch.from_numpy(b).cuda(), out_dtype=torch.float32).cpu().numpy()
-    e = r16(x) @ r16(w).T + b
-    err = float(np.abs(y - e).max()); rel = float(np.linalg.norm(y - e) / np.linalg.norm(e))
-    assert err <= 1e-3 * max(1.0, float(np.abs(e).max())) and rel <= 1e-5, (m, n, k, err, rel)
-print("ok")
-"""
-    env = dict(os.environ, P3D_GEMM_PAIR_DENSE="1")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600,
-                       cwd=str(FX.GOLDEN.parent.parent))
-    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
-
 
 def test_subm_conv3d_residual_bf16():
     c = shell_coords(32, 10.0, 1.2)
@@ -688,3 +660,33 @@ def test_linear_headnorm(dtype, norm, rope):
         check(got, exp, max_abs=4e-3 * max(1.0, float(np.abs(exp).max())), rel_l2=1e-3, what="f16 headnorm")
     else:
         check(got, exp, max_abs=bf16_out_tol(exp), rel_l2=REL_L2, what="bf16 headnorm")
+
+
+def test_conv_row_order_matches_stable_sort():
+    """p3d_conv_row_order (device radix sort) == numpy's stable argsort of
+    (batch, neighbour pattern), on the batch-2 config-0 shell and on a
+    five-item ragged batch."""
+    from pixal3d.cpp_b200.workloads import image_shells, pack_cfg
+    from tests._configs import pattern_order
+    o = ops()
+    packed, _ = pack_cfg(image_shells(3, seed=5))
+    for cs, batch in ((batched(shell_coords(), 2), 2), (packed, 6)):
+        d = dev(cs)
+        perm = o.conv_row_order(d, o.neighbor_map27(d), batch).cpu().numpy()
+        np.testing.assert_array_equal(perm, pattern_order(cs, O.neighbor_map27(cs)))
+
+
+def test_flow_prepare_rejects_unordered_batches():
+    from pixal3d.cpp_b200.flow import FlowModel, HParams
+    from tests._models import random_flow_weights
+    hp = O.FlowHParams(in_channels=8, out_channels=8, model_channels=128, cond_channels=64, num_blocks=1,
+                       num_heads=2, io_resblocks=1, groups=32)
+    fields = {k: getattr(hp, k) for k in HParams.__dataclass_fields__ if hasattr(hp, k)}
+    model = FlowModel(HParams(**fields), random_flow_weights(np.random.default_rng(0), hp))
+    c = batched(shell_coords(16, 5.0, 1.0), 2)
+    bad = np.ascontiguousarray(np.concatenate([c[c[:, 0] == 1], c[c[:, 0] == 0]]))
+    with pytest.raises(L().P3DError, match="contiguous by batch"):
+        model.prepare(dev(bad), 2, (16, 16, 16), [0, 10, 20])
+    # the same flow prepares a valid set afterwards
+    model.prepare(dev(c), 2, (16, 16, 16), [0, 10, 20])
+    model.close()
