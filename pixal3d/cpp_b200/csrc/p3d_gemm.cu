@@ -44,11 +44,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 9 * 32;
-// The cp.async gather variants add 4 producer warps (9-12), so 8 warps share
-// each stage's row gathers (4 cp.async per lane per stage): a warp completes
-// its cp.async instructions slowly, and the stage fill latency bounds the conv.
+// The gather variants add 4 producer warps (9-12): one producer warp per stage
+// slot, up to 8 stages.
 constexpr int kThreadsG = 13 * 32;
-constexpr int kGatherThreads = 256;
 constexpr int kMmaWarp = 8;
 
 struct GemmParams {
@@ -503,21 +501,6 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
     }
 }
 
-// Source row of tile row m0 + t for tap `tap`, as stored in the neighbour map
-// (the sentinel M, or any value outside [0, M), means zero fill; a row past
-// the end reads as -1).  The value is returned unchecked: checking it here
-// would make the caller wait for the load, while it is loaded ahead of use
-// and range-checked where the gather consumes it.
-__device__ __forceinline__ int32_t gather_src(const GemmParams &p, int t, int64_t m0, int tap) {
-    const int64_t row = m0 + t;
-    if (tap >= 27 || row >= p.M) return -1;
-    return __ldg(p.nbr + static_cast<int64_t>(tap) * p.M + row);
-}
-
-__device__ __forceinline__ bool src_valid(const GemmParams &p, int32_t s) {
-    return s >= 0 && static_cast<int64_t>(s) < p.M;
-}
-
 // Residual epilogues read-modify-write the f32 output: pull this lane's row
 // segment into L2 while the tile's MMAs run, so the epilogue's loads hit L2.
 __device__ __forceinline__ void prefetch_residual(const GemmParams &p, int64_t row, int64_t n0, int cols) {
@@ -527,23 +510,6 @@ __device__ __forceinline__ void prefetch_residual(const GemmParams &p, int64_t r
     const uint32_t bytes = static_cast<uint32_t>(c * 4) & ~15u;
     if (bytes == 0 || (reinterpret_cast<uintptr_t>(rp) & 15) != 0) return;
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rp), "r"(bytes) : "memory");
-}
-
-// One producer warp's share of a gather stage when 8 warps fill it: tile
-// rows [16 pw, 16 pw + 16), 4 cp.async instructions of 4 rows each (8 lanes
-// per 128-byte row); lane l < 16 holds the source of row 16 pw + l.
-__device__ __forceinline__ void gather_stage_a16(const GemmParams &p, uint8_t *sa, int pw, int lane, int32_t my_src,
-                                                 int kc) {
-    const int chunk = lane & 7;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int rr = i * 4 + (lane >> 3);
-        const int r = 16 * pw + rr;
-        const int32_t src = __shfl_sync(0xffffffffu, my_src, rr);
-        const bool ok = src_valid(p, src);
-        const uint16_t *g = p.x + (ok ? static_cast<int64_t>(src) * p.ldx + kc + chunk * 8 : 0);
-        cp_async16(sa + r * 128 + ((chunk ^ (r & 7)) << 4), g, ok ? 16u : 0u);
-    }
 }
 
 // Warp-uniform bounded wait: lane 0 polls, the warp follows its verdict.
@@ -864,12 +830,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
     auto tile_kb = [&](int64_t tile) -> int { return GATHER ? __popc(tile_taps(tile)) * kblocks_per_tap : num_kb; };
 
     if (threadIdx.x == 0) {
-        // even CTA: its expect_tx arrival (+ its 128 row-gather threads and
-        // the odd CTA's forwarded gather completion); odd CTA (gather): its
-        // 128 row-gather threads, forwarded by its warp 8.
-        const uint32_t full_count = GATHER ? (rank == 0 ? kGatherThreads + 2 : kGatherThreads) : 1;
+        // full: the even CTA's expect_tx arrival; both CTAs' TMA bytes complete on it
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full_bar[s], full_count);
+            mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -878,7 +841,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
-        if (!GATHER) prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
     if (warp == kMmaWarp) {
@@ -892,68 +855,137 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
 
     if (warp < 4 || (GATHER && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
-        // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) gathers tile
-        // rows [16 pw, 16 pw + 16); lane l < 16 holds row 16 pw + l's source
         const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
-        const int t = warp < 4 ? threadIdx.x : 0;
-        const int grow = 16 * pw + (lane & 15);
-        int stage = 0;
-        uint32_t phase = 0;
         bool ok = true;
-        for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-            const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
-            const int64_t n0 = (tile % n_tiles) * PAIR_N;
-            int32_t cur_src = 0, next_src = 0;
-            // taps still to visit after `tap`; next_tap = 27 when none
-            uint32_t rem = tile_taps(tile);
-            int tap = 0, next_tap = 27;
-            if (GATHER) {
-                tap = __ffs(rem) - 1;
-                rem &= rem - 1;
-                next_tap = rem ? __ffs(rem) - 1 : 27;
-                cur_src = gather_src(p, grow, m0, tap);
-                next_src = gather_src(p, grow, m0, next_tap);
-            }
-            const int nkb = tile_kb(tile);
-            for (int kb = 0; kb < nkb; ++kb) {
-                if (GATHER) {
-                    if (!warp_wait<true>(&empty_bar[stage], phase ^ 1, p.fault)) {
-                        ok = false;
-                        break;
-                    }
-                } else if (t == 0) {
-                    if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, p.fault)) {
-                        ok = false;
-                        break;
-                    }
+        if constexpr (GATHER) {
+            // One producer warp per stage slot (pw < STAGES), as in the 1-CTA
+            // gather: step s = (pair tile, used tap, K block) goes to warp
+            // s % STAGES, which fills this CTA's 128 A rows of the stage with
+            // one tile::gather4 per lane (rows m0 + 4 lane .. + 3; a source
+            // outside [0, M) reads zeros) and its half of B with 2D loads.
+            // Both CTAs' bytes complete on the even CTA's `full` barrier, whose
+            // expect_tx the even CTA posts for both.  Taps no row of the tile
+            // uses are skipped (the step's tap is the (w / kpt)-th set bit of
+            // the tile's mask).
+            static_assert(STAGES <= 8, "one producer warp per stage slot");
+            struct Pos {
+                int64_t tile, m0, n0;
+                uint32_t mask;
+                int w, nsteps;
+            };
+            auto place = [&](Pos &ps) {
+                if (ps.tile >= num_tiles) {
+                    ps.nsteps = 1 << 30;
+                    return;
                 }
-                uint8_t *sa = smem_a + stage * C::A_BYTES;
-                uint8_t *sb = smem_b + stage * C::B_BYTES;
-                const int kc = GATHER ? (kb % kblocks_per_tap) * BK : kb * BK;
-                if (GATHER) {
-                    if (kc == 0 && kb > 0) {
-                        tap = next_tap;
-                        rem &= rem - 1;
-                        next_tap = rem ? __ffs(rem) - 1 : 27;
-                        cur_src = next_src;
-                        next_src = gather_src(p, grow, m0, next_tap);
-                    }
-                    gather_stage_a16(p, sa, pw, lane, cur_src, kc);
+                ps.m0 = (ps.tile / n_tiles) * (2 * BM) + rank * BM;
+                ps.n0 = (ps.tile % n_tiles) * PAIR_N;
+                ps.mask = tile_taps(ps.tile);
+                ps.nsteps = __popc(ps.mask) * kblocks_per_tap;
+            };
+            auto advance = [&](Pos &ps) {
+                ps.w += STAGES;
+                while (ps.w >= ps.nsteps && ps.tile < num_tiles) {
+                    ps.w -= ps.nsteps;
+                    ps.tile += npairs;
+                    place(ps);
                 }
-                if (warp == 0 && lane == 0) {
-                    const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-                    if (rank == 0)
-                        mbar_arrive_expect_tx(&full_bar[stage], 2 * (GATHER ? C::B_BYTES : C::A_BYTES + C::B_BYTES));
-                    if (!GATHER) tma_load_2d_pair(sa, &tmap_a, fb, kc, static_cast<int>(m0));
+            };
+            auto tap_of = [&](const Pos &ps) -> int { return static_cast<int>(__fns(ps.mask, 0, ps.w / kblocks_per_tap + 1)); };
+            auto load4 = [&](const Pos &ps) -> int4 {
+                int r[4] = {-1, -1, -1, -1};
+                if (ps.tile < num_tiles) {
+                    const int64_t tap = tap_of(ps);
 #pragma unroll
-                    for (int j = 0; j < NSUB; ++j)
-                        tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
-                                         static_cast<int>(tap * p.N + n0 + j * 256 + rank * 128));
+                    for (int j = 0; j < 4; ++j) {
+                        const int64_t row = ps.m0 + 4 * lane + j;
+                        if (row < p.M) r[j] = __ldg(p.nbr + tap * p.M + row);
+                    }
                 }
-                if (GATHER) cp_async_mbar_arrive_noinc(&full_bar[stage]);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
+                return make_int4(r[0], r[1], r[2], r[3]);
+            };
+            if (pw < STAGES) {
+                Pos pc{pair, 0, 0, 0u, 0, 0};
+                place(pc);
+                // step pw of this CTA's sequence
+                pc.w = pw;
+                while (pc.w >= pc.nsteps && pc.tile < num_tiles) {
+                    pc.w -= pc.nsteps;
+                    pc.tile += npairs;
+                    place(pc);
+                }
+                Pos pa = pc;
+                const int4 first0 = load4(pa);
+                advance(pa);
+                const int4 first1 = load4(pa);
+                advance(pa);
+                int4 ring0 = first0, ring1 = first1;
+                int64_t st = pw;  // global step index: stage st % STAGES, round st / STAGES
+                while (pc.tile < num_tiles && ok) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        if (pc.tile >= num_tiles || !ok) break;
+                        int4 src;
+                        if (u == 0) {
+                            src = ring0;
+                            ring0 = load4(pa);
+                        } else {
+                            src = ring1;
+                            ring1 = load4(pa);
+                        }
+                        advance(pa);
+                        const int stg = static_cast<int>(st % STAGES);
+                        const uint32_t ph = static_cast<uint32_t>((st / STAGES) & 1);
+                        if (!warp_wait<true>(&empty_bar[stg], ph ^ 1, p.fault)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t *sa = smem_a + stg * C::A_BYTES;
+                        uint8_t *sb = smem_b + stg * C::B_BYTES;
+                        const int tap = tap_of(pc);
+                        const int kc = (pc.w % kblocks_per_tap) * BK;
+                        const uint32_t fb = mapa_shared(smem_u32(&full_bar[stg]), 0);
+                        if (rank == 0 && lane == 0) mbar_arrive_expect_tx(&full_bar[stg], 2 * (C::A_BYTES + C::B_BYTES));
+                        __syncwarp();
+                        tma_gather4_pair(sa + lane * 4 * 128, &tmap_a, fb, kc, src.x, src.y, src.z, src.w);
+                        if (lane == 0) {
+#pragma unroll
+                            for (int j = 0; j < NSUB; ++j)
+                                tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
+                                                 static_cast<int>(tap * p.N + pc.n0 + j * 256 + rank * 128));
+                        }
+                        advance(pc);
+                        st += STAGES;
+                    }
+                }
+            }
+        } else {
+            const int t = threadIdx.x;
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
+                const int64_t n0 = (tile % n_tiles) * PAIR_N;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (t == 0) {
+                        if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, p.fault)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t *sa = smem_a + stage * C::A_BYTES;
+                        uint8_t *sb = smem_b + stage * C::B_BYTES;
+                        const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+                        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
+                        tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, static_cast<int>(m0));
+#pragma unroll
+                        for (int j = 0; j < NSUB; ++j)
+                            tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kb * BK,
+                                             static_cast<int>(n0 + j * 256 + rank * 128));
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
                 }
             }
         }
@@ -981,7 +1013,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
                         break;
                     }
                     tc_fence_after();
-                    if (GATHER) fence_proxy_async_smem();
                     const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
@@ -1012,26 +1043,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
             if (issued) {
                 umma_commit2(smem_u32(done_bar));
                 mbar_wait(done_bar, 0, p.fault);
-            }
-        } else if (GATHER && lane == 0) {
-            // ------------ odd CTA: forward its row-gather completion to rank 0
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-                const int nkb = tile_kb(tile);
-                for (int kb = 0; kb < nkb; ++kb) {
-                    if (!mbar_wait(&full_bar[stage], phase, p.fault)) {
-                        ok = false;
-                        break;
-                    }
-                    fence_proxy_async_smem();
-                    mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), peer));
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
             }
         }
         __syncwarp();
@@ -1213,8 +1224,9 @@ int run_gemm(p3d_ctx *ctx, const void *x, int64_t ldx, const void *w, int ab_dty
         const int nsub = p.N % 512 == 0 ? 2 : 1;
         int rc = make_tmap_16bit_2d(ctx, &tb, w, ab_dtype, w_rows, p.K, p.K, 128);
         if (rc) return rc;
+        // A rows by tile::gather4 from x [M][K] (box 64 columns x 1 row)
+        if ((rc = make_tmap_16bit_2d(ctx, &ta, p.x, ab_dtype, p.M, p.K, p.ldx, 1))) return rc;
         p.idesc = idesc_f32acc(2 * BM, 256, bf16);
-        ta = tb;
         return nsub == 2 ? launch_gemm2<2, true>(ctx, ta, tb, to, p) : launch_gemm2<1, true>(ctx, ta, tb, to, p);
     }
     const int bn = pick_bn(p.N);
