@@ -79,7 +79,7 @@ class _stdout_to_stderr:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg1", "cfg3", "cascade", "cfg4"], default="cfg2")
     ap.add_argument("--steps", type=int, default=None, help="timed steps (cfg4: sampler steps per image)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -714,6 +714,171 @@ def run_reference_cfg1(args):
                               "d2h_bytes_per_step": 0}}), flush=True)
 
 
+# ------------------------------------------------------- decoders
+
+def run_cfg3(args):
+    """the shifted-window SLat decoder (no reference
+    implementation) from the 21,766-voxel 64^3 shell: input linear to 768 +
+    APE, 12 window blocks (8^3 windows, 12 heads x 64, MLP x4), subdivide to
+    128^3 with a seeded Bernoulli(0.5) mask + SparseResBlock3d to C=128,
+    subdivide to 256^3 + SparseResBlock3d to C=32, linear head to 32.  ms per
+    decode; the CPU baseline is this repo's numpy restatement (no reference
+    code exists) run once on the same inputs."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    world, rank, local = init_ranks(torch, dist)
+    from pixal3d.cpp_b200 import dist as D
+    from pixal3d.cpp_b200 import ops
+    from pixal3d.cpp_b200.swin_decoder import SwinDecoder
+    from pixal3d.cpp_b200.workloads import random_swin_weights, shell_coords
+    dev = torch.device("cuda", local)
+    cfg = {"model_channels": 768, "num_heads": 12, "window": 8, "spatial": RES, "groups": 32}
+    rng = np.random.default_rng(41)
+    w = random_swin_weights(rng, c0=768, stages=(128, 32), latent=8, out=32, blocks=12)
+    coords = shell_coords()
+    n = coords.shape[0]
+    x = rng.standard_normal((n, 8)).astype(np.float32)
+    m1 = (rng.random((n, 8)) < 0.5).astype(np.float32)
+    m2 = (rng.random((int(m1.sum()), 8)) < 0.5).astype(np.float32)
+    d = SwinDecoder(cfg, w, device=local)
+    cd, xd = torch.from_numpy(coords).to(dev), torch.from_numpy(x).to(dev)
+    masks = [torch.from_numpy(m1).to(dev), torch.from_numpy(m2).to(dev)]
+    for _ in range(max(args.warmup, 1)):
+        oc, out = d.run(cd, xd, masks)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.ctx(local).launches
+    e0.record()
+    for _ in range(args.steps):
+        oc, out = d.run(cd, xd, masks)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ops.ctx(local).launches - launches0
+    ms = D.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    if rank == 0:
+        # algorithmic flops: block linears + window attention + stage convs/skips
+        C0, blocks = 768, 12
+        fl = blocks * 2 * n * C0 * C0 * (3 + 1 + 4 + 4)
+        for shift in (0, 4):
+            key = ((coords[:, 1] + shift) // 8 * 64 + (coords[:, 2] + shift) // 8) * 64 + (coords[:, 3] + shift) // 8
+            cnt = np.bincount(key).astype(np.float64)
+            fl += (blocks // 2) * 4 * float((cnt * cnt).sum()) * C0
+        rows = [n]
+        cur = cd
+        ci = C0
+        for mask, co in zip(masks, (128, 32)):
+            oc_s, _, _, mm = ops.c2s_topology(cur, 2, mask)
+            cur = oc_s.contiguous()
+            pairs = int((ops.neighbor_map27(cur) < mm).sum().item())
+            fl += 2 * pairs * ci * co + 2 * pairs * co * co + 2 * mm * ci * co
+            rows.append(int(mm))
+            ci = co
+        fl += 2 * rows[-1] * 32 * 32
+        peaks, kind = load_peaks()
+        tf = fl / (ms / 1000.0) / 1e12
+        result = {"metric": "config-3 shifted-window SLat decode (21,766 -> 256^3)", "value": round(ms, 3),
+                  "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                  "higher_is_better": False, "scaling": "weak", "dtype": "f16 operands, f32 accumulate/residual",
+                  "data": "synthetic: config-0 shell, N(0,1) latent, seeded Bernoulli(0.5) masks, random-init weights",
+                  "config": {"workload": "config3: 12 window blocks C=768, stages to C=128 (128^3) and C=32 (256^3)",
+                             "rows_per_level": rows, "parallelism": f"replicas x{world}"},
+                  "tflop": round(fl / 1e12, 4), "achieved_tflops": round(tf, 1),
+                  "frac_of_bf16_burst": round(tf / peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), 4),
+                  "gpu_launches": int(launches), "out_finite": bool(torch.isfinite(out).all())}
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
+            t0 = time.perf_counter()
+            O.swin_decoder_forward(coords, x, cfg, w, [m1, m2])
+            sec = time.perf_counter() - t0
+            result["cpu_baseline"] = {"value": round(sec * 1000.0, 1), "unit": "ms", "cores": os.cpu_count(),
+                                      "kind": "port", "sample": "the numpy restatement of the whole decode, once "
+                                                                "(the config has no reference implementation)"}
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_cascade(args):
+    """The device SLat decoder at cascade scale: five levels (512 -> 256 ->
+    128 -> 64 -> 32 channels) from the 9,682-voxel 64^3 shell to about 4.04M
+    points, guided subdivision with seeded masks (keep 0.565), as the
+    reference's real shape decode grows 9,857 -> 4,005,638 points.  Times the
+    whole decode and each level (ConvNeXt blocks + the channel-to-spatial
+    block into the next level), plus the predicted-subdivision decode."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    world, rank, local = init_ranks(torch, dist)
+    from pixal3d.cpp_b200 import dist as D
+    from pixal3d.cpp_b200 import workloads as WL
+    from pixal3d.cpp_b200.decoder import Decoder
+    dev = torch.device("cuda", local)
+    w = WL.random_decoder_weights(np.random.default_rng(31), WL.CASCADE_CHANNELS, WL.CASCADE_BLOCKS,
+                                  WL.CASCADE_LATENT, WL.CASCADE_OUT)
+    coords = WL.cascade_input()
+    x = np.random.default_rng(32).standard_normal((coords.shape[0], WL.CASCADE_LATENT)).astype(np.float32)
+    guides = [torch.from_numpy(g).to(dev) for g in WL.cascade_guides(coords.shape[0], len(WL.CASCADE_CHANNELS), seed=33)]
+    cd, xd = torch.from_numpy(coords).to(dev), torch.from_numpy(x).to(dev)
+    levels = len(WL.CASCADE_CHANNELS)
+    dg = Decoder(list(WL.CASCADE_CHANNELS), list(WL.CASCADE_BLOCKS), WL.CASCADE_LATENT, WL.CASCADE_OUT, w,
+                 pred_subdiv=False, device=local)
+    dp = Decoder(list(WL.CASCADE_CHANNELS), list(WL.CASCADE_BLOCKS), WL.CASCADE_LATENT, WL.CASCADE_OUT, w,
+                 pred_subdiv=True, device=local)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, r
+
+    reps = max(1, min(args.steps, 5))
+    if world > 1:
+        dist.barrier()
+    ms_full, (oc, out, _) = timed(lambda: dg.run(cd, xd, 1, (RES, RES, RES), guides=guides), reps)
+    cum = [0.0]
+    for stop in range(1, levels):
+        t, _ = timed(lambda: dg.run(cd, xd, 1, (RES, RES, RES), guides=guides, stop_level=stop), reps)
+        cum.append(t)
+    cum.append(ms_full)
+    ms_pred, (ocp, _, _) = timed(lambda: dp.run(cd, xd, 1, (RES, RES, RES)), reps)
+    ms_full = D.max_over_ranks(ms_full, dev)
+    if rank == 0:
+        rows = [coords.shape[0]]
+        n = coords.shape[0]
+        for g in guides:
+            n = int((g > 0).sum().item())
+            rows.append(n)
+        print(json.dumps({
+            "metric": "SLat decoder at cascade scale (9,682 -> 4.04M points)", "value": round(ms_full, 2),
+            "unit": "ms", "n_gpus": world, "steps": reps, "higher_is_better": False, "scaling": "weak",
+            "dtype": "f16 operands, f32 accumulate/residual",
+            "data": "synthetic: r=16 shell at 64^3, N(0,1) 32-channel latent, seeded keep masks p=0.565, "
+                    "random-init weights",
+            "config": {"workload": "five-level decoder 512/256/128/64/32, one ConvNeXt block per level, guided "
+                                   "subdivision", "parallelism": f"replicas x{world}"},
+            "rows_per_level": rows, "out_rows": int(oc.shape[0]),
+            "level_ms": [round(cum[i + 1] - cum[i], 2) for i in range(levels)],
+            "points_per_s": round(oc.shape[0] / (ms_full / 1000.0), 1),
+            "predicted_subdivision": {"ms": round(ms_pred, 2), "out_rows": int(ocp.shape[0])},
+            "out_finite": bool(torch.isfinite(out).all()),
+            "reference_published": "shape decoder 43.0-45.2 s GPU-first, 596.9 s hybrid, 1,822.6 s forced CPU "
+                                   "(RTX 4090 D host, troubleshooting_history.md:387-390)"}), flush=True)
+    dg.close()
+    dp.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------- config 4 (images/s)
 
 CFG4_IMAGES = 64
@@ -875,6 +1040,14 @@ def main():
         args.steps = 25 if args.workload == "cfg4" else 20
     if args.workload == "cfg1":
         (run_reference_cfg1 if args.impl == "reference" else run_cfg1)(args)
+        return
+    if args.workload in ("cfg3", "cascade"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": args.workload,
+                              "unavailable": "the config-3 decoder has no reference implementation; the reference's "
+                                             "cascade decoder (ggml GPU graph) cannot be built (empty ggml submodule)"}))
+            return
+        (run_cfg3 if args.workload == "cfg3" else run_cascade)(args)
         return
     if args.workload == "cfg4":
         if args.impl == "reference":

@@ -149,3 +149,35 @@ def random_decoder_weights(rng: np.random.Generator, chans, num_blocks, latent: 
                            "subdiv_w": xav(8, c), "subdiv_b": vec(8, 0.5)})
     return {"from_latent_w": xav(chans[0], latent), "from_latent_b": vec(chans[0]), "output_w": xav(out, chans[-1]),
             "output_b": vec(out), "blocks": blocks}
+
+
+def random_swin_weights(rng: np.random.Generator, c0: int = 128, stages=(64, 32), latent: int = 8, out: int = 16,
+                        blocks: int = 2, mlp_ratio: int = 4) -> dict:
+    """Random-init weights of the config-3 shifted-window decoder (keys as
+    SwinDecoder takes them): linears xavier-uniform, convs N(0, 1/sqrt(27
+    cin)), norms 1 + N(0, .05), biases N(0, .05)."""
+    def xav(o, i):
+        a = math.sqrt(6.0 / (o + i))
+        return rng.uniform(-a, a, (o, i)).astype(np.float32)
+
+    def vec(n, s=0.05, m=0.0):
+        return (m + rng.standard_normal(n) * s).astype(np.float32)
+
+    def conv(o, i):
+        return (rng.standard_normal((27, o, i)) / math.sqrt(27 * i)).astype(np.float32)
+
+    w = {"from_latent_w": xav(c0, latent), "from_latent_b": vec(c0), "blocks": [], "stages": []}
+    for _ in range(blocks):
+        w["blocks"].append({"norm1_w": vec(c0, 0.05, 1.0), "norm1_b": vec(c0), "qkv_w": xav(3 * c0, c0),
+                            "qkv_b": vec(3 * c0), "out_w": xav(c0, c0), "out_b": vec(c0),
+                            "norm2_w": vec(c0, 0.05, 1.0), "norm2_b": vec(c0), "mlp0_w": xav(mlp_ratio * c0, c0),
+                            "mlp0_b": vec(mlp_ratio * c0), "mlp2_w": xav(c0, mlp_ratio * c0), "mlp2_b": vec(c0)})
+    ci = c0
+    for co in stages:
+        w["stages"].append({"gn1_w": vec(ci, 0.05, 1.0), "gn1_b": vec(ci), "conv1_w": conv(co, ci), "conv1_b": vec(co),
+                            "gn2_w": vec(co, 0.05, 1.0), "gn2_b": vec(co), "conv2_w": conv(co, co),
+                            "conv2_b": vec(co), "skip_w": xav(co, ci), "skip_b": vec(co)})
+        ci = co
+    w["output_w"] = xav(out, ci)
+    w["output_b"] = vec(out)
+    return w

@@ -8,8 +8,6 @@ one-channel GroupNorm groups), 16 output channels, seeded Bernoulli(0.5)
 subdivision masks.  Coordinates bit-exact; features within the north-star
 bound (max-abs 2e-2, relative-L2 5e-3).
 """
-import math
-
 import numpy as np
 import pytest
 
@@ -21,32 +19,9 @@ from pixal3d.cpp_b200.workloads import shell_coords
 pytestmark = pytest.mark.gpu
 
 
-def make_weights(rng, c0=128, stages=(64, 32), latent=8, out=16, blocks=2, mlp_ratio=4):
-    def xav(o, i):
-        a = math.sqrt(6.0 / (o + i))
-        return rng.uniform(-a, a, (o, i)).astype(np.float32)
-
-    def vec(n, s=0.05, m=0.0):
-        return (m + rng.standard_normal(n) * s).astype(np.float32)
-
-    def conv(o, i):
-        return (rng.standard_normal((27, o, i)) / math.sqrt(27 * i)).astype(np.float32)
-
-    w = {"from_latent_w": xav(c0, latent), "from_latent_b": vec(c0), "blocks": [], "stages": []}
-    for _ in range(blocks):
-        w["blocks"].append({"norm1_w": vec(c0, 0.05, 1.0), "norm1_b": vec(c0), "qkv_w": xav(3 * c0, c0),
-                            "qkv_b": vec(3 * c0), "out_w": xav(c0, c0), "out_b": vec(c0),
-                            "norm2_w": vec(c0, 0.05, 1.0), "norm2_b": vec(c0), "mlp0_w": xav(mlp_ratio * c0, c0),
-                            "mlp0_b": vec(mlp_ratio * c0), "mlp2_w": xav(c0, mlp_ratio * c0), "mlp2_b": vec(c0)})
-    ci = c0
-    for co in stages:
-        w["stages"].append({"gn1_w": vec(ci, 0.05, 1.0), "gn1_b": vec(ci), "conv1_w": conv(co, ci), "conv1_b": vec(co),
-                            "gn2_w": vec(co, 0.05, 1.0), "gn2_b": vec(co), "conv2_w": conv(co, co),
-                            "conv2_b": vec(co), "skip_w": xav(co, ci), "skip_b": vec(co)})
-        ci = co
-    w["output_w"] = xav(out, ci)
-    w["output_b"] = vec(out)
-    return w
+def make_weights(rng):
+    from pixal3d.cpp_b200.workloads import random_swin_weights
+    return random_swin_weights(rng)
 
 
 def test_swin_decoder_matches_restatement():
