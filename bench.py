@@ -885,6 +885,14 @@ CFG4_IMAGES = 64
 CFG4_PACK_VOXELS = 400_000  # voxels of one varlen CFG batch (x2 rows with the unconditional copies)
 
 
+def cfg4_cost(voxels: int) -> float:
+    """Relative sampling cost of one image for the LPT plan: linear in the
+    voxel count (convs, linears, norms, cross-attention) plus the trunk
+    self-attention, quadratic in it: 24 x 210 us of a 32 ms config-2 step at
+    21,766 voxels, about 16 % of the step's time."""
+    return voxels * (1.0 + 0.16 * voxels / 21766.0)
+
+
 def run_cfg4(args):
     """BASELINE config 4 on this rank's LPT share of the 64 images."""
     import numpy as np
@@ -900,7 +908,7 @@ def run_cfg4(args):
     dev = torch.device("cuda", local)
     shells = image_shells(CFG4_IMAGES, seed=0)
     sizes = [int(c.shape[0]) for c in shells]
-    plan = D.lpt_assign(sizes, world)
+    plan = D.lpt_assign([cfg4_cost(v) for v in sizes], world)
     packs = split_packs(plan[rank], sizes, CFG4_PACK_VOXELS)
     hp = HParams(in_channels=CH, out_channels=CH, model_channels=C, cond_channels=C, num_blocks=BLOCKS,
                  num_heads=HEADS, mlp_ratio=4.0, io_resblocks=2, groups=32, operand_dtype="f16")
@@ -986,6 +994,7 @@ def run_cfg4(args):
             "per_step_ms_rank0": round(sum(sample_ms) / max(1, len(sample_ms) * args.steps), 3),
             "packs_rank0": len(host), "rank_ms": [round(v, 1) for v in ms_all],
             "imbalance_measured": round(max(ms_all) / (sum(ms_all) / len(ms_all)), 4),
+            "imbalance_planned_cost": round(D.imbalance(plan, [cfg4_cost(v) for v in sizes]), 4),
             "imbalance_planned_voxels": round(D.imbalance(plan, sizes), 4),
             "latents_finite_rank0": finite, "gpu_launches_rank0": int(launches), "clocks": clk,
             "e2e": {"value": round(value, 3), "unit": "images/s", "h2d_bytes_rank0": int(h2d),
