@@ -111,8 +111,8 @@ int p3d_wait_selftest(p3d_ctx *ctx, int complete, int64_t limit_ns, int64_t *out
 int64_t p3d_coord_hash_capacity(int64_t n);
 
 /* Insert every row of coords into an open-addressing table in HBM
- * (warp-cooperative bucketed linear probing: 8 lanes of a warp per key read
- * a window of 8 slots per step; bounded probes).  Keys pack 16 bits per
+ * (warp-cooperative bucketed linear probing: 4 lanes of a warp per key read
+ * a window of 4 slots, one 32-byte sector, per step; bounded probes).  Keys pack 16 bits per
  * field, so batch must lie in [0, 65536) and x, y, z in [-32768, 32768): a
  * row outside that range latches P3D_ERR_INVALID instead of aliasing
  * another key, and p3d_neighbor_map27 reports neighbours outside it as

@@ -487,4 +487,63 @@ __device__ __forceinline__ int batch_of_row(const int32_t *offsets, int nbatch, 
     return b;
 }
 
+// Statistics of the CFG guidance rescale (sparse_batch_std,
+// src/flow_sampler.cpp:164-198): per batch item b, stats[4b .. 4b+3] +=
+// (sum, sum of squares) of x0(pos) and of x0(cfg), x0 = a x - (sigma_min +
+// a t) v with a = 1 - sigma_min and the CFG prediction g v_pos + (1 - g)
+// v_neg (v_pos when v_neg is null).  Each warp takes kStatsRowsPerWarp
+// consecutive rows, its lanes stride over their elements, and it flushes its
+// double partials with one set of atomics per batch segment (rows are
+// contiguous by batch), instead of per row on the same four addresses.
+constexpr int kStatsRowsPerWarp = 64;
+__device__ __forceinline__ void cfg_stats_rows(const float *__restrict__ x, const float *__restrict__ vp,
+                                               const float *__restrict__ vn, int64_t n, int C,
+                                               const int32_t *__restrict__ offsets, int nbatch, float t, float g,
+                                               float sigma_min, double *__restrict__ stats) {
+    const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t r0 = warp_id * kStatsRowsPerWarp;
+    if (r0 >= n) return;
+    const int64_t r1 = r0 + kStatsRowsPerWarp < n ? r0 + kStatsRowsPerWarp : n;
+    const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
+    int b = batch_of_row(offsets, nbatch, r0);
+    int64_t rs = r0;
+    while (rs < r1) {
+        const int64_t bend = offsets[b + 1];
+        const int64_t re = bend < r1 ? bend : r1;
+        if (re <= rs) {  // item b ends before rs (an empty item): move on; past the last item: stop
+            if (b + 1 < nbatch) {
+                ++b;
+                continue;
+            }
+            break;
+        }
+        double s0 = 0, q0 = 0, s1 = 0, q1 = 0;
+        for (int64_t e = rs * C + lane; e < re * C; e += 32) {
+            const float p = vp[e];
+            const float pred = vn ? g * p + (1.0f - g) * vn[e] : p;
+            const float xp = a * x[e] - bb * p;
+            const float xc = a * x[e] - bb * pred;
+            s0 += xp;
+            q0 += static_cast<double>(xp) * xp;
+            s1 += xc;
+            q1 += static_cast<double>(xc) * xc;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+        }
+        if (lane == 0) {
+            atomicAdd(stats + 4 * b + 0, s0);
+            atomicAdd(stats + 4 * b + 1, q0);
+            atomicAdd(stats + 4 * b + 2, s1);
+            atomicAdd(stats + 4 * b + 3, q1);
+        }
+        rs = re;
+    }
+}
+
 }  // namespace p3d

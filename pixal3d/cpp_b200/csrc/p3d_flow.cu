@@ -226,38 +226,8 @@ __global__ void euler_sched_stats_kernel(const float *__restrict__ x, const floa
                                          const float *__restrict__ vn, int64_t n, int C,
                                          const int32_t *__restrict__ offsets, int nbatch, const float *sched,
                                          const int *counter, float sigma_min, double *__restrict__ stats) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= n) return;
-    const int lane = threadIdx.x & 31;
     const float *s = sched + 4 * (*counter);
-    const float t = s[0], g = s[2];
-    const float a = 1.0f - sigma_min, bb = sigma_min + a * t;
-    double s0 = 0, q0 = 0, s1 = 0, q1 = 0;
-    for (int c = lane; c < C; c += 32) {
-        const int64_t i = row * C + c;
-        const float p = vp[i];
-        const float pred = g * p + (1.0f - g) * vn[i];
-        const float xp = a * x[i] - bb * p;
-        const float xc = a * x[i] - bb * pred;
-        s0 += xp;
-        q0 += static_cast<double>(xp) * xp;
-        s1 += xc;
-        q1 += static_cast<double>(xc) * xc;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-        q0 += __shfl_xor_sync(0xffffffffu, q0, o);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        q1 += __shfl_xor_sync(0xffffffffu, q1, o);
-    }
-    if (lane == 0) {
-        const int b = batch_of_row(offsets, nbatch, row);
-        atomicAdd(stats + 4 * b + 0, s0);
-        atomicAdd(stats + 4 * b + 1, q0);
-        atomicAdd(stats + 4 * b + 2, s1);
-        atomicAdd(stats + 4 * b + 3, q1);
-    }
+    cfg_stats_rows(x, vp, vn, n, C, offsets, nbatch, s[0], s[2], sigma_min, stats);
 }
 
 __global__ void euler_sched_kernel(float *__restrict__ x, const float *__restrict__ vp, const float *__restrict__ vn,
@@ -1036,7 +1006,7 @@ extern "C" int p3d_flow_sample_concat(p3d_flow *f, float *x, const void *ctx_fea
             const float *vp = f->vel, *vn = f->vel + half * ch;
             if (rescale) {
                 P3D_CUDA(ctx, cudaMemsetAsync(f->stats, 0, sizeof(double) * 4 * I, f->stream));
-                euler_sched_stats_kernel<<<blocks_for(half, 8), 256, 0, f->stream>>>(
+                euler_sched_stats_kernel<<<blocks_for(ceil_div(half, kStatsRowsPerWarp), 8), 256, 0, f->stream>>>(
                     f->x_state, vp, vn, half, ch, f->fine_off, I, f->sched, f->counter, sigma, f->stats);
                 P3D_TRY(check_launch(ctx, "euler_stats"));
             }

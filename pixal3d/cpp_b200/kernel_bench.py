@@ -17,6 +17,13 @@ Kernels (config-2 shapes unless noted):
   ln         trunk LayerNorm + AdaLN modulation, 8,184 x 1024 f32 -> f16
   attn       trunk self-attention, 2 sequences x 4,092, 16 heads x 64
   cross      trunk cross-attention, 2 x 4,092 queries x 1,029 keys
+  nbr        coordinate hash build + 27-neighbour map, batch-2 shell (43,532)
+  rowsort    conv row order (device radix sort by batch and neighbour pattern)
+  down       2x downsample topology + mean of 1024 f32 channels (43,532 -> 8,184)
+  c2s        channel-to-spatial topology + gather, 21,766 -> ~87k rows x 768
+  window     8^3 window partition + windowed attention, 21,766 x 12 heads (config 3)
+  dconv      config-3 stage-2 conv, ~347k rows, 64 (32 padded) -> 32 channels
+  euler      Euler/CFG update with guidance rescale, 21,766 x 8
 Each run is small enough for an ncu capture (a few hundred MB on the
 device) while its inputs exceed the 126 MB L2.  Prints one JSON line.
 """
@@ -184,6 +191,82 @@ def run(kernel: str, reps: int) -> dict:
         corner = 4 * n * C * 4 * nv
         return {"kernel": kernel, "ms": ms, "points": n, "views": nv, "write_bytes": write, "corner_bytes": corner,
                 "write_gbs": write / ms / 1e6, "corner_gbs": corner / ms / 1e6}
+    if kernel in ("nbr", "rowsort", "down"):
+        coords = torch.from_numpy(batched(shell_coords(), 2)).to(dev)
+        n = coords.shape[0]
+        if kernel == "nbr":
+            ms = _time(lambda: ops.neighbor_map27(coords), reps)
+            bytes_ = n * 16 + 27 * n * 4
+            return {"kernel": kernel, "ms": ms, "gbs": bytes_ / ms / 1e6, "bytes": bytes_, "rows": n}
+        if kernel == "rowsort":
+            nbr = ops.neighbor_map27(coords)
+            ms = _time(lambda: ops.conv_row_order(coords, nbr, 2), reps)
+            bytes_ = 27 * n * 4 + n * 16 + n * 4
+            return {"kernel": kernel, "ms": ms, "gbs": bytes_ / ms / 1e6, "bytes": bytes_, "rows": n}
+        x = torch.randn((n, C), device=dev, generator=g)
+        _, _, child, m = ops.downsample_topology(coords, 2, (64, 64, 64), 2)
+        t_topo = _time(lambda: ops.downsample_topology(coords, 2, (64, 64, 64), 2), reps)
+        ms = _time(lambda: ops.downsample_mean(x, child, 2), reps)
+        bytes_ = n * C * 4 + m * C * 4 + m * 8 * 4
+        return {"kernel": kernel, "ms_mean": ms, "ms_topology": t_topo, "gbs_mean": bytes_ / ms / 1e6,
+                "rows_in": n, "rows_out": m}
+    if kernel == "c2s":
+        cc = torch.from_numpy(shell_coords()).to(dev)
+        n = cc.shape[0]
+        mask = (torch.rand((n, 8), device=dev, generator=g) < 0.5).float()
+        x = torch.randn((n, 8 * 96), device=dev, generator=g)
+        oc, sr, sc, m = ops.c2s_topology(cc, 2, mask)
+        t_topo = _time(lambda: ops.c2s_topology(cc, 2, mask), reps)
+        zero = torch.zeros(m, dtype=torch.int8, device=dev)
+        xs = torch.randn((n, 768), device=dev, generator=g)
+        ms = _time(lambda: ops.c2s_gather(xs, sr, zero, 768), reps)
+        bytes_ = 2 * m * 768 * 4
+        return {"kernel": kernel, "ms_gather": ms, "ms_topology": t_topo, "gbs_gather": bytes_ / ms / 1e6,
+                "rows_in": n, "rows_out": m}
+    if kernel == "window":
+        cc = torch.from_numpy(shell_coords()).to(dev)
+        n, Cw, H = cc.shape[0], 768, 12
+        qkv = torch.randn((n, 3 * Cw), device=dev, generator=g).to(h)
+        perm, cu = ops.window_partition(cc, 1, 8, 4, (64, 64, 64))
+        t_part = _time(lambda: ops.window_partition(cc, 1, 8, 4, (64, 64, 64)), reps)
+        ms = _time(lambda: ops.window_attention(qkv[:, :Cw], qkv[:, Cw:2 * Cw], qkv[:, 2 * Cw:], perm, cu, 8, H, 0.125),
+                   reps)
+        key = (((cc[:, 1] + 4) // 8) * 64 + (cc[:, 2] + 4) // 8) * 64 + (cc[:, 3] + 4) // 8
+        cnt = torch.bincount(key.long()).double()
+        flops = 4.0 * float((cnt * cnt).sum()) * Cw
+        return {"kernel": kernel, "ms_attention": ms, "ms_partition": t_part, "tflops": flops / ms / 1e9,
+                "flops": flops, "rows": n}
+    if kernel == "dconv":
+        cc = shell_coords()
+        # two masked subdivisions (keep 0.5) of the config-0 shell: ~347k rows at 256^3
+        import numpy as np
+        rng = np.random.default_rng(0)
+        c = torch.from_numpy(cc).to(dev)
+        for _ in range(2):
+            m = torch.from_numpy((rng.random((c.shape[0], 8)) < 0.5).astype(np.float32)).to(dev)
+            c, _, _, _ = ops.c2s_topology(c, 2, m)
+            c = c.contiguous()
+        n = c.shape[0]
+        nbr = ops.neighbor_map27(c)
+        pairs = int((nbr < n).sum().item())
+        x = torch.randn((n, 64), device=dev, generator=g).to(h)
+        w = (torch.randn((27, 32, 64), device=dev, generator=g) / math.sqrt(27 * 32)).to(h)
+        b = torch.zeros(32, device=dev)
+        out = torch.empty((n, 32), device=dev)
+        ms = _time(lambda: ops.subm_conv3d(x, nbr, w, b, out=out), reps)
+        flops = 2.0 * pairs * 64 * 32
+        bytes_ = n * 64 * 2 + 27 * n * 4 + n * 32 * 4
+        return {"kernel": kernel, "ms": ms, "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6, "rows": n,
+                "pairs": pairs}
+    if kernel == "euler":
+        n = 21766
+        x = torch.randn((n, 8), device=dev, generator=g)
+        vp = torch.randn((n, 8), device=dev, generator=g)
+        vn = torch.randn((n, 8), device=dev, generator=g)
+        offs = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        ms = _time(lambda: ops.euler_cfg_step(x, vp, vn, offs, 0.5, 0.46, 3.0, 0.7, 1e-5), reps)
+        bytes_ = 4 * n * 8 * 4
+        return {"kernel": kernel, "ms": ms, "gbs": bytes_ / ms / 1e6, "bytes": bytes_}
     raise SystemExit(f"unknown kernel {kernel}")
 
 
