@@ -75,6 +75,13 @@ struct GemmParams {
     // 1: the epilogue stages 32 x 32 boxes in shared memory and writes them
     // with TMA through tmap_o (store, or reduce-add for the residual).
     int tma_out;
+    // 1-CTA gather only: CTA c takes global steps [c T / G, (c+1) T / G) of
+    // the T = tiles * 27 * kblocks (tile, tap, K block) steps instead of whole
+    // tiles, so a ragged last wave is spread over every CTA.  A tile cut
+    // between two CTAs is added into the f32 output by both (atomics; the
+    // host zeroes the output first unless it accumulates a residual), the
+    // bias by the part that holds its first step.
+    int split;
     // Gather (pair kernel): per 256-row tile, bit t set when some row of the
     // tile has a neighbour at tap t; other taps are skipped (their A rows
     // are all zero).  Null: every tap.
@@ -193,6 +200,44 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int64_t row, in
             for (int i = 0; i < 32; ++i)
                 if (i < ncols) o[i] = v[i];
         }
+    }
+}
+
+// Epilogue of a partial tile (split schedule): lane l owns output row `row`;
+// the f32 partial sums (+ bias when add_bias, times the row's gate for a
+// residual epilogue) are added into the f32 output with vector atomics.
+template <int COLS>
+__device__ __forceinline__ void epilogue_rows_atomic(const GemmParams &p, uint32_t tacc, int64_t row, int64_t n0,
+                                                     bool add_bias) {
+#pragma unroll 1
+    for (int cs = 0; cs < COLS; cs += 32) {
+        float v[32];
+        tmem_ld32(tacc + cs, v);
+        tmem_ld_wait();
+        const int64_t col0 = n0 + cs;
+        if (col0 < p.N && row < p.M) {
+            const int ncols = static_cast<int>(p.N - col0 < 32 ? p.N - col0 : 32);
+            if (add_bias && p.bias) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += (i < ncols) ? __ldg(p.bias + col0 + i) : 0.0f;
+            }
+            if ((p.epi & P3D_EPI_RESIDUAL) && p.gate) {
+                const float *g = p.gate + static_cast<int64_t>(batch_of_row(p.batch_offsets, p.nbatch, row)) * p.gate_ld + col0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] *= (i < ncols) ? __ldg(g + i) : 0.0f;
+            }
+            float *o = reinterpret_cast<float *>(p.out) + row * p.ldo + col0;
+            if (ncols == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    atomicAdd(reinterpret_cast<float4 *>(o + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (i < ncols) atomicAdd(o + i, v[i]);
+            }
+        }
+        __syncwarp();  // reconverge before the next tcgen05.ld (.sync.aligned)
     }
 }
 
@@ -548,6 +593,42 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
     const int64_t num_tiles = m_tiles * n_tiles;
     const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
     const int num_kb = GATHER ? 27 * kblocks_per_tap : kblocks_per_tap;
+    // This CTA's work as units (tile, K steps [kb0, kb1)) in order: whole
+    // tiles blockIdx.x + i * gridDim.x, or (split) the tiles of its contiguous
+    // step range [s_lo, s_hi), cut at the range ends.
+    const bool split = GATHER && p.split;
+    const int64_t total_steps = num_tiles * num_kb;
+    const int64_t s_lo = split ? total_steps * blockIdx.x / gridDim.x : 0;
+    const int64_t s_hi = split ? total_steps * (blockIdx.x + 1) / gridDim.x : 0;
+    struct Unit {
+        int64_t tile;
+        int kb0, kb1;
+    };
+    auto first_unit = [&](Unit &u) -> bool {
+        if (split) {
+            if (s_lo >= s_hi) return false;
+            u.tile = s_lo / num_kb;
+            u.kb0 = static_cast<int>(s_lo - u.tile * num_kb);
+            u.kb1 = static_cast<int>(std::min<int64_t>(num_kb, u.kb0 + (s_hi - s_lo)));
+            return true;
+        }
+        u.tile = blockIdx.x;
+        u.kb0 = 0;
+        u.kb1 = num_kb;
+        return u.tile < num_tiles;
+    };
+    auto next_unit = [&](Unit &u) -> bool {
+        if (split) {
+            const int64_t g = (u.tile + 1) * num_kb;  // the next unit starts a tile
+            if (u.kb1 < num_kb || g >= s_hi) return false;
+            u.tile += 1;
+            u.kb0 = 0;
+            u.kb1 = static_cast<int>(std::min<int64_t>(num_kb, s_hi - g));
+            return true;
+        }
+        u.tile += gridDim.x;
+        return u.tile < num_tiles;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -583,63 +664,69 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         bool ok = true;
         bool return_early = false;  // gather: a producer warp without a stage slot
         if constexpr (GATHER) {
-            // One producer warp per stage slot: step s = (local tile, tap, K
-            // block) goes to producer warp s % STAGES (warps past STAGES stay
-            // idle), so the fixed cost of a step (the empty wait, the barrier
-            // arrive, the index bookkeeping) of STAGES steps overlaps; with
-            // cin = 64 a step is one 128 x 64 x 64 MMA, far shorter than that
-            // cost.  Each warp owns one slot and walks its rounds in order,
-            // so its parity waits never alias an older phase.  Lane l gathers tile rows
+            // One producer warp per stage slot: this CTA's step s (a tap and
+            // K block of one of its units, in unit order) goes to producer
+            // warp s % STAGES (warps past STAGES stay idle), so the fixed cost
+            // of a step (the empty wait, the barrier arrive, the index
+            // bookkeeping) of STAGES steps overlaps; with cin = 64 a step is
+            // one 128 x 64 x 64 MMA, far shorter than that cost.  Each warp
+            // owns one slot and walks its rounds in order, so its parity
+            // waits never alias an older phase.  Lane l gathers tile rows
             // [4 l, 4 l + 4) with one TMA tile::gather4 from x; a source
             // index outside [0, M) (the sentinel M, or -1 past the last row)
             // reads TMA's zero fill.  Row indices are loaded two of this
             // warp's steps (2 * STAGES steps) ahead into two fixed registers.
-            const int64_t local_tiles =
-                blockIdx.x < num_tiles ? (num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-            const int64_t total = local_tiles * num_kb;
             static_assert(STAGES <= 8, "one producer warp per stage slot");
             if (pw >= STAGES) return_early = true;
             struct Pos {
-                int64_t lt;  // local tile
-                int w;       // step within the tile: tap * kblocks_per_tap + K block
+                Unit u;
+                int w;  // step within the tile: tap * kblocks_per_tap + K block
                 int64_t m0, n0;
+                bool valid;
             };
             auto place = [&](Pos &ps) {
-                const int64_t tile = blockIdx.x + ps.lt * gridDim.x;
-                ps.m0 = (tile / n_tiles) * BM;
-                ps.n0 = (tile % n_tiles) * BN;
+                ps.m0 = (ps.u.tile / n_tiles) * BM;
+                ps.n0 = (ps.u.tile % n_tiles) * BN;
             };
-            auto advance = [&](Pos &ps) {  // by STAGES steps (num_kb >= 27 > STAGES: at most one wrap)
-                ps.w += STAGES;
-                if (ps.w >= num_kb) {
-                    ps.w -= num_kb;
-                    ++ps.lt;
-                    place(ps);
+            auto advance = [&](Pos &ps, int by) {  // by < 27 <= the steps of a whole tile
+                ps.w += by;
+                while (ps.valid && ps.w >= ps.u.kb1) {
+                    const int over = ps.w - ps.u.kb1;
+                    ps.valid = next_unit(ps.u);
+                    if (ps.valid) {
+                        ps.w = ps.u.kb0 + over;
+                        place(ps);
+                    }
                 }
             };
             auto load4 = [&](const Pos &ps) -> int4 {
-                int r[4];
-                const int64_t tap = ps.w / kblocks_per_tap;
+                int r[4] = {-1, -1, -1, -1};
+                if (ps.valid) {
+                    const int64_t tap = ps.w / kblocks_per_tap;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int64_t row = ps.m0 + 4 * lane + j;
-                    r[j] = (ps.lt < local_tiles && row < p.M) ? __ldg(p.nbr + tap * p.M + row) : -1;
+                    for (int j = 0; j < 4; ++j) {
+                        const int64_t row = ps.m0 + 4 * lane + j;
+                        if (row < p.M) r[j] = __ldg(p.nbr + tap * p.M + row);
+                    }
                 }
                 return make_int4(r[0], r[1], r[2], r[3]);
             };
-            Pos pc{0, pw, 0, 0};
+            Pos pc;
+            pc.valid = first_unit(pc.u);
+            pc.w = pc.u.kb0;
             place(pc);
+            advance(pc, pw);
             Pos pa = pc;
             const int4 first0 = load4(pa);
-            advance(pa);
+            advance(pa, STAGES);
             const int4 first1 = load4(pa);
-            advance(pa);
+            advance(pa, STAGES);
             int4 ring0 = first0, ring1 = first1;
-            for (int64_t s0 = pw; s0 < total && ok && !return_early; s0 += 2 * STAGES) {
+            int64_t st = pw;  // this CTA's step index: stage st % STAGES, round st / STAGES
+            while (pc.valid && ok && !return_early) {
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
-                    const int64_t st = s0 + STAGES * u;
-                    if (st >= total || !ok) break;
+                    if (!pc.valid || !ok) break;
                     int4 src;
                     if (u == 0) {
                         src = ring0;
@@ -648,7 +735,7 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
                         src = ring1;
                         ring1 = load4(pa);
                     }
-                    advance(pa);
+                    advance(pa, STAGES);
                     const int stg = static_cast<int>(st % STAGES);
                     const uint32_t ph = static_cast<uint32_t>((st / STAGES) & 1);
                     if (!warp_wait<false>(&empty_bar[stg], ph ^ 1, p.fault)) {
@@ -665,7 +752,8 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
                     // Tap t's weights are rows [t*N, (t+1)*N) of the stacked [27*N, K] map.
                     if (lane == 0)
                         tma_load_2d(sb, &tmap_b, &full_bar[stg], kc, static_cast<int>(tap * p.N + pc.n0));
-                    advance(pc);
+                    advance(pc, STAGES);
+                    st += STAGES;
                 }
             }
         } else {
@@ -701,14 +789,15 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
             bool ok = true;
             bool issued = false;
             const uint32_t idesc = p.idesc;
-            for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            Unit un;
+            for (bool more = first_unit(un); more && ok; more = next_unit(un)) {
                 if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.fault)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&full_bar[stage], phase, p.fault)) {
                         ok = false;
                         break;
@@ -719,7 +808,7 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
                         umma_f16(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                                 (kb > 0 || kk > 0) ? 1u : 0u);
+                                 (kb > un.kb0 || kk > 0) ? 1u : 0u);
                     issued = true;
                     umma_commit(&empty_bar[stage]);
                     if (++stage == STAGES) {
@@ -747,14 +836,19 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int slot = 0;
-        for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        Unit un;
+        for (bool more = first_unit(un); more; more = next_unit(un)) {
+            const int64_t tile = un.tile;
             const int64_t m0 = (tile / n_tiles) * BM;
             const int64_t n0 = (tile % n_tiles) * BN;
-            if (!p.tma_out) prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
+            const bool whole = un.kb0 == 0 && un.kb1 == num_kb;
+            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
             if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
-            if (p.tma_out)
+            if (!whole)
+                epilogue_rows_atomic<BN>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
+            else if (p.tma_out)
                 epilogue_rows_tma<BN, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
                                                slot);
             else
@@ -1118,7 +1212,18 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     }
     const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, ctx->num_sms));
-    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, p);
+    GemmParams q = p;
+    q.split = 0;
+    // Split schedule for a gather with a ragged last wave of 1-3 waves (e.g.
+    // 171 tiles on 148 SMs): only for an f32 output without an activation,
+    // since cut tiles are summed by atomics.
+    if (GATHER && tiles > grid && tiles < 4 * static_cast<int64_t>(grid) && tiles % grid != 0 &&
+        p.out_dtype == P3D_F32 && !(p.epi & (P3D_EPI_GELU_TANH | P3D_EPI_SILU))) {
+        q.split = 1;
+        if (!(p.epi & P3D_EPI_RESIDUAL))
+            P3D_CUDA(ctx, cudaMemset2DAsync(p.out, sizeof(float) * p.ldo, 0, sizeof(float) * p.N, p.M, ctx->stream));
+    }
+    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, q);
     return check_launch(ctx, "gemm_tc_kernel");
 }
 

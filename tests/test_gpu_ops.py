@@ -690,3 +690,22 @@ def test_flow_prepare_rejects_unordered_batches():
     # the same flow prepares a valid set afterwards
     model.prepare(dev(c), 2, (16, 16, 16), [0, 10, 20])
     model.close()
+
+
+def test_subm_conv3d_split_schedule_residual():
+    """171 tiles of 128 rows on 148 SMs take the split schedule (tiles cut
+    between two CTAs are summed by atomics); with a residual epilogue the
+    output accumulates onto the caller's values, without one it starts from
+    zero.  Both against the oracle on the same f16-rounded operands."""
+    c = shell_coords()
+    x, w, b = _conv_case(c, 64, 64, 21)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    ref = O.subm_conv3d(c, rounded16(x), rounded16(w), b, O.neighbor_map27(c))
+    res = np.random.default_rng(2).standard_normal(ref.shape).astype(np.float32)
+    out = dev(res.copy())
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out, epilogue=L().EPI_RESIDUAL)
+    check(out.cpu().numpy(), res + ref, max_abs=1e-3, rel_l2=1e-5, what="split conv residual")
+    out2 = dev(np.full(ref.shape, 7.0, np.float32))
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out2)
+    check(out2.cpu().numpy(), ref, max_abs=1e-3, rel_l2=1e-5, what="split conv")
