@@ -75,9 +75,9 @@ struct GemmParams {
     // 1: the epilogue stages 32 x 32 boxes in shared memory and writes them
     // with TMA through tmap_o (store, or reduce-add for the residual).
     int tma_out;
-    // 1-CTA gather only: CTA c takes global steps [c T / G, (c+1) T / G) of
-    // the T = tiles * 27 * kblocks (tile, tap, K block) steps instead of whole
-    // tiles, so a ragged last wave is spread over every CTA.  A tile cut
+    // Gather kernels: CTA (pair) c takes global steps [c T / G, (c+1) T / G)
+    // of all tiles' T (tile, tap, K block) steps instead of whole tiles, so a
+    // ragged last wave is spread over every CTA (pair).  A tile cut
     // between two CTAs is added into the f32 output by both (atomics; the
     // host zeroes the output first unless it accumulates a residual), the
     // bias by the part that holds its first step.
@@ -922,6 +922,87 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         return (__ldg(p.tile_taps + tile / n_tiles) | (1u << 13)) & 0x7FFFFFFu;
     };
     auto tile_kb = [&](int64_t tile) -> int { return GATHER ? __popc(tile_taps(tile)) * kblocks_per_tap : num_kb; };
+    // This pair's work as units (tile, steps [kb0, kb1) of the tile's used
+    // taps x K blocks), in order: whole tiles pair + i * npairs.  Split: the
+    // full waves (tiles below r0 = floor(tiles / pairs) * pairs) stay whole
+    // tiles in that order, so all pairs stream the same taps' weights and
+    // nearby rows at a time, and the last, ragged wave's tiles are cut into
+    // equal contiguous step ranges, one per pair (split_info, found by warp 0
+    // below).
+    const bool split = GATHER && p.split;
+    const int64_t r0 = split ? (num_tiles / npairs) * npairs : num_tiles;
+    int64_t *split_info = reinterpret_cast<int64_t *>(done_bar + 2);  // {tile, kb, first step, end step}
+    struct Unit {
+        int64_t tile;
+        int kb0, kb1;
+        int64_t g0;  // last wave: index of step kb0 among the last wave's steps
+    };
+    auto tail_unit = [&](Unit &u) -> bool {
+        u.tile = split_info[0];
+        if (u.tile >= num_tiles) return false;
+        u.kb0 = static_cast<int>(split_info[1]);
+        u.g0 = split_info[2];
+        u.kb1 = static_cast<int>(std::min<int64_t>(tile_kb(u.tile), u.kb0 + (split_info[3] - u.g0)));
+        return true;
+    };
+    auto first_unit = [&](Unit &u) -> bool {
+        u.tile = pair;
+        u.kb0 = 0;
+        u.g0 = 0;
+        if (u.tile >= r0) return split ? tail_unit(u) : false;
+        u.kb1 = tile_kb(u.tile);
+        return true;
+    };
+    auto next_unit = [&](Unit &u) -> bool {
+        if (u.tile >= r0) {  // last wave (split only)
+            const int64_t g = u.g0 + (u.kb1 - u.kb0);
+            if (u.kb1 < tile_kb(u.tile) || g >= split_info[3] || u.tile + 1 >= num_tiles) return false;
+            u.tile += 1;
+            u.kb0 = 0;
+            u.g0 = g;
+            u.kb1 = static_cast<int>(std::min<int64_t>(tile_kb(u.tile), split_info[3] - g));
+            return true;
+        }
+        u.tile += npairs;
+        if (u.tile >= r0) return split ? tail_unit(u) : false;
+        u.kb1 = tile_kb(u.tile);
+        return true;
+    };
+    if (split && warp == 0) {
+        // the last wave's steps T, then this pair's range [T p / P, T (p+1) / P)
+        // and the tile and step where it starts (warp-wide scan over the masks)
+        int64_t total = 0;
+#pragma unroll 4
+        for (int64_t t = r0 + lane; t < num_tiles; t += 32) total += tile_kb(t);  // independent loads
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+        const int64_t s_lo = total * pair / npairs, s_hi = total * (pair + 1) / npairs;
+        int64_t base = 0, t_lo = num_tiles, k_lo = 0;
+        for (int64_t c = r0; c < num_tiles && t_lo == num_tiles; c += 32) {
+            const int64_t t = c + lane;
+            const int v = t < num_tiles ? tile_kb(t) : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, t < num_tiles && base + incl > s_lo);
+            if (hit) {
+                const int l = __ffs(hit) - 1;
+                const int incl_l = __shfl_sync(0xffffffffu, incl, l), v_l = __shfl_sync(0xffffffffu, v, l);
+                t_lo = c + l;
+                k_lo = s_lo - (base + incl_l - v_l);
+            }
+            base += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) {
+            split_info[0] = s_lo < s_hi ? t_lo : num_tiles;
+            split_info[1] = k_lo;
+            split_info[2] = s_lo;
+            split_info[3] = s_hi;
+        }
+    }
 
     if (threadIdx.x == 0) {
         // full: the even CTA's expect_tx arrival; both CTAs' TMA bytes complete on it
@@ -963,32 +1044,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
             // the tile's mask).
             static_assert(STAGES <= 8, "one producer warp per stage slot");
             struct Pos {
-                int64_t tile, m0, n0;
+                Unit u;
+                int w;  // step within the tile's used taps x K blocks
+                int64_t m0, n0;
                 uint32_t mask;
-                int w, nsteps;
+                bool valid;
             };
             auto place = [&](Pos &ps) {
-                if (ps.tile >= num_tiles) {
-                    ps.nsteps = 1 << 30;
-                    return;
-                }
-                ps.m0 = (ps.tile / n_tiles) * (2 * BM) + rank * BM;
-                ps.n0 = (ps.tile % n_tiles) * PAIR_N;
-                ps.mask = tile_taps(ps.tile);
-                ps.nsteps = __popc(ps.mask) * kblocks_per_tap;
+                ps.m0 = (ps.u.tile / n_tiles) * (2 * BM) + rank * BM;
+                ps.n0 = (ps.u.tile % n_tiles) * PAIR_N;
+                ps.mask = tile_taps(ps.u.tile);
             };
-            auto advance = [&](Pos &ps) {
-                ps.w += STAGES;
-                while (ps.w >= ps.nsteps && ps.tile < num_tiles) {
-                    ps.w -= ps.nsteps;
-                    ps.tile += npairs;
-                    place(ps);
+            auto advance = [&](Pos &ps, int by) {
+                ps.w += by;
+                while (ps.valid && ps.w >= ps.u.kb1) {
+                    const int over = ps.w - ps.u.kb1;
+                    ps.valid = next_unit(ps.u);
+                    if (ps.valid) {
+                        ps.w = ps.u.kb0 + over;
+                        place(ps);
+                    }
                 }
             };
             auto tap_of = [&](const Pos &ps) -> int { return static_cast<int>(__fns(ps.mask, 0, ps.w / kblocks_per_tap + 1)); };
             auto load4 = [&](const Pos &ps) -> int4 {
                 int r[4] = {-1, -1, -1, -1};
-                if (ps.tile < num_tiles) {
+                if (ps.valid) {
                     const int64_t tap = tap_of(ps);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
@@ -999,26 +1080,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
                 return make_int4(r[0], r[1], r[2], r[3]);
             };
             if (pw < STAGES) {
-                Pos pc{pair, 0, 0, 0u, 0, 0};
-                place(pc);
-                // step pw of this CTA's sequence
-                pc.w = pw;
-                while (pc.w >= pc.nsteps && pc.tile < num_tiles) {
-                    pc.w -= pc.nsteps;
-                    pc.tile += npairs;
-                    place(pc);
-                }
+                Pos pc;
+                pc.valid = first_unit(pc.u);
+                pc.w = pc.u.kb0;
+                if (pc.valid) place(pc);
+                advance(pc, pw);  // this warp's first step: the pair's step pw
                 Pos pa = pc;
                 const int4 first0 = load4(pa);
-                advance(pa);
+                advance(pa, STAGES);
                 const int4 first1 = load4(pa);
-                advance(pa);
+                advance(pa, STAGES);
                 int4 ring0 = first0, ring1 = first1;
-                int64_t st = pw;  // global step index: stage st % STAGES, round st / STAGES
-                while (pc.tile < num_tiles && ok) {
+                int64_t st = pw;  // the pair's step index: stage st % STAGES, round st / STAGES
+                while (pc.valid && ok) {
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        if (pc.tile >= num_tiles || !ok) break;
+                        if (!pc.valid || !ok) break;
                         int4 src;
                         if (u == 0) {
                             src = ring0;
@@ -1027,7 +1104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
                             src = ring1;
                             ring1 = load4(pa);
                         }
-                        advance(pa);
+                        advance(pa, STAGES);
                         const int stg = static_cast<int>(st % STAGES);
                         const uint32_t ph = static_cast<uint32_t>((st / STAGES) & 1);
                         if (!warp_wait<true>(&empty_bar[stg], ph ^ 1, p.fault)) {
@@ -1048,7 +1125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
                                 tma_load_2d_pair(sb + j * C::B_SUB, &tmap_b, fb, kc,
                                                  static_cast<int>(tap * p.N + pc.n0 + j * 256 + rank * 128));
                         }
-                        advance(pc);
+                        advance(pc, STAGES);
                         st += STAGES;
                     }
                 }
@@ -1093,15 +1170,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
             bool ok = true;
             bool issued = false;
             const uint32_t idesc = p.idesc;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+            Unit un;
+            for (bool more = first_unit(un); more && ok; more = next_unit(un)) {
                 if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1, p.fault)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-                const int nkb = tile_kb(tile);
-                for (int kb = 0; kb < nkb; ++kb) {
+                for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait_cluster(&full_bar[stage], phase, p.fault)) {
                         ok = false;
                         break;
@@ -1115,7 +1192,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
                         for (int j = 0; j < NSUB; ++j)
                             umma2_f16(d_tmem + j * 256, sw128_desc(a_addr + kk * 32),
                                       sw128_desc(b_addr + j * C::B_SUB + kk * 32), idesc,
-                                      (kb > 0 || kk > 0) ? 1u : 0u);
+                                      (kb > un.kb0 || kk > 0) ? 1u : 0u);
                     issued = true;
                     const uint32_t e = smem_u32(&empty_bar[stage]);
                     umma_commit2(e);
@@ -1146,14 +1223,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         int acc = 0;
         uint32_t acc_phase = 0;
         int slot = 0;
-        for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
+        Unit un;
+        for (bool more = first_unit(un); more; more = next_unit(un)) {
+            const int64_t tile = un.tile;
             const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
             const int64_t n0 = (tile % n_tiles) * PAIR_N;
-            if (!p.tma_out) prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
+            const bool whole = un.kb0 == 0 && un.kb1 == tile_kb(tile);
+            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
             if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
-            if (p.tma_out)
+            if (!whole)
+                epilogue_rows_atomic<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
+            else if (p.tma_out)
                 epilogue_rows_tma<C::ACC_COLS, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0,
                                                         smem_o + q * EPI_WARP_BYTES, slot);
             else
@@ -1252,8 +1334,26 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
     }
     const int64_t tiles = ceil_div(p.M, 2 * BM) * ceil_div(p.N, NSUB * 256);
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
+    GemmParams q = p;
+    q.split = 0;
+    // Split schedule for a ragged last wave (e.g. 342 pair tiles of the
+    // config-2 fine level on 74 pairs: 46 pairs would run a fifth tile): each
+    // pair runs 4 whole tiles, then an equal share of the last 46 tiles'
+    // steps.  f32 output without an activation only, since cut tiles are
+    // summed by atomics.
+    if (GATHER && tiles > pairs && tiles % pairs != 0 && tiles < 16 * static_cast<int64_t>(pairs) &&
+        p.out_dtype == P3D_F32 && !(p.epi & (P3D_EPI_GELU_TANH | P3D_EPI_SILU))) {
+        q.split = 1;
+        if (!(p.epi & P3D_EPI_RESIDUAL)) {
+            // zero the rows of the last wave's tiles (the only ones cut)
+            const int64_t n_tiles = ceil_div(p.N, NSUB * 256);
+            const int64_t row0 = ((tiles / pairs) * pairs / n_tiles) * (2 * BM);
+            P3D_CUDA(ctx, cudaMemset2DAsync(static_cast<float *>(p.out) + row0 * p.ldo, sizeof(float) * p.ldo, 0,
+                                            sizeof(float) * p.N, p.M - row0, ctx->stream));
+        }
+    }
     gemm2_tc_kernel<NSUB, GATHER><<<2 * pairs, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(
-        ta, tb, to, p);
+        ta, tb, to, q);
     return check_launch(ctx, "gemm2_tc_kernel");
 }
 

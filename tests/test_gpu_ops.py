@@ -709,3 +709,31 @@ def test_subm_conv3d_split_schedule_residual():
     out2 = dev(np.full(ref.shape, 7.0, np.float32))
     o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out2)
     check(out2.cpu().numpy(), ref, max_abs=1e-3, rel_l2=1e-5, what="split conv")
+
+
+@pytest.mark.gpu
+def test_subm_conv3d_pair_split_schedule():
+    """The CTA-pair conv (C_out a multiple of 256) on 86 pair tiles of 256 rows
+    takes the split schedule on the 74 SM pairs: each pair an equal share of
+    all tiles' (used tap, K block) steps, cut tiles summed by atomics, bias
+    once.  Rows in neighbour-pattern order with tap skipping, plain output
+    (starts from zero whatever the buffer held) and residual epilogue, against
+    the oracle on the same f16-rounded operands."""
+    c = shell_coords()
+    nb = O.neighbor_map27(c)
+    mask = np.zeros(c.shape[0], np.int64)
+    for t in range(27):
+        mask |= (nb[t] < c.shape[0]).astype(np.int64) << t
+    c = np.ascontiguousarray(c[np.argsort(mask, kind="stable")])
+    x, w, b = _conv_case(c, 128, 256, 23)
+    o = ops()
+    nbr = o.neighbor_map27(dev(c))
+    taps = o.conv_tile_taps(nbr)
+    ref = O.subm_conv3d(c, rounded16(x), rounded16(w), b, O.neighbor_map27(c))
+    out = dev(np.full(ref.shape, -3.0, np.float32))
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out, tile_taps=taps)
+    check(out.cpu().numpy(), ref, max_abs=1e-3, rel_l2=1e-5, what="pair split conv")
+    res = np.random.default_rng(3).standard_normal(ref.shape).astype(np.float32)
+    out2 = dev(res.copy())
+    o.subm_conv3d(hf(x), nbr, hf(w), dev(b), out=out2, epilogue=L().EPI_RESIDUAL, tile_taps=taps)
+    check(out2.cpu().numpy(), res + ref, max_abs=1e-3, rel_l2=1e-5, what="pair split conv residual")
