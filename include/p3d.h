@@ -268,16 +268,21 @@ int p3d_conv_tile_taps(p3d_ctx *ctx, const int32_t *nbr, int64_t n, uint32_t *ti
 
 /* Row order under which conv tiles share their missing taps (no reference
  * counterpart: a layout choice of this library's conv): perm[i] = the row
- * at position i when the rows are stably sorted by (batch index, neighbour
- * pattern), the pattern's bit t set when nbr[t][row] < n.  A stable device
- * radix sort, so equal keys keep their input order.  coords [n][4] (batch
- * in [0, batch)), nbr [27][n] of those coords; ws:
- * p3d_conv_row_order_workspace(n, batch) bytes, 256-byte aligned.  Run a
- * conv in this order by gathering the coordinates (and input rows) through
- * perm and building the neighbour map of the reordered coordinates. */
-size_t p3d_conv_row_order_workspace(int64_t n, int batch);
-int p3d_conv_row_order(p3d_ctx *ctx, const int32_t *coords, const int32_t *nbr, int64_t n, int batch, void *ws,
-                       size_t ws_bytes, int32_t *perm);
+ * at position i when the rows are stably sorted by (batch index, chunk,
+ * neighbour pattern).  chunk = row / chunk_rows in the input order (one
+ * chunk when chunk_rows <= 0), so a spatially ordered input (e.g. raster
+ * order) keeps its locality at chunk scale while rows of one chunk are
+ * grouped by pattern; the pattern's bit t is set when nbr[t][row] < n.  A
+ * stable device radix sort, so equal keys keep their input order.  coords
+ * [n][4] (batch in [0, batch)), nbr [27][n] of those coords; ws:
+ * p3d_conv_row_order_workspace(n, batch, chunk_rows) bytes (0 when the key
+ * would not fit 64 bits), 256-byte aligned.  Run a conv in this order by
+ * gathering the coordinates (and input rows) through perm and building the
+ * neighbour map of the reordered coordinates. */
+#define P3D_CONV_ORDER_CHUNK_ROWS 4096 /* chunk_rows of the flow's fine-level conv order */
+size_t p3d_conv_row_order_workspace(int64_t n, int batch, int64_t chunk_rows);
+int p3d_conv_row_order(p3d_ctx *ctx, const int32_t *coords, const int32_t *nbr, int64_t n, int batch,
+                       int64_t chunk_rows, void *ws, size_t ws_bytes, int32_t *perm);
 
 /* Varlen flash attention on tcgen05 tensor cores, head_dim 64, 16-bit in/out
  * (dtype), f32 softmax/accumulation.  rows_q / rows_k: total rows of the q and

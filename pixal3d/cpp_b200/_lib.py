@@ -30,6 +30,8 @@ EPI_GELU_TANH = 1
 EPI_SILU = 2
 EPI_RESIDUAL = 4
 
+CONV_ORDER_CHUNK_ROWS = 4096  # P3D_CONV_ORDER_CHUNK_ROWS
+
 
 class P3DError(RuntimeError):
     def __init__(self, status: int, message: str):
@@ -121,8 +123,8 @@ _sig("p3d_copy_to_device", i32, vp, vp, vp, sz)
 _sig("p3d_copy_to_host", i32, vp, vp, vp, sz)
 _sig("p3d_ctx_synchronize", i32, vp)
 _sig("p3d_wait_selftest", i32, vp, i32, i64, vp)
-_sig("p3d_conv_row_order_workspace", sz, i64, i32)
-_sig("p3d_conv_row_order", i32, vp, vp, vp, i64, i32, vp, sz, vp)
+_sig("p3d_conv_row_order_workspace", sz, i64, i32, i64)
+_sig("p3d_conv_row_order", i32, vp, vp, vp, i64, i32, i64, vp, sz, vp)
 _sig("p3d_downsample_grid_ints", i64, i32, i32, i32, i32, i32)
 _sig("p3d_downsample_topology", i32, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp)
 _sig("p3d_downsample_mean", i32, vp, vp, i64, i32, i32, vp, i32, vp)

@@ -431,7 +431,8 @@ __global__ void batch_offsets_kernel(const int4 *__restrict__ coords, int64_t n,
 // Sort key of a fine-level row: (batch, neighbour pattern), pattern bit t
 // set when nbr[t][row] is a point.
 __global__ void row_pattern_key_kernel(const int4 *__restrict__ coords, const int32_t *__restrict__ nbr, int64_t n,
-                                       uint64_t *__restrict__ keys, int32_t *__restrict__ idx) {
+                                       int64_t chunk_rows, int chunk_bits, uint64_t *__restrict__ keys,
+                                       int32_t *__restrict__ idx) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     uint32_t m = 0;
@@ -439,23 +440,33 @@ __global__ void row_pattern_key_kernel(const int4 *__restrict__ coords, const in
         const int32_t s = __ldg(nbr + static_cast<int64_t>(t) * n + i);
         if (s >= 0 && s < n) m |= 1u << t;
     }
-    keys[i] = (static_cast<uint64_t>(static_cast<uint32_t>(__ldg(&coords[i].x))) << 27) | m;
+    const uint64_t chunk = static_cast<uint64_t>(i / chunk_rows);
+    keys[i] = (static_cast<uint64_t>(static_cast<uint32_t>(__ldg(&coords[i].x))) << (27 + chunk_bits)) | (chunk << 27) | m;
     idx[i] = static_cast<int32_t>(i);
 }
 
-int row_order_end_bit(int batch) {
-    int bits = 1;
-    while ((int64_t(1) << bits) < batch) ++bits;
-    return 27 + bits;
+int bits_for(int64_t count) {
+    int bits = 0;
+    while ((int64_t(1) << bits) < count) ++bits;
+    return bits;
+}
+
+// chunk_rows normalised: <= 0 or >= n means one chunk
+int64_t row_order_chunk(int64_t n, int64_t chunk_rows) { return chunk_rows <= 0 || chunk_rows >= n ? std::max<int64_t>(n, 1) : chunk_rows; }
+
+int row_order_end_bit(int64_t n, int batch, int64_t chunk_rows) {
+    const int64_t chunk = row_order_chunk(n, chunk_rows);
+    return 27 + bits_for((n + chunk - 1) / chunk) + std::max(1, bits_for(batch));
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-size_t row_order_temp_bytes(int64_t n, int batch) {
+size_t row_order_temp_bytes(int64_t n, int batch, int64_t chunk_rows) {
     size_t temp = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, temp, static_cast<const uint64_t *>(nullptr),
                                     static_cast<uint64_t *>(nullptr), static_cast<const int32_t *>(nullptr),
-                                    static_cast<int32_t *>(nullptr), static_cast<int>(n), 0, row_order_end_bit(batch));
+                                    static_cast<int32_t *>(nullptr), static_cast<int>(n), 0,
+                                    row_order_end_bit(n, batch, chunk_rows));
     return temp;
 }
 
@@ -464,33 +475,38 @@ size_t row_order_temp_bytes(int64_t n, int batch) {
 
 using namespace p3d;
 
-extern "C" size_t p3d_conv_row_order_workspace(int64_t n, int batch) {
-    if (n < 0 || batch <= 0 || n >= (int64_t(1) << 31)) return 0;
-    return align256(sizeof(uint64_t) * n) * 2 + align256(sizeof(int32_t) * n) + align256(row_order_temp_bytes(n, batch)) +
-           256;
+extern "C" size_t p3d_conv_row_order_workspace(int64_t n, int batch, int64_t chunk_rows) {
+    if (n < 0 || batch <= 0 || n >= (int64_t(1) << 31) || row_order_end_bit(n, batch, chunk_rows) > 64) return 0;
+    return align256(sizeof(uint64_t) * n) * 2 + align256(sizeof(int32_t) * n) +
+           align256(row_order_temp_bytes(n, batch, chunk_rows)) + 256;
 }
 
 extern "C" int p3d_conv_row_order(p3d_ctx *ctx, const int32_t *coords, const int32_t *nbr, int64_t n, int batch,
-                                  void *ws, size_t ws_bytes, int32_t *perm) {
+                                  int64_t chunk_rows, void *ws, size_t ws_bytes, int32_t *perm) {
     if (!ctx) return P3D_ERR_INVALID;
     P3D_REQUIRE(ctx, coords && nbr && perm && ws && batch > 0 && n >= 0 && n < (int64_t(1) << 31),
                 "p3d_conv_row_order: bad argument");
+    P3D_REQUIRE(ctx, row_order_end_bit(n, batch, chunk_rows) <= 64,
+                "p3d_conv_row_order: chunk_rows too small for a 64-bit (batch, chunk, pattern) key");
     P3D_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(coords) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
                 "p3d_conv_row_order: coords must be 16-byte and ws 256-byte aligned");
-    P3D_REQUIRE(ctx, ws_bytes >= p3d_conv_row_order_workspace(n, batch), "p3d_conv_row_order: workspace too small");
+    P3D_REQUIRE(ctx, ws_bytes >= p3d_conv_row_order_workspace(n, batch, chunk_rows),
+                "p3d_conv_row_order: workspace too small");
     if (n == 0) return P3D_OK;
     uint8_t *w = static_cast<uint8_t *>(ws);
     uint64_t *keys_in = reinterpret_cast<uint64_t *>(w);
     uint64_t *keys_out = reinterpret_cast<uint64_t *>(w + align256(sizeof(uint64_t) * n));
     int32_t *idx = reinterpret_cast<int32_t *>(w + 2 * align256(sizeof(uint64_t) * n));
     void *temp = w + 2 * align256(sizeof(uint64_t) * n) + align256(sizeof(int32_t) * n);
-    size_t temp_bytes = row_order_temp_bytes(n, batch);
-    row_pattern_key_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(reinterpret_cast<const int4 *>(coords), nbr, n,
-                                                                        keys_in, idx);
+    size_t temp_bytes = row_order_temp_bytes(n, batch, chunk_rows);
+    const int64_t chunk = row_order_chunk(n, chunk_rows);
+    row_pattern_key_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const int4 *>(coords), nbr, n, chunk, bits_for((n + chunk - 1) / chunk), keys_in, idx);
     int rc = check_launch(ctx, "row_pattern_key");
     if (rc) return rc;
     const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx, perm,
-                                                          static_cast<int>(n), 0, row_order_end_bit(batch), ctx->stream);
+                                                          static_cast<int>(n), 0, row_order_end_bit(n, batch, chunk_rows),
+                                                          ctx->stream);
     if (e != cudaSuccess) return set_error(ctx, P3D_ERR_CUDA, std::string("p3d_conv_row_order: ") + cudaGetErrorString(e));
     return check_launch(ctx, "row_order_sort");
 }

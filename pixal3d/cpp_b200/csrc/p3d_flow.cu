@@ -765,17 +765,19 @@ extern "C" int p3d_flow_prepare(p3d_flow *f, const int32_t *coords, int64_t n, i
     const bool io = hp.io_resblocks > 0;
     if (io) {
         // Fine level: rows of each batch item stably sorted by neighbour
-        // pattern (device radix sort), so a 256-row conv tile shares its
-        // missing taps and the conv skips them; the input rows are gathered
-        // through perm and the output rows scattered back.
+        // pattern inside chunks of P3D_CONV_ORDER_CHUNK_ROWS caller rows
+        // (device radix sort), so a 256-row conv tile shares its missing taps
+        // and the conv skips them while the tiles in flight keep the caller
+        // order's locality; the input rows are gathered through perm and the
+        // output rows scattered back.
         P3D_TRY(f->alloc(&f->nbr, 27 * n));
         const size_t wsb = p3d_neighbor_map27_workspace(n);
         P3D_TRY(f->alloc(&f->hash_ws, static_cast<int64_t>((wsb + 3) / 4)));
         P3D_TRY(p3d_neighbor_map27_ws(ctx, coords, n, f->hash_ws, wsb, f->nbr));
-        const size_t owb = p3d_conv_row_order_workspace(n, batch);
+        const size_t owb = p3d_conv_row_order_workspace(n, batch, P3D_CONV_ORDER_CHUNK_ROWS);
         P3D_TRY(f->alloc(&f->order_ws, static_cast<int64_t>((owb + 3) / 4)));
         P3D_TRY(f->alloc(&f->perm, n));
-        P3D_TRY(p3d_conv_row_order(ctx, coords, f->nbr, n, batch, f->order_ws, owb, f->perm));
+        P3D_TRY(p3d_conv_row_order(ctx, coords, f->nbr, n, batch, P3D_CONV_ORDER_CHUNK_ROWS, f->order_ws, owb, f->perm));
         gather_coords_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(cin, f->perm, n,
                                                                           reinterpret_cast<int4 *>(f->coords));
         P3D_TRY(check_launch(ctx, "gather_coords"));

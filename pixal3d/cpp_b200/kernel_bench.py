@@ -72,7 +72,7 @@ def _time(fn, reps):
     return e0.elapsed_time(e1) / reps
 
 
-def run(kernel: str, reps: int) -> dict:
+def run(kernel: str, reps: int, chunk: int | None = None) -> dict:
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(0)
@@ -85,8 +85,9 @@ def run(kernel: str, reps: int) -> dict:
         nbr = ops.neighbor_map27(coords)
         taps = None
         if kernel == "conv1024t":
-            # as the flow's fine level runs: rows in neighbour-pattern order, tile taps
-            order = ops.conv_row_order(coords, nbr, 2).long()
+            # as the flow's fine level runs: rows in neighbour-pattern order
+            # inside chunks of caller rows, tile taps
+            order = ops.conv_row_order(coords, nbr, 2, *(() if chunk is None else (chunk,))).long()
             nbr = ops.neighbor_map27(coords[order].contiguous())
             taps = ops.conv_tile_taps(nbr)
         pairs = int((nbr < n).sum().item())
@@ -274,8 +275,13 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True)
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--chunk", type=int, default=None,
+                    help="conv1024t: chunk_rows of the row order (default: the flow's; 0: one chunk)")
     a = ap.parse_args()
-    print(json.dumps(run(a.kernel, a.reps)))
+    r = run(a.kernel, a.reps, a.chunk)
+    if a.chunk is not None:
+        r["chunk_rows"] = a.chunk
+    print(json.dumps(r))
 
 
 if __name__ == "__main__":

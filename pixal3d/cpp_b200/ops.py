@@ -244,16 +244,21 @@ def subm_conv3d(x: torch.Tensor, nbr: torch.Tensor, w: torch.Tensor, bias: torch
     return out
 
 
-def conv_row_order(coords: torch.Tensor, nbr: torch.Tensor, batch: int) -> torch.Tensor:
-    """perm [n] int32: rows stably sorted by (batch, neighbour pattern), the
-    order in which the flow runs its fine-level convs (p3d_conv_row_order)."""
+def conv_row_order(coords: torch.Tensor, nbr: torch.Tensor, batch: int,
+                   chunk_rows: int = L.CONV_ORDER_CHUNK_ROWS) -> torch.Tensor:
+    """perm [n] int32: rows stably sorted by (batch, row // chunk_rows,
+    neighbour pattern); the default chunk is the order in which the flow runs
+    its fine-level convs (p3d_conv_row_order; chunk_rows <= 0: one chunk)."""
     c = ctx(coords.device)
     n = coords.shape[0]
-    ws_bytes = int(L.lib.p3d_conv_row_order_workspace(n, batch))
+    ws_bytes = int(L.lib.p3d_conv_row_order_workspace(n, batch, chunk_rows))
+    if ws_bytes == 0:
+        raise ValueError("conv_row_order: chunk_rows too small for a 64-bit key")
     ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=coords.device)
     base = (ws.data_ptr() + 255) // 256 * 256
     perm = torch.empty(n, dtype=torch.int32, device=coords.device)
-    c.check(L.lib.p3d_conv_row_order(c.h, _p(coords), _p(nbr), n, batch, C.c_void_p(base), ws_bytes, _p(perm)))
+    c.check(L.lib.p3d_conv_row_order(c.h, _p(coords), _p(nbr), n, batch, chunk_rows, C.c_void_p(base), ws_bytes,
+                                     _p(perm)))
     return perm
 
 

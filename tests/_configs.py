@@ -90,12 +90,17 @@ def cfg2():
     return coords, x, ts, offs, ctx, hp, w
 
 
-def pattern_order(coords: np.ndarray, nbr: np.ndarray) -> np.ndarray:
-    """Row order of the flow's fine level: stable sort by (batch, neighbour
-    pattern), the pattern's bit t set when the row has a neighbour at tap t."""
+CONV_ORDER_CHUNK_ROWS = 4096  # P3D_CONV_ORDER_CHUNK_ROWS (include/p3d.h)
+
+
+def pattern_order(coords: np.ndarray, nbr: np.ndarray, chunk_rows: int = CONV_ORDER_CHUNK_ROWS) -> np.ndarray:
+    """Row order of the flow's fine level: stable sort by (batch, row //
+    chunk_rows, neighbour pattern), the pattern's bit t set when the row has a
+    neighbour at tap t (chunk_rows <= 0: one chunk)."""
     n = coords.shape[0]
     pattern = ((nbr < n).astype(np.int64) << np.arange(27, dtype=np.int64)[:, None]).sum(0)
-    key = (coords[:, 0].astype(np.int64) << 32) | pattern
+    chunk = np.arange(n, dtype=np.int64) // chunk_rows if chunk_rows > 0 else np.zeros(n, np.int64)
+    key = (coords[:, 0].astype(np.int64) << 50) | (chunk << 27) | pattern
     return np.argsort(key, kind="stable")
 
 

@@ -664,16 +664,26 @@ def test_linear_headnorm(dtype, norm, rope):
 
 def test_conv_row_order_matches_stable_sort():
     """p3d_conv_row_order (device radix sort) == numpy's stable argsort of
-    (batch, neighbour pattern), on the batch-2 config-0 shell and on a
-    five-item ragged batch."""
+    (batch, row chunk, neighbour pattern), on the batch-2 config-0 shell and
+    on a six-item ragged batch (chunks straddling items), for the flow's
+    chunk, one chunk, and a small chunk; a chunk too small for a 64-bit key
+    is refused."""
     from pixal3d.cpp_b200.workloads import image_shells, pack_cfg
-    from tests._configs import pattern_order
+    from tests._configs import pattern_order, CONV_ORDER_CHUNK_ROWS
+    assert CONV_ORDER_CHUNK_ROWS == L().CONV_ORDER_CHUNK_ROWS
     o = ops()
     packed, _ = pack_cfg(image_shells(3, seed=5))
     for cs, batch in ((batched(shell_coords(), 2), 2), (packed, 6)):
         d = dev(cs)
-        perm = o.conv_row_order(d, o.neighbor_map27(d), batch).cpu().numpy()
-        np.testing.assert_array_equal(perm, pattern_order(cs, O.neighbor_map27(cs)))
+        nb = O.neighbor_map27(cs)
+        nbr = o.neighbor_map27(d)
+        perm = o.conv_row_order(d, nbr, batch).cpu().numpy()
+        np.testing.assert_array_equal(perm, pattern_order(cs, nb))
+        for chunk in (0, 1000):
+            perm = o.conv_row_order(d, nbr, batch, chunk).cpu().numpy()
+            np.testing.assert_array_equal(perm, pattern_order(cs, nb, chunk))
+    with pytest.raises(ValueError, match="64-bit key"):
+        o.conv_row_order(d, nbr, 1 << 30, 1)
 
 
 def test_flow_prepare_rejects_unordered_batches():
