@@ -402,15 +402,16 @@ __device__ __forceinline__ void stage_row(int out_dtype, uint8_t *buf, int lane,
     }
 }
 
-// Lane 0 writes the staged 32-row box at (col0, row0): a TMA store, or for
-// the residual epilogue a TMA reduce-add into the f32 stream.  Rows >= M and
-// columns >= N of the box are clipped by the tensor map's bounds.
-__device__ __forceinline__ void issue_box(const GemmParams &p, const CUtensorMap *tmo, const uint8_t *buf, int lane,
-                                          int64_t col0, int64_t row0, int &slot) {
+// Lane 0 writes the staged 32-row box at (col0, row0): a TMA store, or (the
+// residual epilogue, or part of a tile cut by the split schedule) a TMA
+// reduce-add into the f32 output.  Rows >= M and columns >= N of the box are
+// clipped by the tensor map's bounds.
+__device__ __forceinline__ void issue_box(const CUtensorMap *tmo, const uint8_t *buf, int lane, int64_t col0,
+                                          int64_t row0, int &slot, bool reduce) {
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-        if (p.epi & P3D_EPI_RESIDUAL)
+        if (reduce)
             tma_reduce_add_2d(tmo, buf, static_cast<int>(col0), static_cast<int>(row0));
         else
             tma_store_2d(tmo, buf, static_cast<int>(col0), static_cast<int>(row0));
@@ -419,12 +420,14 @@ __device__ __forceinline__ void issue_box(const GemmParams &p, const CUtensorMap
     slot ^= 1;
 }
 
-// Bias, activation and residual gate of one 32-column chunk of row `row`;
-// false when the chunk lies entirely at or beyond column N (warp-uniform).
-__device__ __forceinline__ bool prep_chunk(const GemmParams &p, int64_t row, int64_t col0, float (&v)[32]) {
+// Bias (null: none), activation and residual gate of one 32-column chunk of
+// row `row`; false when the chunk lies entirely at or beyond column N
+// (warp-uniform).
+__device__ __forceinline__ bool prep_chunk(const GemmParams &p, const float *bias, int64_t row, int64_t col0,
+                                           float (&v)[32]) {
     if (col0 >= p.N) return false;
     const int ncols = static_cast<int>(p.N - col0 < 32 ? p.N - col0 : 32);
-    if (p.bias) add_vec32(v, p.bias + col0, ncols);
+    if (bias) add_vec32(v, bias + col0, ncols);
     if (p.epi & P3D_EPI_GELU_TANH) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
@@ -453,10 +456,12 @@ __device__ __forceinline__ void rope_rotate16(float (&v)[32], const float2 (&r)[
 // row0+31, accumulator columns [0, COLS) = output columns n0 + c).  Boxes
 // are 32 rows x 128 bytes: 32 f32 columns, or 64 16-bit columns staged from
 // two 32-column chunks.  The next chunk's tcgen05.ld is in flight while the
-// current one is finished.
+// current one is finished.  bias: p.bias, or null for a part of a cut tile
+// that does not hold its first step; reduce: TMA reduce-add instead of store.
 template <int COLS, bool HEADNORM>
 __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUtensorMap *tmo, uint32_t tacc,
-                                                  int64_t row0, int lane, int64_t n0, uint8_t *wbuf, int &slot) {
+                                                  int64_t row0, int lane, int64_t n0, uint8_t *wbuf, int &slot,
+                                                  const float *bias, bool reduce) {
     static_assert(COLS % 64 == 0, "epilogue column count");
     const int64_t row = row0 + lane;
     const bool f32 = p.out_dtype == P3D_F32;
@@ -510,9 +515,9 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
                     rope_rotate16(a, r2);
                 }
                 stage_row(p.out_dtype, buf, lane, a, f32 ? 0 : half);
-                if (f32) issue_box(p, tmo, buf, lane, col0 + 32 * half, row0, slot);
+                if (f32) issue_box(tmo, buf, lane, col0 + 32 * half, row0, slot, reduce);
             }
-            if (!f32) issue_box(p, tmo, buf, lane, col0, row0, slot);
+            if (!f32) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
         }
         return;
     }
@@ -526,10 +531,10 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
         __syncwarp();
         tmem_ld32(tacc + cs + 32, b);
         uint8_t *buf = acquire_slot(wbuf, slot, lane);
-        const bool any = prep_chunk(p, row, col0, a);
+        const bool any = prep_chunk(p, bias, row, col0, a);
         if (any) {
             stage_row(p.out_dtype, buf, lane, a, 0);
-            if (f32) issue_box(p, tmo, buf, lane, col0, row0, slot);
+            if (f32) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
         }
         tmem_ld_wait_regs(b);
         if (more) {
@@ -537,11 +542,11 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
             tmem_ld32(tacc + cs + 64, a);
         }
         if (f32) buf = acquire_slot(wbuf, slot, lane);
-        if (prep_chunk(p, row, col0 + 32, b)) {
+        if (prep_chunk(p, bias, row, col0 + 32, b)) {
             stage_row(p.out_dtype, buf, lane, b, f32 ? 0 : 1);
-            if (f32) issue_box(p, tmo, buf, lane, col0 + 32, row0, slot);
+            if (f32) issue_box(tmo, buf, lane, col0 + 32, row0, slot, reduce);
         }
-        if (!f32 && any) issue_box(p, tmo, buf, lane, col0, row0, slot);
+        if (!f32 && any) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
         if (more) tmem_ld_wait_regs(a);
     }
 }
@@ -594,32 +599,36 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
     const int kblocks_per_tap = static_cast<int>((p.K + BK - 1) / BK);
     const int num_kb = GATHER ? 27 * kblocks_per_tap : kblocks_per_tap;
     // This CTA's work as units (tile, K steps [kb0, kb1)) in order: whole
-    // tiles blockIdx.x + i * gridDim.x, or (split) the tiles of its contiguous
-    // step range [s_lo, s_hi), cut at the range ends.
+    // tiles blockIdx.x + i * gridDim.x.  Split: the full waves (tiles below
+    // r0 = floor(tiles / G) * G) stay whole tiles in that order, and the last,
+    // ragged wave's steps are cut into G equal contiguous ranges, range b for
+    // CTA b ([s_lo, s_hi), counted from tile r0's first step).
     const bool split = GATHER && p.split;
-    const int64_t total_steps = num_tiles * num_kb;
-    const int64_t s_lo = split ? total_steps * blockIdx.x / gridDim.x : 0;
-    const int64_t s_hi = split ? total_steps * (blockIdx.x + 1) / gridDim.x : 0;
+    const int64_t r0 = split ? (num_tiles / gridDim.x) * gridDim.x : num_tiles;
+    const int64_t tail_steps = (num_tiles - r0) * num_kb;
+    const int64_t s_lo = tail_steps * blockIdx.x / gridDim.x;
+    const int64_t s_hi = tail_steps * (blockIdx.x + 1) / gridDim.x;
     struct Unit {
         int64_t tile;
         int kb0, kb1;
     };
+    auto tail_unit = [&](Unit &u) -> bool {
+        if (s_lo >= s_hi) return false;
+        u.tile = r0 + s_lo / num_kb;
+        u.kb0 = static_cast<int>(s_lo % num_kb);
+        u.kb1 = static_cast<int>(std::min<int64_t>(num_kb, u.kb0 + (s_hi - s_lo)));
+        return true;
+    };
     auto first_unit = [&](Unit &u) -> bool {
-        if (split) {
-            if (s_lo >= s_hi) return false;
-            u.tile = s_lo / num_kb;
-            u.kb0 = static_cast<int>(s_lo - u.tile * num_kb);
-            u.kb1 = static_cast<int>(std::min<int64_t>(num_kb, u.kb0 + (s_hi - s_lo)));
-            return true;
-        }
         u.tile = blockIdx.x;
         u.kb0 = 0;
         u.kb1 = num_kb;
-        return u.tile < num_tiles;
+        if (u.tile < r0) return true;
+        return split ? tail_unit(u) : false;
     };
     auto next_unit = [&](Unit &u) -> bool {
-        if (split) {
-            const int64_t g = (u.tile + 1) * num_kb;  // the next unit starts a tile
+        if (u.tile >= r0) {  // last wave (split only)
+            const int64_t g = (u.tile - r0 + 1) * num_kb;  // the next unit starts a tile
             if (u.kb1 < num_kb || g >= s_hi) return false;
             u.tile += 1;
             u.kb0 = 0;
@@ -627,7 +636,8 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
             return true;
         }
         u.tile += gridDim.x;
-        return u.tile < num_tiles;
+        if (u.tile < r0) return true;
+        return split ? tail_unit(u) : false;
     };
 
     if (threadIdx.x == 0) {
@@ -757,10 +767,11 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
                 }
             }
         } else {
-            for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int64_t m0 = (tile / n_tiles) * BM;
-                const int64_t n0 = (tile % n_tiles) * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+            Unit un;
+            for (bool more = first_unit(un); more && ok; more = next_unit(un)) {
+                const int64_t m0 = (un.tile / n_tiles) * BM;
+                const int64_t n0 = (un.tile % n_tiles) * BN;
+                for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (t == 0) {
                         if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.fault)) {
                             ok = false;
@@ -846,11 +857,12 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
             if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
-            if (!whole)
-                epilogue_rows_atomic<BN>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
-            else if (p.tma_out)
+            if (p.tma_out)  // a cut tile's part is reduce-added, the bias by the part holding step 0
                 epilogue_rows_tma<BN, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
-                                               slot);
+                                               slot, (!GATHER || un.kb0 == 0) ? p.bias : nullptr,
+                                               (GATHER && !whole) || (p.epi & P3D_EPI_RESIDUAL));
+            else if (!whole)
+                epilogue_rows_atomic<BN>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
             else
                 epilogue_rows<BN, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
@@ -1233,11 +1245,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
             if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
-            if (!whole)
-                epilogue_rows_atomic<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
-            else if (p.tma_out)
+            if (p.tma_out)  // a cut tile's part is reduce-added, the bias by the part holding step 0
                 epilogue_rows_tma<C::ACC_COLS, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0,
-                                                        smem_o + q * EPI_WARP_BYTES, slot);
+                                                        smem_o + q * EPI_WARP_BYTES, slot,
+                                                        un.kb0 == 0 ? p.bias : nullptr,
+                                                        !whole || (p.epi & P3D_EPI_RESIDUAL));
+            else if (!whole)
+                epilogue_rows_atomic<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
             else
                 epilogue_rows<C::ACC_COLS, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
@@ -1297,13 +1311,20 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
     GemmParams q = p;
     q.split = 0;
     // Split schedule for a gather with a ragged last wave of 1-3 waves (e.g.
-    // 171 tiles on 148 SMs): only for an f32 output without an activation,
-    // since cut tiles are summed by atomics.
+    // 171 tiles on 148 SMs): the last wave's tiles are cut into equal step
+    // ranges, one per CTA, whose parts are summed into the f32 output (TMA
+    // reduce-add, else atomics; the last wave's rows zeroed first unless a
+    // residual is accumulated).  f32 outputs without an activation only.
+    // (For the dense trunk linears the cut parts' extra epilogues cost more
+    // than the ragged wave: out-projection 27 -> 36 us, MLP down 61 -> 66 us.)
     if (GATHER && tiles > grid && tiles < 4 * static_cast<int64_t>(grid) && tiles % grid != 0 &&
         p.out_dtype == P3D_F32 && !(p.epi & (P3D_EPI_GELU_TANH | P3D_EPI_SILU))) {
         q.split = 1;
-        if (!(p.epi & P3D_EPI_RESIDUAL))
-            P3D_CUDA(ctx, cudaMemset2DAsync(p.out, sizeof(float) * p.ldo, 0, sizeof(float) * p.N, p.M, ctx->stream));
+        if (!(p.epi & P3D_EPI_RESIDUAL)) {
+            const int64_t row0 = ((tiles / grid) * grid / ceil_div(p.N, BN)) * BM;
+            P3D_CUDA(ctx, cudaMemset2DAsync(static_cast<float *>(p.out) + row0 * p.ldo, sizeof(float) * p.ldo, 0,
+                                            sizeof(float) * p.N, p.M - row0, ctx->stream));
+        }
     }
     gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, q);
     return check_launch(ctx, "gemm_tc_kernel");

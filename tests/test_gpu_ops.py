@@ -283,6 +283,15 @@ gam = torch.from_numpy((1 + 0.1 * rng.standard_normal(2 * 128)).astype(np.float3
 outs = [ops.linear(x, w, b, out_dtype=torch.float32), ops.linear(x, w, b, out_dtype=torch.float16, epilogue=L.EPI_GELU_TANH)]
 r = res.clone(); ops.linear(x, w, b, out=r, epilogue=L.EPI_RESIDUAL, gate=gate, batch_offsets=offs); outs.append(r)
 outs.append(ops.linear_headnorm(x, w, b, 128, gam, 256, table, out=torch.empty((m, n), device="cuda", dtype=torch.float16)))
+# 65 x 4 row/column tiles on 148 SMs: the split schedule cuts the last wave's tiles
+m2, n2 = 8190, 1024
+x2 = torch.from_numpy(rng.standard_normal((m2, 1024)).astype(np.float32)).cuda().half()
+w2 = torch.from_numpy((rng.standard_normal((n2, 1024)) / 32).astype(np.float32)).cuda().half()
+b2 = torch.from_numpy((rng.standard_normal(n2) * 0.1).astype(np.float32)).cuda()
+g2 = torch.from_numpy(rng.standard_normal((2, n2)).astype(np.float32)).cuda()
+o2 = torch.tensor([0, 5000, m2], dtype=torch.int32, device="cuda")
+r2 = torch.from_numpy(rng.standard_normal((m2, n2)).astype(np.float32)).cuda()
+ops.linear(x2, w2, b2, out=r2, epilogue=L.EPI_RESIDUAL, gate=g2, batch_offsets=o2); outs.append(r2)
 torch.save([t.cpu() for t in outs], "OUT")
 print("ok")
 """
@@ -299,6 +308,36 @@ print("ok")
     assert torch.equal(tma[0], direct[0]) and torch.equal(tma[1], direct[1])
     torch.testing.assert_close(tma[2], direct[2], rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(tma[3].float(), direct[3].float(), rtol=1e-3, atol=1e-3)
+    # split schedule: TMA reduce-adds of the cut tiles' parts vs f32 atomics
+    torch.testing.assert_close(tma[4], direct[4], rtol=1e-5, atol=1e-4)
+
+
+def test_linear_residual_split_schedule():
+    """Gated-residual linears with a ragged last wave (64 or 65 row tiles x 4
+    column tiles of 128 x 256 on 148 SMs) take the split schedule: the full
+    wave runs whole tiles, the last wave's tiles are cut into equal K-step
+    ranges whose parts are reduce-added onto the residual stream, the bias by
+    the part holding the first K step.  Against torch fp32 (no TF32) on the
+    same f16 operands; K = 4096 is the MLP-down shape."""
+    rng = np.random.default_rng(46)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for m, k in ((8184, 1024), (8190, 4096)):
+            n = 1024
+            x = hf(rng.standard_normal((m, k)))
+            w = hf(rng.standard_normal((n, k)) / math.sqrt(k))
+            b = dev((rng.standard_normal(n) * 0.1).astype(np.float32))
+            res = dev(rng.standard_normal((m, n)).astype(np.float32))
+            gate = dev(rng.standard_normal((2, n)).astype(np.float32))
+            offs = torch.tensor([0, m // 3, m], dtype=torch.int32, device="cuda")
+            out = res.clone()
+            ops().linear(x, w, b, out=out, epilogue=L().EPI_RESIDUAL, gate=gate, batch_offsets=offs)
+            g = torch.where(torch.arange(m, device="cuda")[:, None] < m // 3, gate[0], gate[1])
+            exp = res + g * (x.float() @ w.float().T + b)
+            check(out.cpu().numpy(), exp.cpu().numpy(), max_abs=1e-3, rel_l2=1e-5, what=f"split residual k={k}")
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 def test_linear_strided_input():
