@@ -283,7 +283,7 @@ gam = torch.from_numpy((1 + 0.1 * rng.standard_normal(2 * 128)).astype(np.float3
 outs = [ops.linear(x, w, b, out_dtype=torch.float32), ops.linear(x, w, b, out_dtype=torch.float16, epilogue=L.EPI_GELU_TANH)]
 r = res.clone(); ops.linear(x, w, b, out=r, epilogue=L.EPI_RESIDUAL, gate=gate, batch_offsets=offs); outs.append(r)
 outs.append(ops.linear_headnorm(x, w, b, 128, gam, 256, table, out=torch.empty((m, n), device="cuda", dtype=torch.float16)))
-# 65 x 4 row/column tiles on 148 SMs: the split schedule cuts the last wave's tiles
+# the trunk's residual shape with a partial last row tile (65 x 4 tiles)
 m2, n2 = 8190, 1024
 x2 = torch.from_numpy(rng.standard_normal((m2, 1024)).astype(np.float32)).cuda().half()
 w2 = torch.from_numpy((rng.standard_normal((n2, 1024)) / 32).astype(np.float32)).cuda().half()
@@ -308,17 +308,15 @@ print("ok")
     assert torch.equal(tma[0], direct[0]) and torch.equal(tma[1], direct[1])
     torch.testing.assert_close(tma[2], direct[2], rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(tma[3].float(), direct[3].float(), rtol=1e-3, atol=1e-3)
-    # split schedule: TMA reduce-adds of the cut tiles' parts vs f32 atomics
+    # trunk shape: TMA reduce-add vs read-modify-write of the residual
     torch.testing.assert_close(tma[4], direct[4], rtol=1e-5, atol=1e-4)
 
 
-def test_linear_residual_split_schedule():
-    """Gated-residual linears with a ragged last wave (64 or 65 row tiles x 4
-    column tiles of 128 x 256 on 148 SMs) take the split schedule: the full
-    wave runs whole tiles, the last wave's tiles are cut into equal K-step
-    ranges whose parts are reduce-added onto the residual stream, the bias by
-    the part holding the first K step.  Against torch fp32 (no TF32) on the
-    same f16 operands; K = 4096 is the MLP-down shape."""
+def test_linear_residual_trunk_shapes():
+    """Gated-residual linears at the trunk's shapes (8,184 rows, or 8,190 with
+    a partial last row tile; 1,024 output columns; K = 1,024 for the attention
+    output projections, 4,096 for MLP down), residual batch segments split
+    unevenly.  Against torch fp32 (no TF32) on the same f16 operands."""
     rng = np.random.default_rng(46)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -335,7 +333,7 @@ def test_linear_residual_split_schedule():
             ops().linear(x, w, b, out=out, epilogue=L().EPI_RESIDUAL, gate=gate, batch_offsets=offs)
             g = torch.where(torch.arange(m, device="cuda")[:, None] < m // 3, gate[0], gate[1])
             exp = res + g * (x.float() @ w.float().T + b)
-            check(out.cpu().numpy(), exp.cpu().numpy(), max_abs=1e-3, rel_l2=1e-5, what=f"split residual k={k}")
+            check(out.cpu().numpy(), exp.cpu().numpy(), max_abs=1e-3, rel_l2=1e-5, what=f"trunk residual k={k}")
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
