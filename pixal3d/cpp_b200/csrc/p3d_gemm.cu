@@ -44,6 +44,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 9 * 32;
+// The dense 1-CTA kernel: 8 epilogue warps (0-7, two per TMEM lane quarter,
+// each taking half of the tile's columns), the MMA warp 8, the producer warp 9.
+constexpr int kThreadsD = 10 * 32;
 // The gather variants add 4 producer warps (9-12): one producer warp per stage
 // slot, up to 8 stages.
 constexpr int kThreadsG = 13 * 32;
@@ -88,9 +91,9 @@ struct GemmParams {
     const uint32_t *tile_taps;
 };
 
-// TMA-store epilogue staging: each of the 4 epilogue warps owns two 4 KB
-// slots, each one 32-row x 128-byte box (32 f32 or 64 16-bit columns) in the
-// 128-byte swizzle.
+// TMA-store epilogue staging: each epilogue warp owns one or two 4 KB slots,
+// each one 32-row x 128-byte box (32 f32 or 64 16-bit columns) in the
+// 128-byte swizzle.  EPI_BYTES: the 4 warps x 2 slots of the pair kernel.
 constexpr int EPI_SLOT_BYTES = 4096;
 constexpr int EPI_WARP_BYTES = 2 * EPI_SLOT_BYTES;
 constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
@@ -103,16 +106,28 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 constexpr int kStageBudget = P3D_GEMM_STAGE_BUDGET;
 
 // 1-CTA tile: 128 x BN, BK = 64; accumulators double-buffered in TMEM.
-template <int BN>
+// Dense tiles of 128 or 256 columns drain each accumulator with 8 epilogue
+// warps of one staging slot each, keeping the operand stages of the 4-warp
+// layout (measured on the trunk linears against two slots and one stage
+// fewer: qkv + head norm + RoPE 50.7 vs 51.2 us, MLP down 58.6 vs 65.0 us);
+// the gather and 64-column tiles with 4 warps of two slots.
+template <int BN, bool GATHER>
 struct Cfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (kStageBudget / STAGE_BYTES) > 8 ? 8 : (kStageBudget / STAGE_BYTES);
+    static constexpr int EPI_WARPS = (!GATHER && BN >= 128) ? 8 : 4;
+    static constexpr int EPI_SLOTS = EPI_WARPS == 8 ? 1 : 2;
+    static constexpr int EPI_WARP_BYTES = EPI_SLOTS * EPI_SLOT_BYTES;
+    static constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
+    static constexpr int EPI_COLS = BN * 4 / EPI_WARPS;  // accumulator columns per epilogue warp
+    static constexpr int BUDGET = EPI_WARPS == 8 ? 232448 - EPI_BYTES - 1024 - 256 : kStageBudget;
+    static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
     static constexpr int ACC_COLS = BN;
     static constexpr int ACC_BUFS = 2;
     static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(SMEM <= 232448, "1-CTA GEMM shared memory");
 };
 
 // CTA-pair tile: 256 x (NSUB * 256).  Each CTA of the pair stages its own 128
@@ -372,8 +387,9 @@ __device__ __forceinline__ void mul_vec32(float (&v)[32], const float *g, int nc
 
 // Staging slot for the next box: wait until the box last issued from this
 // slot (two boxes ago) has been read by the TMA unit.
+template <int SLOTS>
 __device__ __forceinline__ uint8_t *acquire_slot(uint8_t *wbuf, int slot, int lane) {
-    if (lane == 0) bulk_wait_read<1>();
+    if (lane == 0) bulk_wait_read<SLOTS - 1>();
     __syncwarp();
     return wbuf + slot * EPI_SLOT_BYTES;
 }
@@ -406,6 +422,7 @@ __device__ __forceinline__ void stage_row(int out_dtype, uint8_t *buf, int lane,
 // residual epilogue, or part of a tile cut by the split schedule) a TMA
 // reduce-add into the f32 output.  Rows >= M and columns >= N of the box are
 // clipped by the tensor map's bounds.
+template <int SLOTS>
 __device__ __forceinline__ void issue_box(const CUtensorMap *tmo, const uint8_t *buf, int lane, int64_t col0,
                                           int64_t row0, int &slot, bool reduce) {
     fence_proxy_async_smem();
@@ -417,7 +434,7 @@ __device__ __forceinline__ void issue_box(const CUtensorMap *tmo, const uint8_t 
             tma_store_2d(tmo, buf, static_cast<int>(col0), static_cast<int>(row0));
         bulk_commit();
     }
-    slot ^= 1;
+    slot = SLOTS == 1 ? 0 : slot ^ 1;
 }
 
 // Bias (null: none), activation and residual gate of one 32-column chunk of
@@ -458,7 +475,7 @@ __device__ __forceinline__ void rope_rotate16(float (&v)[32], const float2 (&r)[
 // two 32-column chunks.  The next chunk's tcgen05.ld is in flight while the
 // current one is finished.  bias: p.bias, or null for a part of a cut tile
 // that does not hold its first step; reduce: TMA reduce-add instead of store.
-template <int COLS, bool HEADNORM>
+template <int COLS, bool HEADNORM, int SLOTS = 2>
 __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUtensorMap *tmo, uint32_t tacc,
                                                   int64_t row0, int lane, int64_t n0, uint8_t *wbuf, int &slot,
                                                   const float *bias, bool reduce) {
@@ -493,7 +510,7 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
                 for (int i = 0; i < 32; ++i) ss += a[i] * a[i] + b[i] * b[i];
                 inv = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) / max(||v||, eps)
             }
-            uint8_t *buf = acquire_slot(wbuf, slot, lane);
+            uint8_t *buf = acquire_slot<SLOTS>(wbuf, slot, lane);
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 if (half == 1) {
@@ -501,7 +518,7 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
                     tmem_ld32(tacc + cs + 32, a);
                     tmem_ld_wait_regs(a);
                     if (p.bias) add_vec32(a, p.bias + col0 + 32, 32);
-                    if (f32) buf = acquire_slot(wbuf, slot, lane);
+                    if (f32) buf = acquire_slot<SLOTS>(wbuf, slot, lane);
                 }
                 if (norm) {
 #pragma unroll
@@ -515,9 +532,9 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
                     rope_rotate16(a, r2);
                 }
                 stage_row(p.out_dtype, buf, lane, a, f32 ? 0 : half);
-                if (f32) issue_box(tmo, buf, lane, col0 + 32 * half, row0, slot, reduce);
+                if (f32) issue_box<SLOTS>(tmo, buf, lane, col0 + 32 * half, row0, slot, reduce);
             }
-            if (!f32) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
+            if (!f32) issue_box<SLOTS>(tmo, buf, lane, col0, row0, slot, reduce);
         }
         return;
     }
@@ -530,23 +547,23 @@ __device__ __forceinline__ void epilogue_rows_tma(const GemmParams &p, const CUt
         const bool more = cs + 64 < COLS;
         __syncwarp();
         tmem_ld32(tacc + cs + 32, b);
-        uint8_t *buf = acquire_slot(wbuf, slot, lane);
+        uint8_t *buf = acquire_slot<SLOTS>(wbuf, slot, lane);
         const bool any = prep_chunk(p, bias, row, col0, a);
         if (any) {
             stage_row(p.out_dtype, buf, lane, a, 0);
-            if (f32) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
+            if (f32) issue_box<SLOTS>(tmo, buf, lane, col0, row0, slot, reduce);
         }
         tmem_ld_wait_regs(b);
         if (more) {
             __syncwarp();
             tmem_ld32(tacc + cs + 64, a);
         }
-        if (f32) buf = acquire_slot(wbuf, slot, lane);
+        if (f32) buf = acquire_slot<SLOTS>(wbuf, slot, lane);
         if (prep_chunk(p, bias, row, col0 + 32, b)) {
             stage_row(p.out_dtype, buf, lane, b, f32 ? 0 : 1);
-            if (f32) issue_box(tmo, buf, lane, col0 + 32, row0, slot, reduce);
+            if (f32) issue_box<SLOTS>(tmo, buf, lane, col0 + 32, row0, slot, reduce);
         }
-        if (!f32 && any) issue_box(tmo, buf, lane, col0, row0, slot, reduce);
+        if (!f32 && any) issue_box<SLOTS>(tmo, buf, lane, col0, row0, slot, reduce);
         if (more) tmem_ld_wait_regs(a);
     }
 }
@@ -572,18 +589,18 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *f
 }
 
 template <int BN, bool GATHER>
-__global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
+__global__ void __launch_bounds__(GATHER ? kThreadsG : kThreadsD, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_o, const GemmParams p) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, GATHER>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t *smem_a = smem;
     uint8_t *smem_b = smem + STAGES * C::A_BYTES;
-    uint8_t *smem_o = smem_b + STAGES * C::B_BYTES;  // epilogue staging, EPI_BYTES
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_o + EPI_BYTES);
+    uint8_t *smem_o = smem_b + STAGES * C::B_BYTES;  // epilogue staging, C::EPI_BYTES
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem_o + C::EPI_BYTES);
     uint64_t *empty_bar = full_bar + STAGES;
     uint64_t *tfull_bar = empty_bar + STAGES;  // [2]
     uint64_t *tempty_bar = tfull_bar + 2;      // [2]
@@ -647,7 +664,7 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
-            mbar_init(&tempty_bar[a], 4);
+            mbar_init(&tempty_bar[a], C::EPI_WARPS);
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
@@ -663,11 +680,15 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp < 4 || (GATHER && warp > kMmaWarp)) {
+    // roles: gather: producers warps 0-3 and 9-12, epilogue 4-7; dense:
+    // producer warp 9, epilogue 0-7 (4-7 for 64-column tiles); MMA warp 8
+    const bool producer = GATHER ? (warp < 4 || warp > kMmaWarp) : warp == kMmaWarp + 1;
+    const bool epilogue = warp < 8 && (C::EPI_WARPS == 8 || warp >= 4);
+    if (producer) {
         // ------------------------------------------------------------ producer
         // gather: producer pw (warps 0-3 -> 0-3, 9-12 -> 4-7) issues the steps
-        // s with s % 8 == pw; dense: thread 0 issues every TMA load
-        const int t = warp < 4 ? threadIdx.x : 0;
+        // s with s % 8 == pw; dense: lane 0 of warp 9 issues every TMA load
+        const int t = GATHER ? (warp < 4 ? threadIdx.x : 0) : lane;
         const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
         int stage = 0;
         uint32_t phase = 0;
@@ -841,9 +862,14 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
             }
         }
         __syncwarp();
-    } else {
+    } else if (epilogue) {
         // ----------------------------------------------------------- epilogue
+        // warp w drains TMEM lane quarter w % 4, columns [h E, (h+1) E) of
+        // the accumulator (E = C::EPI_COLS; h = w / 4 - 1 with 4 warps, w / 4 with 8)
         const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+        const int h = C::EPI_WARPS == 8 ? (warp >> 2) : 0;
+        const int ew = C::EPI_WARPS == 8 ? warp : q;  // staging slot group
+        constexpr int EC = C::EPI_COLS;
         int acc = 0;
         uint32_t acc_phase = 0;
         int slot = 0;
@@ -851,20 +877,21 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreads, 1)
         for (bool more = first_unit(un); more; more = next_unit(un)) {
             const int64_t tile = un.tile;
             const int64_t m0 = (tile / n_tiles) * BM;
-            const int64_t n0 = (tile % n_tiles) * BN;
+            const int64_t n0 = (tile % n_tiles) * BN + h * EC;
             const bool whole = un.kb0 == 0 && un.kb1 == num_kb;
-            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, BN);
+            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, EC);
             if (!warp_wait<false>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+            const uint32_t tacc =
+                tmem_base + acc * C::ACC_COLS + h * EC + (static_cast<uint32_t>(q * 32) << 16);
             if (p.tma_out)  // a cut tile's part is reduce-added, the bias by the part holding step 0
-                epilogue_rows_tma<BN, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + q * EPI_WARP_BYTES,
-                                               slot, (!GATHER || un.kb0 == 0) ? p.bias : nullptr,
-                                               (GATHER && !whole) || (p.epi & P3D_EPI_RESIDUAL));
+                epilogue_rows_tma<EC, !GATHER, C::EPI_SLOTS>(
+                    p, &tmap_o, tacc, m0 + q * 32, lane, n0, smem_o + ew * C::EPI_WARP_BYTES, slot,
+                    (!GATHER || un.kb0 == 0) ? p.bias : nullptr, (GATHER && !whole) || (p.epi & P3D_EPI_RESIDUAL));
             else if (!whole)
-                epilogue_rows_atomic<BN>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
+                epilogue_rows_atomic<EC>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
             else
-                epilogue_rows<BN, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
+                epilogue_rows<EC, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -1299,7 +1326,7 @@ EncodeFn get_encode_fn() {
 template <int BN, bool GATHER>
 int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &to,
                 const GemmParams &p) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, GATHER>;
     static bool attr_set = false;
     if (!attr_set) {
         P3D_CUDA(ctx, cudaFuncSetAttribute(gemm_tc_kernel<BN, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1326,7 +1353,7 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
                                             sizeof(float) * p.N, p.M - row0, ctx->stream));
         }
     }
-    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(ta, tb, to, q);
+    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreadsD, C::SMEM, ctx->stream>>>(ta, tb, to, q);
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
