@@ -35,6 +35,32 @@ namespace p3d {
 int set_error(p3d_ctx *ctx, int status, const std::string &msg);
 int check_launch(p3d_ctx *ctx, const char *what);
 
+// ---- Programmatic dependent launch.  A kernel launched by launch_pdl may
+// start (its prologue: barrier init, TMEM allocation, tensor-map prefetch)
+// while the previous kernel in the stream is still running; it must call
+// pdl_wait() before its first access to global memory another kernel wrote or
+// reads (the wait returns once the previous grid has completed and its writes
+// are visible; without a programmatic dependency it returns at once).
+// pdl_trigger() lets the next such kernel be scheduled once every CTA of this
+// grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Makes `device` current for the guard's scope and restores the caller's.

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(256) layernorm_reg_kernel(const float *__restr
                                                             const int32_t *__restrict__ offsets, int nbatch,
                                                             TO *__restrict__ out) {
     constexpr int C = 128 * NV;
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= n) return;
     const int lane = threadIdx.x & 31;
@@ -594,8 +596,8 @@ extern "C" int p3d_layernorm_modulate(p3d_ctx *ctx, const float *x, int64_t n, i
     if (reg) {
 #define P3D_LN_REG(NVV)                                                                                         \
     case NVV:                                                                                                  \
-        layernorm_reg_kernel<TO, NVV><<<grid, 256, 0, ctx->stream>>>(x, n, eps, gamma, beta, mod, mod_ld,      \
-                                                                      batch_offsets, nbatch, static_cast<TO *>(out)); \
+        P3D_CUDA(ctx, launch_pdl(layernorm_reg_kernel<TO, NVV>, dim3(grid), dim3(256), 0, ctx->stream, x, n, eps,   \
+                                 gamma, beta, mod, mod_ld, batch_offsets, nbatch, static_cast<TO *>(out)));      \
         break;
         P3D_DISPATCH(out_dtype, TO, {
             switch (nv) {

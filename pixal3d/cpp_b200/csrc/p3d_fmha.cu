@@ -174,6 +174,8 @@ template <typename T>
 __global__ void __launch_bounds__(kThreadsF, 2)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
+    pdl_wait();  // q/k/v and the sequence offsets come from the previous kernels
+    pdl_trigger();
     const int seq = blockIdx.z, head = blockIdx.y;
     const int q0 = p.cu_q[seq], q1 = p.cu_q[seq + 1];
     const int k0 = p.cu_k[seq], k1 = p.cu_k[seq + 1];
@@ -429,14 +431,15 @@ int p3d_fmha_tc(p3d_ctx *ctx, const void *q, int64_t ldq, const void *k, int64_t
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
             attr_done[0] = true;
         }
-        fmha_tc_kernel<__nv_bfloat16><<<grid, kThreadsF, SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
+        P3D_CUDA(ctx, launch_pdl(fmha_tc_kernel<__nv_bfloat16>, grid, dim3(kThreadsF), SMEM_BYTES, ctx->stream, tq, tk,
+                                 tv, p));
     } else {
         if (!attr_done[1]) {
             P3D_CUDA(ctx, cudaFuncSetAttribute(fmha_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                SMEM_BYTES));
             attr_done[1] = true;
         }
-        fmha_tc_kernel<__half><<<grid, kThreadsF, SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
+        P3D_CUDA(ctx, launch_pdl(fmha_tc_kernel<__half>, grid, dim3(kThreadsF), SMEM_BYTES, ctx->stream, tq, tk, tv, p));
     }
     return check_launch(ctx, "fmha_tc");
 }

@@ -679,6 +679,8 @@ __global__ void __launch_bounds__(GATHER ? kThreadsG : kThreadsD, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();     // the previous kernel's outputs (our inputs) are complete from here
+    pdl_trigger();  // every CTA of this persistent grid is resident: the next kernel may queue
 
     // roles: gather: producers warps 0-3 and 9-12, epilogue 4-7; dense:
     // producer warp 9, epilogue 0-7 (4-7 for 64-column tiles); MMA warp 8
@@ -1008,6 +1010,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         return true;
     };
     if (split && warp == 0) {
+        pdl_wait();
         // the last wave's steps T, then this pair's range [T p / P, T (p+1) / P)
         // and the tile and step where it starts (warp-wide scan over the masks)
         int64_t total = 0;
@@ -1066,6 +1069,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
     cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     if (warp < 4 || (GATHER && warp > kMmaWarp)) {
         // ------------------------------------------------------------ producer
@@ -1353,7 +1358,8 @@ int launch_gemm(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, cons
                                             sizeof(float) * p.N, p.M - row0, ctx->stream));
         }
     }
-    gemm_tc_kernel<BN, GATHER><<<grid, GATHER ? kThreadsG : kThreadsD, C::SMEM, ctx->stream>>>(ta, tb, to, q);
+    P3D_CUDA(ctx, launch_pdl(gemm_tc_kernel<BN, GATHER>, dim3(grid), dim3(GATHER ? kThreadsG : kThreadsD), C::SMEM,
+                             ctx->stream, ta, tb, to, q));
     return check_launch(ctx, "gemm_tc_kernel");
 }
 
@@ -1400,8 +1406,8 @@ int launch_gemm2(p3d_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, con
                                             sizeof(float) * p.N, p.M - row0, ctx->stream));
         }
     }
-    gemm2_tc_kernel<NSUB, GATHER><<<2 * pairs, GATHER ? kThreadsG : kThreads, C::SMEM, ctx->stream>>>(
-        ta, tb, to, q);
+    P3D_CUDA(ctx, launch_pdl(gemm2_tc_kernel<NSUB, GATHER>, dim3(2 * pairs), dim3(GATHER ? kThreadsG : kThreads),
+                             C::SMEM, ctx->stream, ta, tb, to, q));
     return check_launch(ctx, "gemm2_tc_kernel");
 }
 
