@@ -932,6 +932,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
     using C = Cfg2<NSUB>;
     constexpr int STAGES = C::STAGES;
     constexpr int PAIR_N = NSUB * 256;
+    // Epilogue warps per CTA: with 4 stages (NSUB = 2) the 4 gather warps
+    // 9-12 have no stage slot and drain the accumulator's second half, so
+    // the MMA (one accumulator buffer) waits on half as long an epilogue;
+    // one 4 KB staging slot each.  Otherwise warps 4-7 with two slots.
+    constexpr int EPI_WARPS = (GATHER && STAGES + 4 <= 8 && NSUB == 2) ? 8 : 4;
+    constexpr int EPI_SLOTS = EPI_WARPS == 8 ? 1 : 2;
+    constexpr int EPI_COLS = C::ACC_COLS * 4 / EPI_WARPS;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -1054,7 +1061,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
-            mbar_init(&tempty_bar[a], 8);
+            mbar_init(&tempty_bar[a], 2 * EPI_WARPS);
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
@@ -1072,7 +1079,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
     pdl_wait();
     pdl_trigger();
 
-    if (warp < 4 || (GATHER && warp > kMmaWarp)) {
+    const bool epilogue2 = EPI_WARPS == 8 && warp > kMmaWarp;  // second epilogue group
+    if ((warp < 4 || (GATHER && warp > kMmaWarp)) && !epilogue2) {
         // ------------------------------------------------------------ producer
         const int pw = warp < 4 ? warp : warp - (kMmaWarp + 1) + 4;
         bool ok = true;
@@ -1263,7 +1271,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         __syncwarp();
     } else {
         // ----------------------------------------------------------- epilogue
+        // warp w drains TMEM lane quarter w % 4, accumulator columns
+        // [h E, (h+1) E) (E = EPI_COLS; h = 1 for the second group)
         const int q = warp & 3;
+        const int h = epilogue2 ? 1 : 0;
+        const int ew = h * 4 + q;  // staging slot group
         int acc = 0;
         uint32_t acc_phase = 0;
         int slot = 0;
@@ -1271,21 +1283,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         for (bool more = first_unit(un); more; more = next_unit(un)) {
             const int64_t tile = un.tile;
             const int64_t m0 = (tile / n_tiles) * (2 * BM) + rank * BM;
-            const int64_t n0 = (tile % n_tiles) * PAIR_N;
+            const int64_t n0 = (tile % n_tiles) * PAIR_N + h * EPI_COLS;
             const bool whole = un.kb0 == 0 && un.kb1 == tile_kb(tile);
-            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, PAIR_N);
+            if (!p.tma_out && whole) prefetch_residual(p, m0 + q * 32 + lane, n0, EPI_COLS);
             if (!warp_wait<true>(&tfull_bar[acc], acc_phase, p.fault)) break;
             tc_fence_after();
-            const uint32_t tacc = tmem_base + acc * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+            const uint32_t tacc =
+                tmem_base + acc * C::ACC_COLS + h * EPI_COLS + (static_cast<uint32_t>(q * 32) << 16);
             if (p.tma_out)  // a cut tile's part is reduce-added, the bias by the part holding step 0
-                epilogue_rows_tma<C::ACC_COLS, !GATHER>(p, &tmap_o, tacc, m0 + q * 32, lane, n0,
-                                                        smem_o + q * EPI_WARP_BYTES, slot,
-                                                        un.kb0 == 0 ? p.bias : nullptr,
-                                                        !whole || (p.epi & P3D_EPI_RESIDUAL));
+                epilogue_rows_tma<EPI_COLS, !GATHER, EPI_SLOTS>(p, &tmap_o, tacc, m0 + q * 32, lane, n0,
+                                                                smem_o + ew * EPI_SLOTS * EPI_SLOT_BYTES, slot,
+                                                                un.kb0 == 0 ? p.bias : nullptr,
+                                                                !whole || (p.epi & P3D_EPI_RESIDUAL));
             else if (!whole)
-                epilogue_rows_atomic<C::ACC_COLS>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
+                epilogue_rows_atomic<EPI_COLS>(p, tacc, m0 + q * 32 + lane, n0, un.kb0 == 0);
             else
-                epilogue_rows<C::ACC_COLS, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
+                epilogue_rows<EPI_COLS, !GATHER>(p, tacc, m0 + q * 32 + lane, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
