@@ -100,10 +100,7 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 // Shared memory for the operand stages of one CTA (the rest of the 227 KB
 // holds the epilogue staging and the barriers).
-#ifndef P3D_GEMM_STAGE_BUDGET
-#define P3D_GEMM_STAGE_BUDGET 196608
-#endif
-constexpr int kStageBudget = P3D_GEMM_STAGE_BUDGET;
+constexpr int kStageBudget = 196608;
 
 // 1-CTA tile: 128 x BN, BK = 64; accumulators double-buffered in TMEM.
 // Dense tiles of 128 or 256 columns drain each accumulator with 8 epilogue
