@@ -80,8 +80,11 @@ __device__ __forceinline__ void store4(TO *p, float a, float b, float c, float d
     }
 }
 
+// C = 1024 (NV = 8, the trunk): 4 blocks per SM (64 registers) keep 4,736
+// rows in flight instead of 3,552 at the unbounded 74 registers (8,184 x 1,024
+// f32 -> f16 with modulation: 9.84 -> 8.48 us).
 template <typename TO, int NV>
-__global__ void __launch_bounds__(256) layernorm_reg_kernel(const float *__restrict__ x, int64_t n, float eps,
+__global__ void __launch_bounds__(256, NV == 8 ? 4 : 1) layernorm_reg_kernel(const float *__restrict__ x, int64_t n, float eps,
                                                             const float *__restrict__ gamma,
                                                             const float *__restrict__ beta,
                                                             const float *__restrict__ mod, int64_t mod_ld,
